@@ -1,0 +1,354 @@
+"""Benchmark of the neural-texture hot path on B200 (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...   (one process per GPU)
+
+Headline (`value`): BASELINE config 1 training throughput, train samples/s for the whole
+job -- one step = fused training pass (sample, forward, loss, backward, gradient
+reduction, latent scatter) + fused Adam over the MLP and both latent grids, 262,144
+samples on a 1024^2 synthetic material with 512^2x8 + 256^2x8 fp16 latents.  The whole
+training state (~51 MB) fits in L2, so L2 is flushed (256 MB write) before every timed
+step and each step is timed alone with CUDA events on the launching stream.  At N > 1
+every rank trains its own material (weak scaling, no collective in the data path; BASELINE
+config 4a's partitioning).  Config 0 decode throughput (texels/s) is reported alongside.
+
+`--impl reference` times the reference algorithm on the host cores instead (the CPU port
+in oracle/, since the reference's own training path cannot be compiled: its
+tiny-cuda-nn submodule is empty).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG1 = dict(workload="config1_train_1024sq_8ch", image=(1024, 1024), grids=((512, 512), (256, 256)), C=8,
+            cout=8, lattice=(512, 512))
+CFG0 = dict(workload="config0_decode_1024sq_8ch", image=(1024, 1024), grids=((512, 512), (256, 256)), C=8,
+            cout=8)
+L2_FLUSH_BYTES = 256 << 20
+
+# algorithmic work per unit (basis of roofline.achieved)
+MLP_FLOP_FWD = 2 * (32 * 64 + 64 * 64 + 64 * 8)          # 13,312 per texel / sample
+MLP_FLOP_TRAIN = 3 * MLP_FLOP_FWD                         # fwd + dX + dW = 39,936 per sample
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return dict(hbm=d["hbm_gbs"], tensor=d["bf16_tflops"], tensor_sustained=d["bf16_tflops_sustained"],
+                    source="measured")
+    return dict(hbm=6650.0, tensor=1590.0, tensor_sustained=1400.0, source="fallback")
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        try:
+            return json.load(open(path))
+        except Exception:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_train_baseline(O, seconds=12.0):
+    """Oracle (CPU port of the reference algorithm) training throughput on a bounded sample
+    of config 1 on all host cores: train pass over a slice of the lattice + full Adam."""
+    import numpy as np
+    from neural_textures_b200.api import he_normal_weights, zero_padded_inputs
+    threads = os.cpu_count() or 1
+    C, cout = CFG1["C"], CFG1["cout"]
+    rng = np.random.default_rng(0)
+    grids = [O.f2h(rng.uniform(-1, 1, (h, w, C))) for (w, h) in CFG1["grids"]]
+    Ws = he_normal_weights(0, cout)
+    Ws[0] = zero_padded_inputs(Ws[0], 2 * C + 8)
+    W = [w.view(np.uint16).copy() for w in Ws]
+    b = [np.zeros(64, np.uint16), np.zeros(64, np.uint16), np.zeros(cout, np.uint16)]
+    model = O.OracleModel(C, cout, grids, W, b)
+    iw, ih = CFG1["image"]
+    tgt = O.generate_target(iw, ih, cout, 0, threads=threads)
+    lw, lh = CFG1["lattice"]
+    s = O.make_sampler(iw, ih, lw, lh, step=1)
+    n = 4096
+    t0 = time.perf_counter()
+    O.train_pass(model, tgt, s, threads=threads, first=0, count=n)
+    dt = time.perf_counter() - t0
+    n = int(min(lw * lh, max(4096, n * seconds / max(dt, 1e-6) * 0.8)))
+    t0 = time.perf_counter()
+    O.train_pass(model, tgt, s, threads=threads, first=0, count=n)
+    t_pass = time.perf_counter() - t0
+    per_sample = t_pass / n
+    # Adam over every parameter (single pass of the CPU Adam port)
+    P = sum(g.size for g in grids)
+    wv = np.zeros(P, np.uint16)
+    g = np.full(P, 1e-3, np.float32)
+    m = np.zeros(P, np.float32)
+    v = np.zeros(P, np.float32)
+    t0 = time.perf_counter()
+    O.adam_f16(wv, g, m, v, 1e-2, 0.9, 0.99, 1e-8, 1)
+    t_adam = time.perf_counter() - t0
+    step_time = per_sample * lw * lh + t_adam
+    return {"value": (lw * lh) / step_time, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{n} of {lw * lh} config-1 samples (train pass, oracle/nt_oracle.c, OpenMP) "
+                      f"+ one Adam pass over all {P} latent params; step time extrapolated to the full batch"}
+
+
+def run_reference(args):
+    """--impl reference: the CPU port of the reference algorithm on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    O.build()
+    vals = []
+    cpu_train_baseline(O, seconds=2.0)  # warm-up (page-in, thread start)
+    for _ in range(args.steps):
+        vals.append(cpu_train_baseline(O, seconds=max(1.0, 60.0 / max(args.steps, 1)))["value"])
+    last = cpu_train_baseline(O, seconds=1.0)
+    value = statistics.median(vals)
+    line = {"impl": "reference", "metric": "train samples/s (fwd+bwd+Adam), config 1", "value": value,
+            "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * CFG1["lattice"][0] * CFG1["lattice"][1] / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": CFG1["workload"], "global_batch": CFG1["lattice"][0] * CFG1["lattice"][1]},
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": last["cores"], "kind": "port",
+                             "sample": last["sample"]},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference CUDA/tiny-cuda-nn path cannot be built (empty submodule); CPU port of its "
+                    "algorithm timed instead"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-iters", type=int, default=50)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    import neural_textures_b200 as nt
+    from neural_textures_b200 import _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    L = _native.load()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    args.warmup = max(args.warmup, 3)
+
+    # ---- config 1 training ---------------------------------------------------------------
+    tex = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                           output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
+    tex.init(seed=rank)
+    scratch = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    B = CFG1["lattice"][0] * CFG1["lattice"][1]
+
+    def step_once(step, ev=None):
+        p = tex.params(step=step)
+        if ev:
+            ev[0].record(stream)
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 0, sptr))
+        if ev:
+            ev[1].record(stream)
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), sptr))
+        if ev:
+            ev[2].record(stream)
+
+    for w in range(args.warmup):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(w + 1)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    launches0 = nt.launch_count()
+    torch.cuda.synchronize(dev)
+    for k in range(args.steps):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(args.warmup + k + 1, events[k])
+    torch.cuda.synchronize(dev)
+    launches = nt.launch_count() - launches0 - args.steps  # exclude the L2 flushes
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t_train = sum(e[0].elapsed_time(e[1]) for e in events) / args.steps   # ms
+    t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / args.steps
+    t_step = t_train + t_adam
+    if world > 1:
+        t = torch.tensor([t_step], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_step_max = t.item()
+    else:
+        t_step_max = t_step
+    value = world * B / (t_step_max * 1e-3)
+
+    # ---- e2e through the C ABI: params from pinned host memory, loss read back per step ----
+    loss_host = torch.zeros(1, dtype=torch.float32, pin_memory=True)
+    pbytes = ctypes.sizeof(_native.NtKernelParams)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e2e_steps = args.steps
+    t0 = time.perf_counter()
+    for k in range(e2e_steps):
+        tex.loss_accum.zero_()
+        p = tex.params(step=10_000 + k)
+        _native.check(L.nt_train_step(ctypes.byref(p), sptr))
+        loss_host.copy_(tex.loss_accum, non_blocking=True)
+        stream.synchronize()
+    e2e_time = (time.perf_counter() - t0) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_time], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_time = t.item()
+    e2e_value = world * B / e2e_time
+
+    # ---- config 0 decode -----------------------------------------------------------------
+    dtex = nt.NeuralTexture(*CFG0["image"], grid_sizes=CFG0["grids"], latent_channels=CFG0["C"],
+                            output_channels=CFG0["cout"], device=dev)
+    dtex.init(seed=100 + rank)
+    out = torch.empty((CFG0["image"][0] * CFG0["image"][1], CFG0["cout"]), dtype=torch.float16, device=dev)
+    dp = dtex.params(inference_output=out)
+    for _ in range(5):
+        _native.check(L.nt_invoke_inference(ctypes.byref(dp), sptr))
+    dev_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.decode_iters)]
+    for k in range(args.decode_iters):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        dev_ev[k][0].record(stream)
+        _native.check(L.nt_invoke_inference(ctypes.byref(dp), sptr))
+        dev_ev[k][1].record(stream)
+    torch.cuda.synchronize(dev)
+    t_dec = sum(a.elapsed_time(b) for a, b in dev_ev) / args.decode_iters
+    texels = CFG0["image"][0] * CFG0["image"][1]
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    pk = peaks()
+    tr = ncu_traffic()
+    train_flop = MLP_FLOP_TRAIN * B
+    achieved_tf = train_flop / (t_train * 1e-3) / 1e12
+    P = sum(w * h for (w, h) in CFG1["grids"]) * CFG1["C"]
+    adam_bytes = 28 * P  # w 2 + g 4 + m 4 + v 4 read, w 2 + m 4 + v 4 + g 4 written
+    dec_bytes = sum(w * h for (w, h) in CFG0["grids"]) * CFG0["C"] * 2 + texels * CFG0["cout"] * 2
+    line = {
+        "metric": "train samples/s (fwd+bwd+Adam), config 1; decoded texels/s, config 0",
+        "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t_step_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
+        "config": {"workload": CFG1["workload"], "global_batch": B * world, "samples_per_gpu": B,
+                   "latents": "512^2x8 + 256^2x8 fp16", "mlp": "32-64-64-8", "parallelism": f"materials x{world}",
+                   "l2": "flushed (256 MB write) before every timed step"},
+        "roofline": {"kernel": "train_kernel", "bound": "tensor", "achieved": achieved_tf, "peak": pk["tensor"],
+                     "unit": "TFLOP/s", "frac": achieved_tf / pk["tensor"],
+                     "traffic": tr.get("train_kernel", {}).get("bytes_per_launch"),
+                     "peak_source": pk["source"] + " burst bf16",
+                     "algorithmic": f"{MLP_FLOP_TRAIN} FLOP/sample x {B} samples"},
+        "kernels_ms": {"train_kernel": t_train, "adam_kernel": t_adam},
+        "adam_roofline": {"bound": "hbm", "achieved": adam_bytes / (t_adam * 1e-3) / 1e9, "peak": pk["hbm"],
+                          "unit": "GB/s", "frac": adam_bytes / (t_adam * 1e-3) / 1e9 / pk["hbm"],
+                          "traffic": tr.get("adam_kernel", {}).get("bytes_per_launch"),
+                          "algorithmic": f"28 B/param x {P} params"},
+        "decode": {"workload": CFG0["workload"], "value": texels / (t_dec * 1e-3), "unit": "texels/s",
+                   "ms": t_dec, "tensor_frac": MLP_FLOP_FWD * texels / (t_dec * 1e-3) / 1e12 / pk["tensor"],
+                   "hbm_frac": dec_bytes / (t_dec * 1e-3) / 1e9 / pk["hbm"],
+                   "traffic": tr.get("decode_kernel", {}).get("bytes_per_launch")},
+        "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": pbytes,
+                "d2h_bytes_per_step": 4,
+                "note": "nt_train_step through the C ABI per step: parameter block from host memory, loss copied "
+                        "to pinned host memory and synchronised; no L2 flush"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.build()
+        line["cpu_baseline"] = cpu_train_baseline(O)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,210 @@
+/*
+ * nt_capi.h -- C-ABI boundary of the B200 neural-texture trainer / decoder.
+ *
+ * Everything here is plain C: POD structs, raw device pointers, sizes and an opaque
+ * stream handle.  No C++ or torch type crosses this boundary.  All device buffers are
+ * owned by the caller (the reference allocates every buffer in its driver,
+ * main.cpp:657-793); the library allocates no device memory of its own.
+ *
+ * Reference interface replaced (mavenkim2/neural_textures):
+ *   train.h:120-157   struct KernelParams            -> NtKernelParams
+ *   train.h:22-27     enum TrainingKernelType        -> NtTrainingKernelType
+ *   train.h:29-35     struct AdamConstants           -> NtAdamConstants
+ *   train.h:51-67     struct Feature                 -> NtFeature
+ *   train.h:158       InvokeOptimizeNetwork          -> nt_invoke_optimize_network
+ *   train.h:159       InvokeOptimizeFeatures         -> nt_invoke_optimize_features
+ *   train.h:160       InvokeTraining                 -> nt_invoke_training
+ *   train.h:161       InvokeInference                -> nt_invoke_inference
+ *   tests/forward_pass_test.h:6  RunForwardPassTest  -> nt_run_forward_pass_test
+ * The reference's entry points return void and surface errors at the next device
+ * synchronisation (main.cpp:103-110); every entry point here returns an nt_status and
+ * never throws.
+ *
+ * Network (fixed by the build, not by macros as in train.h:9-20):
+ *   input  32 = 2 x C latent channels + 8 positional features, zero padded
+ *   hidden 64 (ReLU) -> 64 (ReLU) -> output_channels (linear, <= 16)
+ * Weights are fp16, column-major and padded to multiples of 16 exactly as the reference
+ * stores them (train.h:84-112, main.cpp:195): layer l has W[col * padIn + row] with
+ * padIn = {32, 64, 64} and padOut = {64, 64, 16}.  Biases are fp16 with one entry per
+ * output (train.h:114-118).  Padded weight entries must be zero.
+ */
+#ifndef NT_CAPI_H
+#define NT_CAPI_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NT_API __attribute__((visibility("default")))
+#else
+#define NT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NT_CAPI_VERSION 1
+
+#define NT_NUM_FEATURES 2        /* latent grids; the reference has 4 float3 features (train.h:18) */
+#define NT_NUM_NETWORK_LAYERS 3  /* train.h:17 */
+#define NT_MLP_INPUT 32
+#define NT_MLP_HIDDEN 64
+#define NT_MAX_OUTPUT 16         /* train.h:11 NT_OUTPUT_SIZE */
+#define NT_POSENC_FEATURES 8     /* 2 frequencies x (u, v) x (sin, cos) */
+
+typedef enum nt_status {
+    NT_OK = 0,
+    NT_ERR_INVALID_ARG = 1,
+    NT_ERR_CUDA = 2,
+    NT_ERR_NCCL = 3,
+    NT_ERR_TIMEOUT = 4,
+    NT_ERR_BOUNDS = 5,
+    NT_ERR_UNSUPPORTED = 6
+} nt_status;
+
+/* train.h:22-27 */
+typedef enum NtTrainingKernelType {
+    NT_TRAIN_UNCONSTRAINED = 0, /* latents are free fp16 grids */
+    NT_TRAIN_BLOCK_FEATURES = 1, /* BC6 block latents: not built (returns NT_ERR_UNSUPPORTED) */
+    NT_TRAIN_FINALIZE = 2        /* network gradients only, latents frozen */
+} NtTrainingKernelType;
+
+typedef enum NtDtype { NT_DTYPE_F16 = 0, NT_DTYPE_F32 = 1 } NtDtype;
+
+/* Opaque CUDA stream (cudaStream_t); NULL means the legacy default stream. */
+typedef void *nt_stream_t;
+
+/* train.h:29-35 */
+typedef struct NtAdamConstants {
+    float beta1;
+    float beta2;
+    float learning_rate;
+    float epsilon;
+} NtAdamConstants;
+
+/* train.h:51-67, reduced to one mip level of fp16 channel-interleaved latents:
+ * grid[(y * width + x) * channels + c].  gradients / moment1 / moment2 are fp32 with the
+ * same layout (they may be NULL for decode-only use). */
+typedef struct NtFeature {
+    void *grid;         /* fp16 */
+    float *gradients;
+    float *moment1;
+    float *moment2;
+    int32_t width;
+    int32_t height;
+} NtFeature;
+
+/* train.h:120-157.  Passed by pointer; the library copies what it needs at launch, so the
+ * struct may be modified or freed as soon as the call returns. */
+typedef struct NtKernelParams {
+    NtFeature features[NT_NUM_FEATURES];
+    int32_t latent_channels;   /* C per grid: 8 or 12 */
+    int32_t output_channels;   /* used outputs (train.h:147 usedOutputChannels), 1..16 */
+
+    void *network_weights[NT_NUM_NETWORK_LAYERS];          /* fp16, padded column-major */
+    float *network_weight_gradients[NT_NUM_NETWORK_LAYERS];
+    float *network_weight_moment1[NT_NUM_NETWORK_LAYERS];
+    float *network_weight_moment2[NT_NUM_NETWORK_LAYERS];
+    void *network_biases[NT_NUM_NETWORK_LAYERS];           /* fp16, {64, 64, output_channels} */
+    float *network_bias_gradients[NT_NUM_NETWORK_LAYERS];
+    float *network_bias_moment1[NT_NUM_NETWORK_LAYERS];
+    float *network_bias_moment2[NT_NUM_NETWORK_LAYERS];
+
+    NtAdamConstants network_adam;
+    NtAdamConstants feature_adam;
+
+    /* Training target (stands in for train.h:69-77 ReferenceTexture): fp16
+     * [image_height][image_width][output_channels], sampled with Catmull-Rom and wrap
+     * addressing like filter/catmull_rom.h:39-89.  May be NULL for decode without MSE. */
+    const void *target;
+    float channel_loss_weights[NT_MAX_OUTPUT]; /* train.cu:876-888 channelWeights */
+
+    /* Decode output [image_height * image_width][output_channels] (train.cu:950-955). */
+    void *inference_output;
+    int32_t inference_output_dtype;  /* NtDtype */
+    float *inference_mse_accum;      /* optional: += sum of squared error vs target */
+
+    int32_t image_width;
+    int32_t image_height;
+
+    /* Training samples: one jittered sample per cell of a lattice_width x lattice_height
+     * lattice laid over the image (train.cu:827-844 uses one cell per texel of a 512^2
+     * region; sample_stride_* generalises the cell size in texels). */
+    int32_t lattice_width;
+    int32_t lattice_height;
+    float sample_stride_x;
+    float sample_stride_y;
+    int32_t texel_offset_x;          /* train.h:153-154 */
+    int32_t texel_offset_y;
+    int32_t num_samples;             /* must equal lattice_width * lattice_height */
+    int32_t step;                    /* train.h:156; Adam uses t = max(step, 1) */
+    uint32_t seed;                   /* 0 reproduces the reference's per-sample seeds */
+
+    float *loss_accum;               /* optional: += sum over samples and channels of err^2 */
+} NtKernelParams;
+
+/* ---- library ------------------------------------------------------------------------ */
+NT_API int32_t nt_version(void);
+NT_API const char *nt_get_last_error_string(void);
+NT_API size_t nt_kernel_params_size(void);
+/* Offset of a named field of NtKernelParams (for binding checks), or (size_t)-1. */
+NT_API size_t nt_kernel_params_offset(const char *field);
+/* Kernels launched by this library on the calling thread since load (for launch accounting). */
+NT_API uint64_t nt_launch_count(void);
+
+/* ---- train.h:158-161 ------------------------------------------------------------------ */
+
+/* train.h:160.  One fused pass over params->num_samples samples: sample latents and
+ * target, MLP forward, weighted L2 loss, MLP backward.  ACCUMULATES into the network
+ * weight/bias gradients and (UNCONSTRAINED) the latent gradients; the optimizers consume
+ * and zero them, as in the reference (train.cu:586, :621, :638). */
+NT_API nt_status nt_invoke_training(const NtKernelParams *params, NtTrainingKernelType type,
+                             nt_stream_t stream);
+
+/* train.h:158.  Adam over the three weight matrices and bias vectors (train.cu:681-726). */
+NT_API nt_status nt_invoke_optimize_network(const NtKernelParams *params, nt_stream_t stream);
+
+/* train.h:159.  Adam over every latent texel of both grids (train.cu:764-803). */
+NT_API nt_status nt_invoke_optimize_features(const NtKernelParams *params, NtTrainingKernelType type,
+                                      nt_stream_t stream);
+
+/* One launch doing the work of nt_invoke_optimize_network + nt_invoke_optimize_features
+ * (no reference counterpart; the reference makes two launches, main.cpp:1072-1076). */
+NT_API nt_status nt_invoke_optimize_all(const NtKernelParams *params, nt_stream_t stream);
+
+/* train.h:161.  Decode every texel centre of the image (train.cu:917-961). */
+NT_API nt_status nt_invoke_inference(const NtKernelParams *params, nt_stream_t stream);
+
+/* One training step as the reference driver runs it (main.cpp:1071-1077):
+ * training pass, then fused Adam over network and latents.  The caller increments step. */
+NT_API nt_status nt_train_step(const NtKernelParams *params, nt_stream_t stream);
+
+/* ---- tests/forward_pass_test.h:6 ------------------------------------------------------ */
+
+/* Known-answer test of the 12 -> 16 (ReLU) -> 16 network (tests/forward_pass_test.cu:152-275):
+ * returns 1 on pass, 0 on fail, and prints the first mismatch.  Runs on the current device. */
+NT_API int32_t nt_run_forward_pass_test(void);
+/* Same network on caller data: inputs [32][12] fp16, W0/W1 [16][16] column-major fp16,
+ * b0/b1 [16] fp16, outputs [32][16] fp16 (all device pointers). */
+NT_API nt_status nt_forward_pass_12x16x16(const void *inputs, const void *w0, const void *w1,
+                                   const void *b0, const void *b1, void *outputs,
+                                   nt_stream_t stream);
+
+/* ---- seeded set-up helpers (not in the reference: it loads EXR files, main.cpp:436-556) -- */
+
+/* Synthetic target: per channel the sigmoid of a sum of 16 seeded sinusoids with
+ * 1..64 cycles per texture and random direction and phase; fp16 [height][width][channels].
+ * pbr_normals with 12 channels: channels 3..5 hold the normal of the height channel 9. */
+NT_API nt_status nt_generate_target(void *target, int32_t width, int32_t height, int32_t channels,
+                             uint32_t seed, int32_t pbr_normals, nt_stream_t stream);
+/* Latent grid ~ U(-1, 1), fp16, hash-seeded. */
+NT_API nt_status nt_init_latents(void *grid, int64_t count, uint32_t seed, nt_stream_t stream);
+/* Device-side L2 flush helper: writes `bytes` of `scratch` (caller-owned). */
+NT_API nt_status nt_flush_l2(void *scratch, size_t bytes, nt_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NT_CAPI_H */

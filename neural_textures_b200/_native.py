@@ -1,0 +1,131 @@
+"""ctypes binding of libnt_b200.so (the C ABI declared in include/nt_capi.h).
+
+The library is built in-tree (neural_textures_b200/lib/libnt_b200.so).  There is no
+fallback: if the library is missing or fails to load, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+from . import build as _build
+
+LIB_PATH = _build.LIB
+
+NT_NUM_FEATURES = 2
+NT_NUM_NETWORK_LAYERS = 3
+NT_MAX_OUTPUT = 16
+
+NT_OK = 0
+STATUS_NAMES = {0: "NT_OK", 1: "NT_ERR_INVALID_ARG", 2: "NT_ERR_CUDA", 3: "NT_ERR_NCCL",
+                4: "NT_ERR_TIMEOUT", 5: "NT_ERR_BOUNDS", 6: "NT_ERR_UNSUPPORTED"}
+
+NT_TRAIN_UNCONSTRAINED = 0
+NT_TRAIN_BLOCK_FEATURES = 1
+NT_TRAIN_FINALIZE = 2
+NT_DTYPE_F16 = 0
+NT_DTYPE_F32 = 1
+
+
+class NtAdamConstants(C.Structure):
+    _fields_ = [("beta1", C.c_float), ("beta2", C.c_float), ("learning_rate", C.c_float),
+                ("epsilon", C.c_float)]
+
+
+class NtFeature(C.Structure):
+    _fields_ = [("grid", C.c_void_p), ("gradients", C.c_void_p), ("moment1", C.c_void_p),
+                ("moment2", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32)]
+
+
+class NtKernelParams(C.Structure):
+    _fields_ = [
+        ("features", NtFeature * NT_NUM_FEATURES),
+        ("latent_channels", C.c_int32),
+        ("output_channels", C.c_int32),
+        ("network_weights", C.c_void_p * 3),
+        ("network_weight_gradients", C.c_void_p * 3),
+        ("network_weight_moment1", C.c_void_p * 3),
+        ("network_weight_moment2", C.c_void_p * 3),
+        ("network_biases", C.c_void_p * 3),
+        ("network_bias_gradients", C.c_void_p * 3),
+        ("network_bias_moment1", C.c_void_p * 3),
+        ("network_bias_moment2", C.c_void_p * 3),
+        ("network_adam", NtAdamConstants),
+        ("feature_adam", NtAdamConstants),
+        ("target", C.c_void_p),
+        ("channel_loss_weights", C.c_float * NT_MAX_OUTPUT),
+        ("inference_output", C.c_void_p),
+        ("inference_output_dtype", C.c_int32),
+        ("inference_mse_accum", C.c_void_p),
+        ("image_width", C.c_int32),
+        ("image_height", C.c_int32),
+        ("lattice_width", C.c_int32),
+        ("lattice_height", C.c_int32),
+        ("sample_stride_x", C.c_float),
+        ("sample_stride_y", C.c_float),
+        ("texel_offset_x", C.c_int32),
+        ("texel_offset_y", C.c_int32),
+        ("num_samples", C.c_int32),
+        ("step", C.c_int32),
+        ("seed", C.c_uint32),
+        ("loss_accum", C.c_void_p),
+    ]
+
+
+# Every symbol include/nt_capi.h declares: name -> (restype, argtypes)
+_P = C.POINTER(NtKernelParams)
+SIGNATURES = {
+    "nt_version": (C.c_int32, []),
+    "nt_get_last_error_string": (C.c_char_p, []),
+    "nt_kernel_params_size": (C.c_size_t, []),
+    "nt_kernel_params_offset": (C.c_size_t, [C.c_char_p]),
+    "nt_launch_count": (C.c_uint64, []),
+    "nt_invoke_training": (C.c_int, [_P, C.c_int, C.c_void_p]),
+    "nt_invoke_optimize_network": (C.c_int, [_P, C.c_void_p]),
+    "nt_invoke_optimize_features": (C.c_int, [_P, C.c_int, C.c_void_p]),
+    "nt_invoke_optimize_all": (C.c_int, [_P, C.c_void_p]),
+    "nt_invoke_inference": (C.c_int, [_P, C.c_void_p]),
+    "nt_train_step": (C.c_int, [_P, C.c_void_p]),
+    "nt_run_forward_pass_test": (C.c_int32, []),
+    "nt_forward_pass_12x16x16": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
+    "nt_generate_target": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32,
+                                     C.c_int32, C.c_void_p]),
+    "nt_init_latents": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
+    "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
+}
+
+_lib = None
+
+
+class NtError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+def load(path: str | None = None):
+    """Load (once) and bind libnt_b200.so.  Raises OSError if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise OSError(f"{p} is missing: build it with `python -m neural_textures_b200.build` "
+                      "(there is no CPU fallback)")
+    lib = C.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != NT_OK:
+        msg = load().nt_get_last_error_string().decode(errors="replace")
+        raise NtError(status, msg)
+
+
+def last_error() -> str:
+    return load().nt_get_last_error_string().decode(errors="replace")

@@ -1,0 +1,250 @@
+"""Host-side mirror of the reference's training / decode interface over the C ABI.
+
+mavenkim2/neural_textures exposes train.h:158-161 (InvokeOptimizeNetwork,
+InvokeOptimizeFeatures, InvokeTraining, InvokeInference) taking a KernelParams by value,
+and tests/forward_pass_test.h:6 (RunForwardPassTest).  The same entry points are exported
+here under the same names (plus snake_case aliases); they take an NtKernelParams built from
+device buffers and raise NtError when the library rejects a call, as the reference's
+driver raises std::runtime_error from CheckCuda (main.cpp:103-110).
+
+NeuralTexture owns the device buffers of one material (what the reference's driver
+allocates in main.cpp:657-793) using torch only as the allocator; every computation runs
+in libnt_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import math
+
+import numpy as np
+
+from . import _native as N
+from ._native import NtError, NtKernelParams, check, load
+
+
+class TrainingKernelType(enum.IntEnum):
+    """train.h:22-27"""
+    UNCONSTRAINED = N.NT_TRAIN_UNCONSTRAINED
+    BLOCK_FEATURES = N.NT_TRAIN_BLOCK_FEATURES
+    FINALIZE = N.NT_TRAIN_FINALIZE
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return int(stream.cuda_stream)
+
+
+def InvokeTraining(params: NtKernelParams, type=TrainingKernelType.UNCONSTRAINED, stream=None):
+    """train.h:160 -- fused sample / forward / loss / backward, accumulating gradients."""
+    check(load().nt_invoke_training(C.byref(params), int(type), _stream(stream)))
+
+
+def InvokeOptimizeNetwork(params: NtKernelParams, stream=None):
+    """train.h:158 -- Adam over the network weights and biases (consumes and zeroes grads)."""
+    check(load().nt_invoke_optimize_network(C.byref(params), _stream(stream)))
+
+
+def InvokeOptimizeFeatures(params: NtKernelParams, type=TrainingKernelType.UNCONSTRAINED, stream=None):
+    """train.h:159 -- Adam over both latent grids (consumes and zeroes grads)."""
+    check(load().nt_invoke_optimize_features(C.byref(params), int(type), _stream(stream)))
+
+
+def InvokeOptimizeAll(params: NtKernelParams, stream=None):
+    """Network + latent Adam in one launch."""
+    check(load().nt_invoke_optimize_all(C.byref(params), _stream(stream)))
+
+
+def InvokeInference(params: NtKernelParams, stream=None):
+    """train.h:161 -- decode every texel centre into params.inference_output."""
+    check(load().nt_invoke_inference(C.byref(params), _stream(stream)))
+
+
+def TrainStep(params: NtKernelParams, stream=None):
+    """One training step as the reference driver issues it (main.cpp:1071-1076)."""
+    check(load().nt_train_step(C.byref(params), _stream(stream)))
+
+
+def RunForwardPassTest() -> bool:
+    """tests/forward_pass_test.h:6 -- the 12 -> 16 -> 16 known-answer test on the device."""
+    return bool(load().nt_run_forward_pass_test())
+
+
+invoke_training = InvokeTraining
+invoke_optimize_network = InvokeOptimizeNetwork
+invoke_optimize_features = InvokeOptimizeFeatures
+invoke_optimize_all = InvokeOptimizeAll
+invoke_inference = InvokeInference
+train_step = TrainStep
+run_forward_pass_test = RunForwardPassTest
+
+
+def launch_count() -> int:
+    return int(load().nt_launch_count())
+
+
+# ---------------------------------------------------------------------------------------
+# parameter initialisation (host, seeded)
+
+PAD_IN = (32, 64, 64)
+PAD_OUT = (64, 64, 16)
+
+
+def he_normal_weights(seed: int, cout: int) -> list[np.ndarray]:
+    """He-normal N(0, 2 / fan_in) weights in the padded column-major fp16 layout
+    (W[out * padIn + in]); padded rows / columns are zero.  Returned as fp16 arrays."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for l in range(3):
+        W = np.zeros((PAD_OUT[l], PAD_IN[l]), np.float32)
+        active_out = 64 if l < 2 else cout
+        fan = PAD_IN[l]
+        W[:active_out, :fan] = rng.standard_normal((active_out, fan)) * math.sqrt(2.0 / fan)
+        out.append(W.astype(np.float16).reshape(-1))
+    return out
+
+
+def zero_padded_inputs(W0: np.ndarray, n_inputs: int) -> np.ndarray:
+    """Zero layer-0 weights of the padded inputs (>= n_inputs)."""
+    W = W0.reshape(64, 32).copy()
+    W[:, n_inputs:] = 0
+    return W.reshape(-1)
+
+
+class NeuralTexture:
+    """Device state of one material: two fp16 latent grids, the 32 -> 64 -> 64 -> cout
+    network, fp32 gradients and Adam moments for everything, and the fp16 target."""
+
+    def __init__(self, image_w: int, image_h: int, grid_sizes=((512, 512), (256, 256)),
+                 latent_channels: int = 8, output_channels: int = 8, device="cuda",
+                 lattice=None, latent_lr: float = 1e-2, network_lr: float = 5e-3,
+                 beta1: float = 0.9, beta2: float = 0.99, eps: float = 1e-8):
+        import torch
+        self.torch = torch
+        self.device = torch.device(device)
+        self.image_w, self.image_h = image_w, image_h
+        self.C, self.cout = latent_channels, output_channels
+        self.grid_sizes = [tuple(g) for g in grid_sizes]
+        f16, f32 = torch.float16, torch.float32
+        z = lambda shape, dt: torch.zeros(shape, dtype=dt, device=self.device)
+        self.grids = [z((h, w, self.C), f16) for (w, h) in self.grid_sizes]
+        self.ggrads = [z(g.shape, f32) for g in self.grids]
+        self.gm1 = [z(g.shape, f32) for g in self.grids]
+        self.gm2 = [z(g.shape, f32) for g in self.grids]
+        self.W = [z(PAD_OUT[l] * PAD_IN[l], f16) for l in range(3)]
+        self.b = [z(64, f16), z(64, f16), z(self.cout, f16)]
+        self.gW = [z(w.shape, f32) for w in self.W]
+        self.mW = [z(w.shape, f32) for w in self.W]
+        self.vW = [z(w.shape, f32) for w in self.W]
+        self.gb = [z(b.shape, f32) for b in self.b]
+        self.mb = [z(b.shape, f32) for b in self.b]
+        self.vb = [z(b.shape, f32) for b in self.b]
+        self.target = z((image_h, image_w, self.cout), f16)
+        self.loss_accum = z(1, f32)
+        if lattice is None:
+            lattice = (image_w, image_h)
+        self.lattice = tuple(lattice)
+        self.latent_adam = (beta1, beta2, latent_lr, eps)
+        self.network_adam = (beta1, beta2, network_lr, eps)
+        self.channel_weights = [1.0] * self.cout
+        self.seed = 0
+        self.step = 0
+
+    # -- initialisation -------------------------------------------------------------------
+    def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False,
+             stream=None):
+        torch = self.torch
+        L = load()
+        for i, g in enumerate(self.grids):
+            check(L.nt_init_latents(g.data_ptr(), g.numel(), seed * 7919 + i + 1, _stream(stream)))
+        Ws = he_normal_weights(seed, self.cout)
+        Ws[0] = zero_padded_inputs(Ws[0], 2 * self.C + 8)
+        for l in range(3):
+            self.W[l].copy_(torch.from_numpy(Ws[l]).to(self.device))
+            self.b[l].zero_()
+        ts = seed if target_seed is None else target_seed
+        check(L.nt_generate_target(self.target.data_ptr(), self.image_w, self.image_h, self.cout,
+                                   ts, int(pbr_normals), _stream(stream)))
+        for t in self.ggrads + self.gm1 + self.gm2 + self.gW + self.mW + self.vW + self.gb + self.mb + self.vb:
+            t.zero_()
+        self.step = 0
+
+    def load_host(self, grids, W, b, target=None):
+        """Upload host fp16 arrays (grids [h][w][C], padded W, b, optional target)."""
+        torch = self.torch
+        for g, src in zip(self.grids, grids):
+            g.copy_(torch.from_numpy(np.ascontiguousarray(src)).view(torch.float16).reshape(g.shape))
+        for dst, src in zip(self.W, W):
+            dst.copy_(torch.from_numpy(np.ascontiguousarray(src)).view(torch.float16).reshape(dst.shape))
+        for dst, src in zip(self.b, b):
+            dst.copy_(torch.from_numpy(np.ascontiguousarray(src)).view(torch.float16).reshape(dst.shape))
+        if target is not None:
+            self.target.copy_(torch.from_numpy(np.ascontiguousarray(target)).view(torch.float16)
+                              .reshape(self.target.shape))
+
+    # -- parameter block --------------------------------------------------------------------
+    def params(self, step: int | None = None, inference_output=None, mse_accum=None,
+               loss_accum: bool = True) -> NtKernelParams:
+        p = NtKernelParams()
+        for i in range(2):
+            f = p.features[i]
+            f.grid = self.grids[i].data_ptr()
+            f.gradients = self.ggrads[i].data_ptr()
+            f.moment1 = self.gm1[i].data_ptr()
+            f.moment2 = self.gm2[i].data_ptr()
+            f.width, f.height = self.grid_sizes[i]
+        p.latent_channels, p.output_channels = self.C, self.cout
+        for l in range(3):
+            p.network_weights[l] = self.W[l].data_ptr()
+            p.network_weight_gradients[l] = self.gW[l].data_ptr()
+            p.network_weight_moment1[l] = self.mW[l].data_ptr()
+            p.network_weight_moment2[l] = self.vW[l].data_ptr()
+            p.network_biases[l] = self.b[l].data_ptr()
+            p.network_bias_gradients[l] = self.gb[l].data_ptr()
+            p.network_bias_moment1[l] = self.mb[l].data_ptr()
+            p.network_bias_moment2[l] = self.vb[l].data_ptr()
+        (p.network_adam.beta1, p.network_adam.beta2, p.network_adam.learning_rate,
+         p.network_adam.epsilon) = self.network_adam
+        (p.feature_adam.beta1, p.feature_adam.beta2, p.feature_adam.learning_rate,
+         p.feature_adam.epsilon) = self.latent_adam
+        p.target = self.target.data_ptr()
+        for c in range(self.cout):
+            p.channel_loss_weights[c] = self.channel_weights[c]
+        if inference_output is not None:
+            p.inference_output = inference_output.data_ptr()
+            p.inference_output_dtype = (N.NT_DTYPE_F32 if inference_output.dtype == self.torch.float32
+                                        else N.NT_DTYPE_F16)
+        if mse_accum is not None:
+            p.inference_mse_accum = mse_accum.data_ptr()
+        p.image_width, p.image_height = self.image_w, self.image_h
+        p.lattice_width, p.lattice_height = self.lattice
+        p.sample_stride_x = self.image_w / self.lattice[0]
+        p.sample_stride_y = self.image_h / self.lattice[1]
+        p.num_samples = self.lattice[0] * self.lattice[1]
+        p.step = self.step if step is None else step
+        p.seed = self.seed
+        if loss_accum:
+            p.loss_accum = self.loss_accum.data_ptr()
+        return p
+
+    # -- operations ---------------------------------------------------------------------------
+    def train_step(self, stream=None, params: NtKernelParams | None = None):
+        TrainStep(params or self.params(), stream)
+        self.step += 1
+
+    def decode(self, dtype=None, stream=None, out=None):
+        torch = self.torch
+        if out is None:
+            out = torch.empty((self.image_h * self.image_w, self.cout),
+                              dtype=dtype or torch.float16, device=self.device)
+        InvokeInference(self.params(inference_output=out), stream)
+        return out
+
+    def host_model(self):
+        """fp16 copies (numpy uint16 bit patterns) of grids, weights and biases."""
+        torch = self.torch
+        to16 = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+        return ([to16(g) for g in self.grids], [to16(w) for w in self.W], [to16(b) for b in self.b])

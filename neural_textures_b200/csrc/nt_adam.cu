@@ -1,0 +1,93 @@
+// nt_adam.cu -- one fused Adam launch over any set of fp16 parameter buffers with fp32
+// gradient / first / second moment buffers (MLP weights, biases and both latent grids).
+//
+// Restates AdamUpdateParameter (mavenkim2/neural_textures train.cu:521-543) with the
+// buffer semantics of OptimizeParameterBuffer (train.cu:566-588): entries whose gradient is
+// exactly zero are skipped (their moments do not decay) and every consumed gradient is
+// zeroed.  The reference launches the network optimizer as a single warp (train.cu:985-988)
+// and the latent optimizer as a second kernel; here one launch streams all segments with
+// 16-byte vector accesses.  The float operations are written out with explicit rounding in
+// the order of the reference expression so the result is bit-identical to the CPU oracle;
+// the bias corrections 1 - beta^t are computed once per step on the host.
+#include "nt_kernels.cuh"
+
+namespace nt {
+
+__device__ __forceinline__ float adam_one(float w, float g, float &m, float &v, const AdamSegment &s)
+{
+    const float m1 = __fadd_rn(__fmul_rn(s.beta1, m), __fmul_rn(__fsub_rn(1.f, s.beta1), g));
+    const float m2 = __fadd_rn(__fmul_rn(s.beta2, v), __fmul_rn(__fmul_rn(__fsub_rn(1.f, s.beta2), g), g));
+    m = m1;
+    v = m2;
+    const float mhat = __fdiv_rn(m1, s.bc1);
+    const float vhat = __fdiv_rn(m2, s.bc2);
+    return __fsub_rn(w, __fdiv_rn(__fmul_rn(s.lr, mhat), __fadd_rn(__fsqrt_rn(vhat), s.eps)));
+}
+
+constexpr int kAdamThreads = 256;
+constexpr int kAdamPerThread = 8;
+
+__global__ void __launch_bounds__(kAdamThreads) adam_kernel(const AdamLaunch p)
+{
+    const int b = blockIdx.x;
+    int si = 0;
+#pragma unroll 1
+    while (si + 1 < p.nseg && b >= p.seg[si + 1].first_block) ++si;
+    const AdamSegment &s = p.seg[si];
+    const int64_t i0 = ((int64_t)(b - s.first_block) * kAdamThreads + threadIdx.x) * kAdamPerThread;
+    if (i0 >= s.n) return;
+    const bool vec = i0 + kAdamPerThread <= s.n && ((reinterpret_cast<uintptr_t>(s.w) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(s.g) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(s.m) & 15) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(s.v) & 15) == 0);
+    if (vec) {
+        const float4 g0 = *reinterpret_cast<const float4 *>(s.g + i0);
+        const float4 g1 = *reinterpret_cast<const float4 *>(s.g + i0 + 4);
+        float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        bool any = false;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) any |= gv[e] != 0.f;
+        if (!any) return;
+        uint4 wraw = *reinterpret_cast<const uint4 *>(s.w + i0);
+        float4 m0 = *reinterpret_cast<const float4 *>(s.m + i0);
+        float4 m1 = *reinterpret_cast<const float4 *>(s.m + i0 + 4);
+        float4 v0 = *reinterpret_cast<const float4 *>(s.v + i0);
+        float4 v1 = *reinterpret_cast<const float4 *>(s.v + i0 + 4);
+        float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        __half *wh = reinterpret_cast<__half *>(&wraw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if (gv[e] == 0.f) continue;
+            wh[e] = __float2half_rn(adam_one(__half2float(wh[e]), gv[e], mv[e], vv[e], s));
+        }
+        *reinterpret_cast<uint4 *>(s.w + i0) = wraw;
+        *reinterpret_cast<float4 *>(s.m + i0) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+        *reinterpret_cast<float4 *>(s.m + i0 + 4) = make_float4(mv[4], mv[5], mv[6], mv[7]);
+        *reinterpret_cast<float4 *>(s.v + i0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        *reinterpret_cast<float4 *>(s.v + i0 + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
+        *reinterpret_cast<float4 *>(s.g + i0) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(s.g + i0 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+        const int64_t end = i0 + kAdamPerThread < s.n ? i0 + kAdamPerThread : s.n;
+        for (int64_t i = i0; i < end; ++i) {
+            const float g = s.g[i];
+            if (g == 0.f) continue;
+            float m = s.m[i], v = s.v[i];
+            s.w[i] = __float2half_rn(adam_one(__half2float(s.w[i]), g, m, v, s));
+            s.m[i] = m;
+            s.v[i] = v;
+            s.g[i] = 0.f;
+        }
+    }
+}
+
+cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream)
+{
+    if (p.total_blocks <= 0) return cudaSuccess;
+    adam_kernel<<<p.total_blocks, kAdamThreads, 0, stream>>>(p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace nt

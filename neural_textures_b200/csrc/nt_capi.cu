@@ -1,0 +1,388 @@
+// nt_capi.cu -- the extern "C" boundary (include/nt_capi.h): argument validation, launch
+// descriptors, per-step Adam constants and error reporting.  No exception crosses the ABI;
+// every entry point returns an nt_status and records a message for
+// nt_get_last_error_string().
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstddef>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <string>
+#include <utility>
+
+#include "nt_capi.h"
+#include "nt_kernels.cuh"
+
+namespace nt {
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int sm_count()
+{
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 148;
+    }
+    return cached[dev];
+}
+
+cudaError_t set_smem_limit(const void *kernel, size_t bytes)
+{
+    static std::mutex mu;
+    static std::set<std::pair<const void *, int>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({kernel, dev})) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done.insert({kernel, dev});
+    return e;
+}
+
+cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t seed, int32_t pbr, cudaStream_t st);
+cudaError_t launch_init_latents(void *grid, int64_t count, uint32_t seed, cudaStream_t st);
+cudaError_t launch_flush(void *scratch, size_t bytes, cudaStream_t st);
+
+}  // namespace nt
+
+using namespace nt;
+
+static thread_local std::string g_last_error;
+
+static nt_status fail(nt_status st, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+static nt_status check_cuda(cudaError_t e, const char *what)
+{
+    if (e == cudaSuccess) return NT_OK;
+    return fail(NT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+#define NT_REQUIRE(cond, ...)                                     \
+    do {                                                          \
+        if (!(cond)) return fail(NT_ERR_INVALID_ARG, __VA_ARGS__); \
+    } while (0)
+
+static nt_status validate_network(const NtKernelParams *p)
+{
+    NT_REQUIRE(p->latent_channels == 8 || p->latent_channels == 12,
+               "latent_channels must be 8 or 12 (got %d)", p->latent_channels);
+    NT_REQUIRE(p->output_channels >= 1 && p->output_channels <= NT_MAX_OUTPUT,
+               "output_channels must be in [1, %d] (got %d)", NT_MAX_OUTPUT, p->output_channels);
+    for (int l = 0; l < NT_NUM_NETWORK_LAYERS; ++l) {
+        NT_REQUIRE(p->network_weights[l] && aligned16(p->network_weights[l]),
+                   "network_weights[%d] must be a non-null 16-byte aligned device pointer", l);
+        NT_REQUIRE(p->network_biases[l], "network_biases[%d] is null", l);
+    }
+    for (int f = 0; f < NT_NUM_FEATURES; ++f) {
+        const NtFeature &ft = p->features[f];
+        NT_REQUIRE(ft.grid && aligned16(ft.grid), "features[%d].grid must be a non-null 16-byte aligned pointer", f);
+        NT_REQUIRE(ft.width >= 1 && ft.height >= 1, "features[%d] has empty size %dx%d", f, ft.width, ft.height);
+        NT_REQUIRE((int64_t)ft.width * ft.height * p->latent_channels < (int64_t)1 << 31,
+                   "features[%d] is too large", f);
+    }
+    return NT_OK;
+}
+
+static NetView net_view(const NtKernelParams *p)
+{
+    NetView n;
+    for (int l = 0; l < 3; ++l) {
+        n.W[l] = reinterpret_cast<const __half *>(p->network_weights[l]);
+        n.b[l] = reinterpret_cast<const __half *>(p->network_biases[l]);
+    }
+    n.cout = p->output_channels;
+    return n;
+}
+
+static AdamSegment make_segment(void *w, float *g, float *m, float *v, int64_t n, const NtAdamConstants &c,
+                                int32_t step)
+{
+    AdamSegment s;
+    s.w = reinterpret_cast<__half *>(w);
+    s.g = g;
+    s.m = m;
+    s.v = v;
+    s.n = n;
+    s.lr = c.learning_rate;
+    s.beta1 = c.beta1;
+    s.beta2 = c.beta2;
+    s.eps = c.epsilon;
+    const int t = step > 0 ? step : 1;  // train.cu:528
+    s.bc1 = 1.0f - powf(c.beta1, (float)t);
+    s.bc2 = 1.0f - powf(c.beta2, (float)t);
+    s.first_block = 0;
+    return s;
+}
+
+static void finalize_adam(AdamLaunch &a)
+{
+    int blocks = 0;
+    for (int i = 0; i < a.nseg; ++i) {
+        a.seg[i].first_block = blocks;
+        blocks += (int)((a.seg[i].n + 256 * 8 - 1) / (256 * 8));
+    }
+    a.total_blocks = blocks;
+}
+
+static nt_status add_network_segments(const NtKernelParams *p, AdamLaunch &a)
+{
+    static const int64_t wcount[3] = {64 * 32, 64 * 64, 16 * 64};
+    const int64_t bcount[3] = {64, 64, p->output_channels};
+    for (int l = 0; l < 3; ++l) {
+        NT_REQUIRE(p->network_weight_gradients[l] && p->network_weight_moment1[l] && p->network_weight_moment2[l],
+                   "network weight gradient / moment buffers of layer %d are required", l);
+        NT_REQUIRE(p->network_bias_gradients[l] && p->network_bias_moment1[l] && p->network_bias_moment2[l],
+                   "network bias gradient / moment buffers of layer %d are required", l);
+        a.seg[a.nseg++] = make_segment(p->network_weights[l], p->network_weight_gradients[l],
+                                       p->network_weight_moment1[l], p->network_weight_moment2[l], wcount[l],
+                                       p->network_adam, p->step);
+        a.seg[a.nseg++] = make_segment(p->network_biases[l], p->network_bias_gradients[l],
+                                       p->network_bias_moment1[l], p->network_bias_moment2[l], bcount[l],
+                                       p->network_adam, p->step);
+    }
+    return NT_OK;
+}
+
+static nt_status add_feature_segments(const NtKernelParams *p, AdamLaunch &a)
+{
+    for (int f = 0; f < NT_NUM_FEATURES; ++f) {
+        const NtFeature &ft = p->features[f];
+        NT_REQUIRE(ft.gradients && ft.moment1 && ft.moment2,
+                   "features[%d] gradient / moment buffers are required", f);
+        a.seg[a.nseg++] = make_segment(ft.grid, ft.gradients, ft.moment1, ft.moment2,
+                                       (int64_t)ft.width * ft.height * p->latent_channels, p->feature_adam, p->step);
+    }
+    return NT_OK;
+}
+
+extern "C" {
+
+int32_t nt_version(void) { return NT_CAPI_VERSION; }
+
+const char *nt_get_last_error_string(void) { return g_last_error.c_str(); }
+
+size_t nt_kernel_params_size(void) { return sizeof(NtKernelParams); }
+
+size_t nt_kernel_params_offset(const char *field)
+{
+    if (!field) return (size_t)-1;
+#define NT_FIELD(name) \
+    if (!strcmp(field, #name)) return offsetof(NtKernelParams, name);
+    NT_FIELD(features)
+    NT_FIELD(latent_channels)
+    NT_FIELD(output_channels)
+    NT_FIELD(network_weights)
+    NT_FIELD(network_weight_gradients)
+    NT_FIELD(network_weight_moment1)
+    NT_FIELD(network_weight_moment2)
+    NT_FIELD(network_biases)
+    NT_FIELD(network_bias_gradients)
+    NT_FIELD(network_bias_moment1)
+    NT_FIELD(network_bias_moment2)
+    NT_FIELD(network_adam)
+    NT_FIELD(feature_adam)
+    NT_FIELD(target)
+    NT_FIELD(channel_loss_weights)
+    NT_FIELD(inference_output)
+    NT_FIELD(inference_output_dtype)
+    NT_FIELD(inference_mse_accum)
+    NT_FIELD(image_width)
+    NT_FIELD(image_height)
+    NT_FIELD(lattice_width)
+    NT_FIELD(lattice_height)
+    NT_FIELD(sample_stride_x)
+    NT_FIELD(sample_stride_y)
+    NT_FIELD(texel_offset_x)
+    NT_FIELD(texel_offset_y)
+    NT_FIELD(num_samples)
+    NT_FIELD(step)
+    NT_FIELD(seed)
+    NT_FIELD(loss_accum)
+#undef NT_FIELD
+    return (size_t)-1;
+}
+
+uint64_t nt_launch_count(void) { return g_launches.load(); }
+
+nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type, nt_stream_t stream)
+{
+    NT_REQUIRE(p, "params is null");
+    if (type == NT_TRAIN_BLOCK_FEATURES)
+        return fail(NT_ERR_UNSUPPORTED, "BLOCK_FEATURES training (BC6 block latents) is not built");
+    NT_REQUIRE(type == NT_TRAIN_UNCONSTRAINED || type == NT_TRAIN_FINALIZE, "unknown training kernel type %d",
+               (int)type);
+    nt_status st = validate_network(p);
+    if (st != NT_OK) return st;
+    NT_REQUIRE(p->target && aligned16(p->target), "target must be a non-null 16-byte aligned device pointer");
+    NT_REQUIRE(p->image_width >= 1 && p->image_height >= 1, "image size must be positive");
+    NT_REQUIRE(p->lattice_width >= 1 && p->lattice_height >= 1, "lattice size must be positive");
+    NT_REQUIRE((int64_t)p->lattice_width * p->lattice_height == p->num_samples,
+               "num_samples (%d) must equal lattice_width * lattice_height (%d x %d)", p->num_samples,
+               p->lattice_width, p->lattice_height);
+    NT_REQUIRE(p->sample_stride_x > 0.f && p->sample_stride_y > 0.f, "sample strides must be positive");
+    for (int l = 0; l < 3; ++l)
+        NT_REQUIRE(p->network_weight_gradients[l] && p->network_bias_gradients[l],
+                   "network gradient buffers of layer %d are required", l);
+    if (type == NT_TRAIN_UNCONSTRAINED)
+        for (int f = 0; f < NT_NUM_FEATURES; ++f)
+            NT_REQUIRE(p->features[f].gradients && aligned16(p->features[f].gradients),
+                       "features[%d].gradients must be a 16-byte aligned device pointer", f);
+
+    TrainLaunch L;
+    memset(&L, 0, sizeof L);
+    for (int f = 0; f < 2; ++f) {
+        L.grid[f] = reinterpret_cast<const __half *>(p->features[f].grid);
+        L.ggrid[f] = p->features[f].gradients;
+        L.gw[f] = p->features[f].width;
+        L.gh[f] = p->features[f].height;
+    }
+    L.net = net_view(p);
+    for (int l = 0; l < 3; ++l) {
+        L.gW[l] = p->network_weight_gradients[l];
+        L.gb[l] = p->network_bias_gradients[l];
+    }
+    L.target = reinterpret_cast<const __half *>(p->target);
+    for (int c = 0; c < 16; ++c) L.cw[c] = c < p->output_channels ? p->channel_loss_weights[c] : 0.f;
+    L.sampler.image_w = p->image_width;
+    L.sampler.image_h = p->image_height;
+    L.sampler.lattice_w = p->lattice_width;
+    L.sampler.lattice_h = p->lattice_height;
+    L.sampler.stride_x = p->sample_stride_x;
+    L.sampler.stride_y = p->sample_stride_y;
+    L.sampler.offset_x = p->texel_offset_x;
+    L.sampler.offset_y = p->texel_offset_y;
+    L.sampler.step = (uint32_t)p->step;
+    L.sampler.seed = p->seed;
+    L.inv_num_samples = 1.0f / (float)p->num_samples;
+    L.loss_accum = p->loss_accum;
+    L.finalize = type == NT_TRAIN_FINALIZE;
+    L.tiles_x = (p->lattice_width + kTileSide - 1) / kTileSide;
+    L.tiles_y = (p->lattice_height + kTileSide - 1) / kTileSide;
+    return check_cuda(launch_train(L, p->latent_channels, (cudaStream_t)stream), "training kernel");
+}
+
+nt_status nt_invoke_optimize_network(const NtKernelParams *p, nt_stream_t stream)
+{
+    NT_REQUIRE(p, "params is null");
+    nt_status st = validate_network(p);
+    if (st != NT_OK) return st;
+    AdamLaunch a;
+    memset(&a, 0, sizeof a);
+    if ((st = add_network_segments(p, a)) != NT_OK) return st;
+    finalize_adam(a);
+    return check_cuda(launch_adam(a, (cudaStream_t)stream), "Adam (network)");
+}
+
+nt_status nt_invoke_optimize_features(const NtKernelParams *p, NtTrainingKernelType type, nt_stream_t stream)
+{
+    NT_REQUIRE(p, "params is null");
+    if (type == NT_TRAIN_BLOCK_FEATURES)
+        return fail(NT_ERR_UNSUPPORTED, "BLOCK_FEATURES optimisation (BC6 block latents) is not built");
+    if (type == NT_TRAIN_FINALIZE) return NT_OK;  // main.cpp:1074: features are frozen
+    nt_status st = validate_network(p);
+    if (st != NT_OK) return st;
+    AdamLaunch a;
+    memset(&a, 0, sizeof a);
+    if ((st = add_feature_segments(p, a)) != NT_OK) return st;
+    finalize_adam(a);
+    return check_cuda(launch_adam(a, (cudaStream_t)stream), "Adam (features)");
+}
+
+nt_status nt_invoke_optimize_all(const NtKernelParams *p, nt_stream_t stream)
+{
+    NT_REQUIRE(p, "params is null");
+    nt_status st = validate_network(p);
+    if (st != NT_OK) return st;
+    AdamLaunch a;
+    memset(&a, 0, sizeof a);
+    if ((st = add_network_segments(p, a)) != NT_OK) return st;
+    if ((st = add_feature_segments(p, a)) != NT_OK) return st;
+    finalize_adam(a);
+    return check_cuda(launch_adam(a, (cudaStream_t)stream), "Adam (fused)");
+}
+
+nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
+{
+    NT_REQUIRE(p, "params is null");
+    nt_status st = validate_network(p);
+    if (st != NT_OK) return st;
+    NT_REQUIRE(p->image_width >= 1 && p->image_height >= 1, "image size must be positive");
+    NT_REQUIRE(p->inference_output, "inference_output is null");
+    NT_REQUIRE(p->inference_output_dtype == NT_DTYPE_F16 || p->inference_output_dtype == NT_DTYPE_F32,
+               "inference_output_dtype must be NT_DTYPE_F16 or NT_DTYPE_F32");
+    NT_REQUIRE(!(p->inference_output_dtype == NT_DTYPE_F16 && p->output_channels == 8) ||
+                   aligned16(p->inference_output),
+               "inference_output must be 16-byte aligned");
+    NT_REQUIRE(!p->inference_mse_accum || p->target, "inference_mse_accum requires a target");
+    DecodeLaunch L;
+    memset(&L, 0, sizeof L);
+    for (int f = 0; f < 2; ++f) {
+        L.grid[f] = reinterpret_cast<const __half *>(p->features[f].grid);
+        L.gw[f] = p->features[f].width;
+        L.gh[f] = p->features[f].height;
+    }
+    L.net = net_view(p);
+    L.out = p->inference_output;
+    L.out_f32 = p->inference_output_dtype == NT_DTYPE_F32;
+    L.target = reinterpret_cast<const __half *>(p->target);
+    L.mse_accum = p->inference_mse_accum;
+    L.image_w = p->image_width;
+    L.image_h = p->image_height;
+    L.tiles_x = (p->image_width + kTileSide - 1) / kTileSide;
+    L.tiles_y = (p->image_height + kTileSide - 1) / kTileSide;
+    return check_cuda(launch_decode(L, p->latent_channels, (cudaStream_t)stream), "decode kernel");
+}
+
+nt_status nt_train_step(const NtKernelParams *p, nt_stream_t stream)
+{
+    nt_status st = nt_invoke_training(p, NT_TRAIN_UNCONSTRAINED, stream);
+    if (st != NT_OK) return st;
+    return nt_invoke_optimize_all(p, stream);
+}
+
+nt_status nt_generate_target(void *target, int32_t width, int32_t height, int32_t channels, uint32_t seed,
+                             int32_t pbr_normals, nt_stream_t stream)
+{
+    NT_REQUIRE(target, "target is null");
+    NT_REQUIRE(width >= 1 && height >= 1, "target size must be positive");
+    NT_REQUIRE(channels >= 1 && channels <= 16, "target channels must be in [1, 16]");
+    return check_cuda(launch_target(target, width, height, channels, seed, pbr_normals, (cudaStream_t)stream),
+                      "target generator");
+}
+
+nt_status nt_init_latents(void *grid, int64_t count, uint32_t seed, nt_stream_t stream)
+{
+    NT_REQUIRE(grid, "grid is null");
+    NT_REQUIRE(count >= 0, "count must be non-negative");
+    if (count == 0) return NT_OK;
+    return check_cuda(launch_init_latents(grid, count, seed, (cudaStream_t)stream), "latent init");
+}
+
+nt_status nt_flush_l2(void *scratch, size_t bytes, nt_stream_t stream)
+{
+    NT_REQUIRE(scratch && aligned16(scratch), "scratch must be a 16-byte aligned device pointer");
+    if (bytes < 16) return NT_OK;
+    return check_cuda(launch_flush(scratch, bytes, (cudaStream_t)stream), "L2 flush");
+}
+
+}  // extern "C"

@@ -1,0 +1,237 @@
+// nt_common.cuh -- device helpers shared by the decode, training, Adam and codec kernels.
+//
+// Sampling conventions restate mavenkim2/neural_textures:
+//   texel centre uv * size - 0.5, floor, fraction ........ train.cu:288-291
+//   wrap addressing ...................................... train.cu:65-69
+//   Catmull-Rom weights (a = -0.5) ....................... filter/catmull_rom.h:56-59
+//   per-sample xorshift32 RNG and seed ................... train.cu:37-58, :833
+//   jittered sample per lattice cell, clamped ............ train.cu:827-844
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nt_capi.h"
+
+namespace nt {
+
+constexpr int kNumSms = 148;  // B200; the host reads the real count at run time
+
+// ---------------------------------------------------------------------------------------
+// fp16 packing
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi)
+{
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t v)
+{
+    __half2 h = *reinterpret_cast<__half2 *>(&v);
+    return __half22float2(h);
+}
+
+__device__ __forceinline__ float round_half(float f) { return __half2float(__float2half_rn(f)); }
+
+// ---------------------------------------------------------------------------------------
+// RNG (train.cu:37-58).  seed 0 reproduces the reference's per-sample seeds exactly.
+
+__device__ __forceinline__ uint32_t rng_seed(uint32_t sample_index, uint32_t step, uint32_t seed)
+{
+    uint32_t s = sample_index ^ (step * 747796405u + 2891336453u) ^ (seed * 0x9E3779B9u);
+    return s ? s : 1u;
+}
+
+__device__ __forceinline__ uint32_t rng_next(uint32_t &x)
+{
+    x ^= x << 13;
+    x ^= x >> 17;
+    x ^= x << 5;
+    return x;
+}
+
+__device__ __forceinline__ float rng_uniform(uint32_t &x)
+{
+    return (float)(rng_next(x) & 0x00FFFFFFu) * (1.0f / 16777216.0f);
+}
+
+// ---------------------------------------------------------------------------------------
+// Sample placement.  Every operation is explicitly rounded (no contraction) so the
+// positions, and therefore the floor() decisions of the filter, are bit-identical to the
+// CPU oracle.
+
+struct SamplerView {
+    int32_t image_w, image_h;
+    int32_t lattice_w, lattice_h;
+    float stride_x, stride_y;
+    int32_t offset_x, offset_y;
+    uint32_t step, seed;
+};
+
+__device__ __forceinline__ float clampf(float x, float lo, float hi)
+{
+    return x < lo ? lo : (x > hi ? hi : x);
+}
+
+__device__ __forceinline__ void sample_uv(const SamplerView &s, int32_t ix, int32_t iy, float &u,
+                                          float &v)
+{
+    const uint32_t index = (uint32_t)iy * (uint32_t)s.lattice_w + (uint32_t)ix;
+    uint32_t st = rng_seed(index, s.step, s.seed);
+    const float jx = __fsub_rn(rng_uniform(st), 0.5f);
+    const float jy = __fsub_rn(rng_uniform(st), 0.5f);
+    const float tx = __fadd_rn(__fadd_rn((float)ix, 0.5f), jx);
+    const float ty = __fadd_rn(__fadd_rn((float)iy, 0.5f), jy);
+    float px = __fadd_rn(__fmul_rn(tx, s.stride_x), (float)s.offset_x);
+    float py = __fadd_rn(__fmul_rn(ty, s.stride_y), (float)s.offset_y);
+    px = clampf(px, 0.5f, __fsub_rn((float)s.image_w, 0.5f));
+    py = clampf(py, 0.5f, __fsub_rn((float)s.image_h, 0.5f));
+    u = __fdiv_rn(px, (float)s.image_w);
+    v = __fdiv_rn(py, (float)s.image_h);
+}
+
+// Decode texel centres (train.cu:926-933).
+__device__ __forceinline__ void texel_uv(int32_t x, int32_t y, int32_t w, int32_t h, float &u,
+                                         float &v)
+{
+    u = __fdiv_rn(__fadd_rn((float)x, 0.5f), (float)w);
+    v = __fdiv_rn(__fadd_rn((float)y, 0.5f), (float)h);
+}
+
+// ---------------------------------------------------------------------------------------
+// Catmull-Rom footprint
+
+__device__ __forceinline__ int32_t wrap_coord(int32_t c, int32_t n)
+{
+    int32_t r = c % n;
+    return r < 0 ? r + n : r;
+}
+
+__device__ __forceinline__ void catmull_rom_weights(float f, float w[4])
+{
+    w[0] = f * (f * (f * -0.5f + 1.0f) - 0.5f);
+    w[1] = f * f * (f * 1.5f - 2.5f) + 1.0f;
+    w[2] = f * (f * (f * -1.5f + 2.0f) + 0.5f);
+    w[3] = f * f * (f * 0.5f - 0.5f);
+}
+
+// The 4x4 footprint of one sample in one grid: wrapped texel columns / rows and weights.
+struct Footprint {
+    int32_t xs[4];
+    int32_t ys[4];
+    float wx[4];
+    float wy[4];
+};
+
+// filter/catmull_rom.h:46-52: samplePos = uv * size; texPos1 = floor(samplePos - 0.5) + 0.5;
+// f = samplePos - texPos1 (explicitly rounded, so the fraction is bit-identical to the
+// reference's).  Returns the index of the [1, 1] tap.
+__device__ __forceinline__ int32_t cr_base(float uv, int32_t size, float &f)
+{
+    const float sp = __fmul_rn(uv, (float)size);
+    const float fl = floorf(__fsub_rn(sp, 0.5f));
+    f = __fsub_rn(sp, __fadd_rn(fl, 0.5f));
+    return (int32_t)fl;
+}
+
+__device__ __forceinline__ void footprint(float u, float v, int32_t w, int32_t h, Footprint &fp)
+{
+    float fx, fy;
+    const int32_t bx = cr_base(u, w, fx), by = cr_base(v, h, fy);
+    catmull_rom_weights(fx, fp.wx);
+    catmull_rom_weights(fy, fp.wy);
+    // bx - 1 >= -1 and bx + 2 <= w + 1 for uv in [0, 1]; one conditional wrap suffices when
+    // w >= 2, and wrap_coord handles everything else.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        fp.xs[i] = wrap_coord(bx - 1 + i, w);
+        fp.ys[i] = wrap_coord(by - 1 + i, h);
+    }
+}
+
+// Catmull-Rom gather of C channels (C = 8 or 12; channel-interleaved fp16 grid), fp32
+// accumulation: row sums first, then the weighted sum of rows (same order as the oracle).
+template <int C>
+__device__ __forceinline__ void gather_cr(const __half *__restrict__ grid, int32_t w,
+                                          const Footprint &fp, float out[C])
+{
+    static_assert(C % 4 == 0, "channel count must be a multiple of 4");
+#pragma unroll
+    for (int k = 0; k < C; ++k) out[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float row[C];
+#pragma unroll
+        for (int k = 0; k < C; ++k) row[k] = 0.f;
+        const __half *rp = grid + (size_t)fp.ys[j] * (size_t)w * C;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half *tp = rp + (size_t)fp.xs[i] * C;
+            if constexpr (C % 8 == 0) {
+#pragma unroll
+                for (int q = 0; q < C / 8; ++q) {
+                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(tp) + q);
+                    const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = unpack_half2(r[e]);
+                        row[q * 8 + 2 * e] = fmaf(fp.wx[i], f.x, row[q * 8 + 2 * e]);
+                        row[q * 8 + 2 * e + 1] = fmaf(fp.wx[i], f.y, row[q * 8 + 2 * e + 1]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < C / 4; ++q) {
+                    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(tp) + q);
+                    const float2 a = unpack_half2(raw.x), b = unpack_half2(raw.y);
+                    row[q * 4 + 0] = fmaf(fp.wx[i], a.x, row[q * 4 + 0]);
+                    row[q * 4 + 1] = fmaf(fp.wx[i], a.y, row[q * 4 + 1]);
+                    row[q * 4 + 2] = fmaf(fp.wx[i], b.x, row[q * 4 + 2]);
+                    row[q * 4 + 3] = fmaf(fp.wx[i], b.y, row[q * 4 + 3]);
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < C; ++k) out[k] = fmaf(fp.wy[j], row[k], out[k]);
+    }
+}
+
+// Runtime-channel Catmull-Rom gather (targets with any channel count <= 16).
+__device__ __forceinline__ void gather_cr_any(const __half *__restrict__ grid, int32_t w, int32_t c,
+                                              const Footprint &fp, float out[16])
+{
+#pragma unroll
+    for (int k = 0; k < 16; ++k) out[k] = 0.f;
+    for (int j = 0; j < 4; ++j) {
+        float row[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) row[k] = 0.f;
+        const __half *rp = grid + (size_t)fp.ys[j] * (size_t)w * c;
+        for (int i = 0; i < 4; ++i) {
+            const __half *tp = rp + (size_t)fp.xs[i] * c;
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                if (k < c) row[k] = fmaf(fp.wx[i], __half2float(tp[k]), row[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) out[k] = fmaf(fp.wy[j], row[k], out[k]);
+    }
+}
+
+// Positional features [sin 2pi u, cos 2pi u, sin 2pi v, cos 2pi v, sin 4pi u, ...].
+__device__ __forceinline__ void posenc(float u, float v, float out[8])
+{
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float m = (float)(2 << k);
+        sincospif(m * u, &out[4 * k + 0], &out[4 * k + 1]);
+        sincospif(m * v, &out[4 * k + 2], &out[4 * k + 3]);
+    }
+}
+
+// Launch counter (host-visible through nt_launch_count).
+void count_launch();
+
+}  // namespace nt

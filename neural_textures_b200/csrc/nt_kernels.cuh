@@ -1,0 +1,74 @@
+// nt_kernels.cuh -- launch descriptors shared by the C-ABI layer and the kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nt_common.cuh"
+
+namespace nt {
+
+constexpr int kTileSide = 16;        // lattice cells / texels per tile side
+constexpr int kTileSamples = 256;    // = kTileSide^2, one per thread
+constexpr int kThreads = 256;        // 8 warps
+
+struct NetView {
+    const __half *W[3];  // global, padded column-major
+    const __half *b[3];  // global, {64, 64, cout}
+    int32_t cout;
+};
+
+struct TrainLaunch {
+    const __half *grid[2];
+    float *ggrid[2];
+    int32_t gw[2], gh[2];
+    NetView net;
+    float *gW[3];
+    float *gb[3];
+    const __half *target;
+    float cw[16];
+    SamplerView sampler;
+    float inv_num_samples;
+    float *loss_accum;
+    int32_t finalize;
+    int32_t tiles_x, tiles_y;
+};
+
+struct DecodeLaunch {
+    const __half *grid[2];
+    int32_t gw[2], gh[2];
+    NetView net;
+    void *out;
+    int32_t out_f32;
+    const __half *target;  // optional, fp16 [h][w][cout]
+    float *mse_accum;      // optional
+    int32_t image_w, image_h;
+    int32_t tiles_x, tiles_y;
+};
+
+constexpr int kMaxAdamSegments = 8;
+
+struct AdamSegment {
+    __half *w;
+    float *g, *m, *v;
+    int64_t n;
+    float lr, beta1, beta2, eps, bc1, bc2;
+    int32_t first_block;
+};
+
+struct AdamLaunch {
+    AdamSegment seg[kMaxAdamSegments];
+    int32_t nseg;
+    int32_t total_blocks;
+};
+
+// Returns the number of CTAs used (0 on launch failure; cudaGetLastError holds the error).
+cudaError_t launch_train(const TrainLaunch &p, int channels, cudaStream_t stream);
+cudaError_t launch_decode(const DecodeLaunch &p, int channels, cudaStream_t stream);
+cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream);
+int sm_count();
+// Raise the dynamic shared-memory limit of `kernel` once per device.
+cudaError_t set_smem_limit(const void *kernel, size_t bytes);
+
+}  // namespace nt

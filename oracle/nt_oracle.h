@@ -1,0 +1,124 @@
+/*
+ * nt_oracle.h -- CPU restatement of the reference's neural-texture hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker for the CUDA path and the
+ * timed CPU baseline of bench.py; the product never links, loads or calls it.  Only
+ * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm use it.
+ *
+ * Every function cites the reference file:line (mavenkim2/neural_textures) whose behaviour
+ * it restates.  Where the build deliberately differs from the reference (Catmull-Rom on
+ * the latents instead of bilinear, fp32 accumulation, loss-gradient scaling), the
+ * function says so.  Compiled with -ffp-contract=off so that every float expression
+ * rounds exactly as written.
+ */
+#ifndef NT_ORACLE_H
+#define NT_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- fp16 ------------------------------------------------------------------------ */
+uint16_t nto_f2h(float f);  /* round to nearest even, like __float2half */
+float nto_h2f(uint16_t h);  /* exact, like __half2float */
+void nto_f2h_array(const float *in, uint16_t *out, int64_t n);
+void nto_h2f_array(const uint16_t *in, float *out, int64_t n);
+
+/* ---- per-sample RNG and sample placement (train.cu:37-58, :827-844) --------------- */
+uint32_t nto_rng_seed(uint32_t sample_index, uint32_t step, uint32_t seed);
+uint32_t nto_rng_next(uint32_t *state);
+float nto_rng_uniform(uint32_t *state);
+
+typedef struct nto_sampler {
+    int32_t image_w, image_h;
+    int32_t lattice_w, lattice_h;
+    float stride_x, stride_y;
+    int32_t offset_x, offset_y;
+    int32_t step;
+    uint32_t seed;
+} nto_sampler;
+void nto_sample_uv(const nto_sampler *s, int64_t index, float *u, float *v);
+void nto_sample_uv_array(const nto_sampler *s, float *uv /* [n][2] */);
+
+/* ---- Catmull-Rom latent sampling ---------------------------------------------------- */
+void nto_catmull_rom_weights(float f, float w[4]);
+int32_t nto_wrap(int32_t coord, int32_t size);
+/* Sample a channel-interleaved fp16 grid at uv (texel-centre convention, wrap).
+ * taps_out (optional): base texel (x, y) and the 4 + 4 weights. */
+void nto_sample_grid(const uint16_t *grid, int32_t w, int32_t h, int32_t c, float u, float v,
+                     float *out, int32_t base_out[2], float wx_out[4], float wy_out[4]);
+void nto_posenc(float u, float v, float out[8]);
+
+/* ---- network -------------------------------------------------------------------------- */
+typedef struct nto_model {
+    int32_t channels;       /* C per grid */
+    int32_t cout;           /* output channels, <= 16 */
+    int32_t gw[2], gh[2];
+    const uint16_t *grid[2];
+    const uint16_t *W[3];   /* padded column-major fp16: [64][32], [64][64], [16][64] */
+    const uint16_t *b[3];   /* fp16: 64, 64, cout */
+} nto_model;
+
+typedef struct nto_fwd {
+    float x[32];
+    float h1[64];
+    float h2[64];
+    float y[16];     /* fp16-rounded outputs */
+    int32_t base[2][2];
+    float wx[2][4], wy[2][4];
+} nto_fwd;
+
+void nto_forward_sample(const nto_model *m, float u, float v, nto_fwd *f);
+
+/* Decode all texel centres; out is fp16 (out_f32 = 0) or fp32 [h*w][cout].
+ * target (optional, fp16 [h][w][cout]) accumulates the SSE into *sse. */
+void nto_decode(const nto_model *m, int32_t w, int32_t h, void *out, int32_t out_f32,
+                const uint16_t *target, double *sse, int32_t threads);
+/* Decode only texel indices [first, first + count) (used for bounded CPU baselines). */
+void nto_decode_range(const nto_model *m, int32_t w, int32_t h, int64_t first, int64_t count,
+                      void *out, int32_t out_f32, int32_t threads);
+
+typedef struct nto_train_args {
+    const uint16_t *target;    /* fp16 [image_h][image_w][cout] */
+    const float *channel_weights; /* [cout] or NULL */
+    nto_sampler sampler;
+    int32_t finalize;          /* 1: no latent gradients */
+} nto_train_args;
+
+/* One training pass: accumulates network and latent gradients (fp32, already scaled by
+ * 1 / num_samples) and returns the weighted sum of squared errors. */
+double nto_train_pass(const nto_model *m, const nto_train_args *a, float *gW[3], float *gb[3],
+                      float *ggrid[2], int32_t threads);
+/* Same, restricted to samples [first, first + count) of the lattice (bounded baselines). */
+double nto_train_pass_range(const nto_model *m, const nto_train_args *a, int64_t first,
+                            int64_t count, float *gW[3], float *gb[3], float *ggrid[2],
+                            int32_t threads);
+
+/* ---- Adam (train.cu:521-564, :566-588) ---------------------------------------------- */
+void nto_adam_bias_correction(float beta1, float beta2, int32_t step, float *bc1, float *bc2);
+void nto_adam_f16(uint16_t *w, float *g, float *m, float *v, int64_t n, float lr, float beta1,
+                  float beta2, float eps, float bc1, float bc2);
+void nto_adam_f32(float *w, float *g, float *m, float *v, int64_t n, float lr, float beta1,
+                  float beta2, float eps, float bc1, float bc2);
+
+/* ---- synthetic target --------------------------------------------------------------- */
+void nto_target_params(uint32_t seed, int32_t channel, int32_t k, int32_t *fu, int32_t *fv,
+                       float *phase, float *amp);
+void nto_generate_target(uint16_t *out, int32_t w, int32_t h, int32_t channels, uint32_t seed,
+                         int32_t pbr_normals, int32_t threads);
+
+/* ---- tests/forward_pass_test.cu:45-150 known-answer test ---------------------------- */
+void nto_fwdtest_generate(uint16_t inputs[32 * 12], uint16_t w0[256], uint16_t w1[256],
+                          uint16_t b0[16], uint16_t b1[16]);
+void nto_fwdtest_reference(const uint16_t inputs[32 * 12], const uint16_t w0[256],
+                           const uint16_t w1[256], const uint16_t b0[16], const uint16_t b1[16],
+                           float out[32 * 16]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,297 @@
+"""ctypes binding of the CPU oracle (oracle/nt_oracle.c) and of the reference-extract library.
+
+TEST INFRASTRUCTURE ONLY.  Imported by tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference arm, as the checker; the product package never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libnt_oracle.so")
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libnt_ref.so")
+
+_lib = None
+_ref = None
+
+u16p = C.POINTER(C.c_uint16)
+f32p = C.POINTER(C.c_float)
+i32p = C.POINTER(C.c_int32)
+
+
+def build(force: bool = False) -> str:
+    """Compile the oracle with make (gcc, OpenMP)."""
+    if force or not os.path.exists(LIB_PATH) or _stale():
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def _stale() -> bool:
+    t = os.path.getmtime(LIB_PATH)
+    for f in ("nt_oracle.c", "nt_oracle_codec.c", "nt_oracle.h"):
+        if os.path.getmtime(os.path.join(HERE, f)) > t:
+            return True
+    return False
+
+
+def build_ref(reference_root: str | None = None) -> str | None:
+    """Build oracle/_ref from the reference sources when they are present (this container)."""
+    root = reference_root or os.environ.get("NT_REFERENCE_ROOT", "/root/reference")
+    if not os.path.exists(os.path.join(root, "train.cu")):
+        return None
+    subprocess.run([os.path.join(HERE, "build_ref.sh"), root], check=True,
+                   stdout=subprocess.DEVNULL)
+    return REF_LIB_PATH
+
+
+class Sampler(C.Structure):
+    _fields_ = [("image_w", C.c_int32), ("image_h", C.c_int32),
+                ("lattice_w", C.c_int32), ("lattice_h", C.c_int32),
+                ("stride_x", C.c_float), ("stride_y", C.c_float),
+                ("offset_x", C.c_int32), ("offset_y", C.c_int32),
+                ("step", C.c_int32), ("seed", C.c_uint32)]
+
+
+class Model(C.Structure):
+    _fields_ = [("channels", C.c_int32), ("cout", C.c_int32),
+                ("gw", C.c_int32 * 2), ("gh", C.c_int32 * 2),
+                ("grid", u16p * 2), ("W", u16p * 3), ("b", u16p * 3)]
+
+
+class TrainArgs(C.Structure):
+    _fields_ = [("target", u16p), ("channel_weights", f32p), ("sampler", Sampler),
+                ("finalize", C.c_int32)]
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(LIB_PATH)
+        L.nto_f2h.restype = C.c_uint16
+        L.nto_f2h.argtypes = [C.c_float]
+        L.nto_h2f.restype = C.c_float
+        L.nto_h2f.argtypes = [C.c_uint16]
+        L.nto_rng_seed.restype = C.c_uint32
+        L.nto_rng_seed.argtypes = [C.c_uint32, C.c_uint32, C.c_uint32]
+        L.nto_rng_next.restype = C.c_uint32
+        L.nto_rng_next.argtypes = [C.POINTER(C.c_uint32)]
+        L.nto_rng_uniform.restype = C.c_float
+        L.nto_rng_uniform.argtypes = [C.POINTER(C.c_uint32)]
+        L.nto_sample_uv_array.argtypes = [C.POINTER(Sampler), f32p]
+        L.nto_catmull_rom_weights.argtypes = [C.c_float, f32p]
+        L.nto_wrap.restype = C.c_int32
+        L.nto_wrap.argtypes = [C.c_int32, C.c_int32]
+        L.nto_sample_grid.argtypes = [u16p, C.c_int32, C.c_int32, C.c_int32, C.c_float,
+                                      C.c_float, f32p, i32p, f32p, f32p]
+        L.nto_posenc.argtypes = [C.c_float, C.c_float, f32p]
+        L.nto_decode.argtypes = [C.POINTER(Model), C.c_int32, C.c_int32, C.c_void_p, C.c_int32,
+                                 u16p, C.POINTER(C.c_double), C.c_int32]
+        L.nto_decode_range.argtypes = [C.POINTER(Model), C.c_int32, C.c_int32, C.c_int64,
+                                       C.c_int64, C.c_void_p, C.c_int32, C.c_int32]
+        L.nto_train_pass.restype = C.c_double
+        L.nto_train_pass.argtypes = [C.POINTER(Model), C.POINTER(TrainArgs), f32p * 3, f32p * 3,
+                                     f32p * 2, C.c_int32]
+        L.nto_train_pass_range.restype = C.c_double
+        L.nto_train_pass_range.argtypes = [C.POINTER(Model), C.POINTER(TrainArgs), C.c_int64,
+                                           C.c_int64, f32p * 3, f32p * 3, f32p * 2, C.c_int32]
+        L.nto_adam_bias_correction.argtypes = [C.c_float, C.c_float, C.c_int32, f32p, f32p]
+        for name, wt in (("nto_adam_f16", u16p), ("nto_adam_f32", f32p)):
+            getattr(L, name).argtypes = [wt, f32p, f32p, f32p, C.c_int64, C.c_float, C.c_float,
+                                         C.c_float, C.c_float, C.c_float, C.c_float]
+        L.nto_target_params.argtypes = [C.c_uint32, C.c_int32, C.c_int32, i32p, i32p, f32p, f32p]
+        L.nto_generate_target.argtypes = [u16p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32,
+                                          C.c_int32, C.c_int32]
+        L.nto_fwdtest_generate.argtypes = [u16p] * 5
+        L.nto_fwdtest_reference.argtypes = [u16p] * 5 + [f32p]
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The library compiled from the reference's own source lines, or None if unavailable."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_LIB_PATH):
+            if build_ref() is None:
+                return None
+        R = C.CDLL(REF_LIB_PATH)
+        R.ref_fwdtest.argtypes = [u16p] * 5 + [f32p]
+        R.ref_rng.argtypes = [C.c_uint32, C.c_int, C.POINTER(C.c_uint32), f32p]
+        R.ref_wrap.restype = C.c_int
+        R.ref_wrap.argtypes = [C.c_int, C.c_int]
+        R.ref_clamp.restype = C.c_float
+        R.ref_clamp.argtypes = [C.c_float, C.c_float, C.c_float]
+        R.ref_catmull_rom.argtypes = [C.c_float, C.c_float, f32p, f32p]
+        R.ref_adam_f16.argtypes = [u16p, f32p, f32p, C.c_float, C.c_float, C.c_float, C.c_float,
+                                   C.c_float, C.c_int]
+        R.ref_adam_f32.argtypes = [f32p, f32p, f32p, C.c_float, C.c_float, C.c_float, C.c_float,
+                                   C.c_float, C.c_int]
+        R.ref_decompress_bc6.argtypes = [f32p, f32p, C.c_int, C.c_float, f32p]
+        _ref = R
+    return _ref
+
+
+# ---------------------------------------------------------------------------------------
+# numpy helpers
+
+def _p(a: np.ndarray, t):
+    assert a.flags["C_CONTIGUOUS"], "arrays passed to the oracle must be C-contiguous"
+    return a.ctypes.data_as(t)
+
+
+def f2h(a) -> np.ndarray:
+    """fp32 -> fp16 bits (uint16) with the oracle's rounding (same as numpy's)."""
+    return np.asarray(a, dtype=np.float32).astype(np.float16).view(np.uint16)
+
+
+def h2f(a) -> np.ndarray:
+    return np.asarray(a, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+@dataclass
+class OracleModel:
+    """Host copy of a model: fp16 bit arrays (uint16)."""
+    channels: int
+    cout: int
+    grids: list          # 2 x uint16 [h][w][C]
+    W: list              # 3 x uint16 padded column-major
+    b: list              # 3 x uint16
+
+    def ctype(self) -> Model:
+        m = Model()
+        m.channels = self.channels
+        m.cout = self.cout
+        for g in range(2):
+            m.gh[g], m.gw[g] = self.grids[g].shape[0], self.grids[g].shape[1]
+            m.grid[g] = _p(self.grids[g], u16p)
+        for l in range(3):
+            m.W[l] = _p(self.W[l], u16p)
+            m.b[l] = _p(self.b[l], u16p)
+        return m
+
+
+def make_sampler(image_w, image_h, lattice_w, lattice_h, step=0, seed=0, stride_x=None,
+                 stride_y=None, offset_x=0, offset_y=0) -> Sampler:
+    s = Sampler()
+    s.image_w, s.image_h = image_w, image_h
+    s.lattice_w, s.lattice_h = lattice_w, lattice_h
+    s.stride_x = float(image_w) / lattice_w if stride_x is None else stride_x
+    s.stride_y = float(image_h) / lattice_h if stride_y is None else stride_y
+    s.offset_x, s.offset_y = offset_x, offset_y
+    s.step, s.seed = step, seed
+    return s
+
+
+def sample_uv(sampler: Sampler) -> np.ndarray:
+    n = sampler.lattice_w * sampler.lattice_h
+    out = np.zeros((n, 2), np.float32)
+    lib().nto_sample_uv_array(C.byref(sampler), _p(out, f32p))
+    return out
+
+
+def decode(model: OracleModel, w: int, h: int, out_f32: bool = False, threads: int = 1):
+    out = np.zeros((h * w, model.cout), np.float32 if out_f32 else np.uint16)
+    m = model.ctype()
+    sse = C.c_double(0.0)
+    lib().nto_decode(C.byref(m), w, h, out.ctypes.data, int(out_f32), None, C.byref(sse), threads)
+    return out
+
+
+def decode_range(model: OracleModel, w: int, h: int, first: int, count: int, threads: int = 1):
+    out = np.zeros((count, model.cout), np.uint16)
+    m = model.ctype()
+    lib().nto_decode_range(C.byref(m), w, h, first, count, out.ctypes.data, 0, threads)
+    return out
+
+
+def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel_weights=None,
+               finalize: bool = False, threads: int = 1, first: int = 0, count: int | None = None):
+    """One training pass.  Returns (sse, gW[3], gb[3], ggrid[2]) with fresh fp32 grads."""
+    m = model.ctype()
+    a = TrainArgs()
+    a.target = _p(target, u16p)
+    cw = None
+    if channel_weights is not None:
+        cw = np.ascontiguousarray(channel_weights, np.float32)
+        a.channel_weights = _p(cw, f32p)
+    a.sampler = sampler
+    a.finalize = int(finalize)
+    gW = [np.zeros(x.shape, np.float32) for x in model.W]
+    gb = [np.zeros(64, np.float32), np.zeros(64, np.float32), np.zeros(model.cout, np.float32)]
+    gg = [np.zeros(g.shape, np.float32) for g in model.grids]
+    pW = (f32p * 3)(*[_p(x, f32p) for x in gW])
+    pb = (f32p * 3)(*[_p(x, f32p) for x in gb])
+    pg = (f32p * 2)(*[_p(x, f32p) for x in gg])
+    if count is None:
+        sse = lib().nto_train_pass(C.byref(m), C.byref(a), pW, pb, pg, threads)
+    else:
+        sse = lib().nto_train_pass_range(C.byref(m), C.byref(a), first, count, pW, pb, pg,
+                                         threads)
+    return sse, gW, gb, gg
+
+
+def bias_correction(beta1, beta2, step):
+    b1, b2 = C.c_float(), C.c_float()
+    lib().nto_adam_bias_correction(beta1, beta2, step, C.byref(b1), C.byref(b2))
+    return b1.value, b2.value
+
+
+def adam_f16(w, g, m, v, lr, beta1, beta2, eps, step):
+    """In-place Adam on fp16 bits w (uint16) with fp32 g, m, v (train.cu:521-588)."""
+    bc1, bc2 = bias_correction(beta1, beta2, step)
+    lib().nto_adam_f16(_p(w, u16p), _p(g, f32p), _p(m, f32p), _p(v, f32p), w.size, lr, beta1,
+                       beta2, eps, bc1, bc2)
+
+
+def adam_f32(w, g, m, v, lr, beta1, beta2, eps, step):
+    bc1, bc2 = bias_correction(beta1, beta2, step)
+    lib().nto_adam_f32(_p(w, f32p), _p(g, f32p), _p(m, f32p), _p(v, f32p), w.size, lr, beta1,
+                       beta2, eps, bc1, bc2)
+
+
+def generate_target(w, h, channels, seed, pbr_normals=False, threads=1) -> np.ndarray:
+    out = np.zeros((h, w, channels), np.uint16)
+    lib().nto_generate_target(_p(out, u16p), w, h, channels, seed, int(pbr_normals), threads)
+    return out
+
+
+def fwdtest():
+    """(inputs, w0, w1, b0, b1, expected) of the forward-pass known-answer test."""
+    inputs = np.zeros(32 * 12, np.uint16)
+    w0 = np.zeros(256, np.uint16)
+    w1 = np.zeros(256, np.uint16)
+    b0 = np.zeros(16, np.uint16)
+    b1 = np.zeros(16, np.uint16)
+    out = np.zeros(32 * 16, np.float32)
+    L = lib()
+    L.nto_fwdtest_generate(*[_p(x, u16p) for x in (inputs, w0, w1, b0, b1)])
+    L.nto_fwdtest_reference(*[_p(x, u16p) for x in (inputs, w0, w1, b0, b1)], _p(out, f32p))
+    return inputs, w0, w1, b0, b1, out
+
+
+# ---------------------------------------------------------------------------------------
+# seeded model construction (shared by tests and bench)
+
+def he_normal_weights(rng: np.random.Generator, cout: int):
+    """fp16 padded column-major weights, He-normal N(0, 2 / fan_in) on the active block."""
+    shapes = [(64, 32, 32), (64, 64, 64), (16, 64, 64)]  # (padOut, padIn, fan_in)
+    Ws = []
+    for l, (po, pi, fan) in enumerate(shapes):
+        W = np.zeros((po, pi), np.float32)
+        active_out = 64 if l < 2 else cout
+        W[:active_out, :fan] = rng.standard_normal((active_out, fan)) * np.sqrt(2.0 / fan)
+        Ws.append(f2h(W).reshape(-1).copy())
+    return Ws
+
+
+def zero_input_rows(W0: np.ndarray, n_inputs: int) -> np.ndarray:
+    """Zero the padded input rows of layer 0 (inputs >= n_inputs)."""
+    W = W0.reshape(64, 32).copy()
+    W[:, n_inputs:] = 0
+    return W.reshape(-1)

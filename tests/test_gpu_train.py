@@ -1,0 +1,216 @@
+"""Training parity: the fused CUDA training pass and the fused Adam against the CPU oracle.
+
+- one training pass (train.cu:818-915 semantics): network and latent gradients, relative
+  L2 error <= 2e-2 per buffer; the sum of squared errors within 1e-3 relative;
+- Adam (train.cu:521-588): bit-exact, including the zero-gradient skip and the zeroing;
+- a multi-step run: the loss after N steps within 2% of the oracle's;
+- full BASELINE config-1 size: size-independent identities (every latent gradient sums to
+  sum_i db1[i] W1[i][k]; gradients finite; loss finite).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from tests.model_utils import make_texture, oracle_model, rel_l2, target_host
+
+pytestmark = pytest.mark.gpu
+
+GRAD_TOL = 2e-2
+
+
+def _host(t):
+    return t.detach().cpu().numpy().copy()
+
+
+def _train_pass_gpu(tex, finalize=False):
+    import torch
+    import neural_textures_b200 as nt
+    tex.loss_accum.zero_()
+    kind = nt.TrainingKernelType.FINALIZE if finalize else nt.TrainingKernelType.UNCONSTRAINED
+    nt.InvokeTraining(tex.params(), kind)
+    torch.cuda.synchronize()
+    return (tex.loss_accum.item(), [_host(g) for g in tex.gW], [_host(g) for g in tex.gb],
+            [_host(g) for g in tex.ggrads])
+
+
+def _oracle_pass(oracle, tex, finalize=False):
+    s = oracle.make_sampler(tex.image_w, tex.image_h, tex.lattice[0], tex.lattice[1], step=tex.step,
+                            seed=tex.seed)
+    return oracle.train_pass(oracle_model(oracle, tex), target_host(tex), s,
+                             channel_weights=np.array(tex.channel_weights, np.float32), finalize=finalize,
+                             threads=8)
+
+
+CASES = [
+    # image, grids, C, cout, lattice
+    ((64, 64), ((32, 32), (16, 16)), 8, 8, (32, 32)),
+    ((96, 80), ((48, 40), (24, 20)), 12, 12, (48, 40)),
+    ((70, 50), ((35, 25), (17, 12)), 8, 10, (37, 23)),
+    ((32, 32), ((32, 32), (8, 8)), 8, 8, (32, 32)),
+]
+
+
+@pytest.mark.parametrize("image,grids,C,cout,lattice", CASES)
+def test_training_pass_matches_oracle(cuda, oracle, image, grids, C, cout, lattice):
+    tex = make_texture(image, grids, C, cout, lattice=lattice, seed=7)
+    tex.step = 3
+    sse, gW, gb, gg = _train_pass_gpu(tex)
+    rsse, rW, rb, rg = _oracle_pass(oracle, tex)
+    assert abs(sse - rsse) <= 1e-3 * rsse, (sse, rsse)
+    for l in range(3):
+        assert rel_l2(gW[l], rW[l]) <= GRAD_TOL, f"dW{l}: {rel_l2(gW[l], rW[l])}"
+        assert rel_l2(gb[l], rb[l]) <= GRAD_TOL, f"db{l}: {rel_l2(gb[l], rb[l])}"
+    for g in range(2):
+        assert rel_l2(gg[g], rg[g]) <= GRAD_TOL, f"latent grid {g}: {rel_l2(gg[g], rg[g])}"
+    # padded weight rows / columns receive no gradient
+    assert np.all(gW[2].reshape(16, 64)[cout:] == 0)
+    assert np.all(gW[0].reshape(64, 32)[:, 2 * C + 8:] == 0)
+
+
+def test_finalize_leaves_latent_gradients_untouched(cuda, oracle):
+    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=1)
+    sse, gW, gb, gg = _train_pass_gpu(tex, finalize=True)
+    rsse, rW, rb, rg = _oracle_pass(oracle, tex, finalize=True)
+    assert all(np.all(g == 0) for g in gg)
+    assert rel_l2(gW[1], rW[1]) <= GRAD_TOL
+
+
+def test_channel_loss_weights(cuda, oracle):
+    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=4)
+    tex.channel_weights = [1.0, 0.5, 2.0, 0.0, 1.0, 3.0, 0.25, 1.0]
+    sse, gW, gb, gg = _train_pass_gpu(tex)
+    rsse, rW, rb, rg = _oracle_pass(oracle, tex)
+    assert abs(sse - rsse) <= 1e-3 * rsse
+    assert rel_l2(gW[2], rW[2]) <= GRAD_TOL
+    assert np.all(gb[2][3] == 0)
+
+
+def test_gradients_accumulate_across_passes(cuda):
+    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=9)
+    _, gW1, _, gg1 = _train_pass_gpu(tex)
+    _, gW2, _, gg2 = _train_pass_gpu(tex)  # same step: same samples, grads double
+    assert rel_l2(gW2[1], 2 * gW1[1]) < 1e-5
+    assert rel_l2(gg2[0], 2 * gg1[0]) < 1e-5
+
+
+def test_adam_bit_exact(cuda, oracle):
+    import torch
+    import neural_textures_b200 as nt
+    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=2)
+    rng = np.random.default_rng(5)
+    bufs = tex.gW + tex.gb + tex.ggrads
+    for t in bufs + tex.mW + tex.vW + tex.mb + tex.vb + tex.gm1 + tex.gm2:
+        vals = (rng.standard_normal(t.shape) * 10.0 ** rng.integers(-6, 0, t.shape)).astype(np.float32)
+        t.copy_(torch.from_numpy(vals))
+    for t in tex.vW + tex.vb + tex.gm2:
+        t.abs_()
+    for t in bufs:
+        t.view(-1)[::13] = 0.0
+    before = {k: [_host(x) for x in v] for k, v in dict(W=tex.W, b=tex.b, grids=tex.grids, gW=tex.gW, gb=tex.gb,
+                                                          gg=tex.ggrads, mW=tex.mW, vW=tex.vW, mb=tex.mb,
+                                                          vb=tex.vb, m1=tex.gm1, m2=tex.gm2).items()}
+    step = 17
+    nt.InvokeOptimizeAll(tex.params(step=step))
+    torch.cuda.synchronize()
+    b1, b2, lr, eps = tex.network_adam
+    for l in range(3):
+        w = before["W"][l].view(np.uint16).copy()
+        g, m, v = before["gW"][l].copy(), before["mW"][l].copy(), before["vW"][l].copy()
+        oracle.adam_f16(w, g, m, v, lr, b1, b2, eps, step)
+        np.testing.assert_array_equal(_host(tex.W[l]).view(np.uint16), w)
+        np.testing.assert_array_equal(_host(tex.mW[l]), m)
+        np.testing.assert_array_equal(_host(tex.vW[l]), v)
+        np.testing.assert_array_equal(_host(tex.gW[l]), g)
+        w = before["b"][l].view(np.uint16).copy()
+        g, m, v = before["gb"][l].copy(), before["mb"][l].copy(), before["vb"][l].copy()
+        oracle.adam_f16(w, g, m, v, lr, b1, b2, eps, step)
+        np.testing.assert_array_equal(_host(tex.b[l]).view(np.uint16), w)
+        np.testing.assert_array_equal(_host(tex.vb[l]), v)
+    b1, b2, lr, eps = tex.latent_adam
+    for gi in range(2):
+        w = before["grids"][gi].view(np.uint16).reshape(-1).copy()
+        g = before["gg"][gi].reshape(-1).copy()
+        m = before["m1"][gi].reshape(-1).copy()
+        v = before["m2"][gi].reshape(-1).copy()
+        oracle.adam_f16(w, g, m, v, lr, b1, b2, eps, step)
+        np.testing.assert_array_equal(_host(tex.grids[gi]).view(np.uint16).reshape(-1), w)
+        np.testing.assert_array_equal(_host(tex.gm1[gi]).reshape(-1), m)
+        np.testing.assert_array_equal(_host(tex.gm2[gi]).reshape(-1), v)
+        assert np.all(_host(tex.ggrads[gi]) == 0)
+
+
+def test_separate_optimizers_equal_fused(cuda):
+    import torch
+    import neural_textures_b200 as nt
+    a = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=6)
+    b = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=6)
+    for tex in (a, b):
+        nt.InvokeTraining(tex.params())
+    nt.InvokeOptimizeAll(a.params(step=1))
+    nt.InvokeOptimizeNetwork(b.params(step=1))
+    nt.InvokeOptimizeFeatures(b.params(step=1))
+    torch.cuda.synchronize()
+    for x, y in zip(a.W + a.grids + a.mW + a.gm1, b.W + b.grids + b.mW + b.gm1):
+        assert torch.equal(x, y)
+
+
+def test_multi_step_loss_matches_oracle(cuda, oracle):
+    """Run N steps on both sides with identical sampling; compare the mean loss of the last
+    10 steps (2% tolerance, the north-star criterion) and the loss decrease."""
+    import torch
+    n_steps = 300
+    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=12)
+    model_grids, model_W, model_b = tex.host_model()
+    tgt = target_host(tex)
+    losses_gpu = []
+    for step in range(n_steps):
+        tex.loss_accum.zero_()
+        tex.train_step(params=tex.params(step=step))
+        losses_gpu.append(tex.loss_accum.item())
+    # oracle: the same loop on host copies
+    grids = [g.copy() for g in model_grids]
+    W = [w.copy() for w in model_W]
+    b = [x.copy() for x in model_b]
+    zeros = lambda a: np.zeros(a.shape, np.float32)
+    mW, vW = [zeros(w) for w in W], [zeros(w) for w in W]
+    mb, vb = [zeros(x) for x in b], [zeros(x) for x in b]
+    mg, vg = [zeros(g) for g in grids], [zeros(g) for g in grids]
+    b1, b2, lr_n, eps = tex.network_adam
+    lr_l = tex.latent_adam[2]
+    losses_ref = []
+    for step in range(n_steps):
+        model = oracle.OracleModel(channels=8, cout=8, grids=grids, W=W, b=b)
+        s = oracle.make_sampler(64, 64, 32, 32, step=step)
+        sse, gW, gb, gg = oracle.train_pass(model, tgt, s, threads=8)
+        losses_ref.append(sse)
+        for l in range(3):
+            oracle.adam_f16(W[l], gW[l], mW[l], vW[l], lr_n, b1, b2, eps, step)
+            oracle.adam_f16(b[l], gb[l], mb[l], vb[l], lr_n, b1, b2, eps, step)
+        for gi in range(2):
+            flat = grids[gi].reshape(-1)
+            oracle.adam_f16(flat, gg[gi].reshape(-1), mg[gi].reshape(-1), vg[gi].reshape(-1), lr_l, b1, b2, eps,
+                            step)
+    lg, lr_ = np.mean(losses_gpu[-10:]), np.mean(losses_ref[-10:])
+    assert lg < 0.5 * losses_gpu[0], "training must reduce the loss"
+    assert abs(lg - lr_) <= 0.02 * lr_, (lg, lr_)
+
+
+def test_full_config1_step_identities(cuda):
+    """BASELINE config 1 at full size (1024^2 image, 512^2x8 + 256^2x8 latents, 262,144
+    samples): one pass; sum over texels of each latent gradient channel equals
+    sum_i db1[i] W1[i][k] (the Catmull-Rom weights of every sample sum to one)."""
+    import torch
+    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=21)
+    sse, gW, gb, gg = _train_pass_gpu(tex)
+    assert np.isfinite(sse) and sse > 0
+    for a in gW + gb + gg:
+        assert np.isfinite(a).all()
+    W1 = _host(tex.W[0]).astype(np.float64).reshape(64, 32)
+    db1 = gb[0].astype(np.float64)
+    for g in range(2):
+        flat = gg[g].astype(np.float64).reshape(-1, 8)
+        lhs = flat.sum(0)
+        rhs = db1 @ W1[:, g * 8:(g + 1) * 8]
+        tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
+        assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)

@@ -63,55 +63,67 @@ def ncu_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU, polled through NVML
+    every 10 ms in a background thread while the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.lines = []
+    def __init__(self, torch_device):
+        self.dev = torch_device
+        self.samples = []
+        self.reasons = set()
+        self.smax = None
+        self._stop = threading.Event()
+        self.err = None
+
+    def _handle(self, nv):
+        import torch
+        try:
+            props = torch.cuda.get_device_properties(self.dev)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.dev.index or 0)
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except Exception:
-            self.proc = None
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = self._handle(nv)
+            self.smax = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.get_reasons = get
+        except Exception as e:  # no NVML: report it, keep benchmarking
+            self.err = f"nvml unavailable: {e}"
+            return
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                bits = int(self.get_reasons(self.h))
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception as e:
+                self.err = str(e)
+                break
+            time.sleep(0.01)
 
     def stop(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.err and not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err], "samples": 0}
+        self._stop.set()
+        self.thread.join(timeout=2)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_min_mhz": min(self.samples) if self.samples else None,
+                "sm_max_mhz": self.smax, "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def cpu_train_baseline(O, seconds=12.0):
@@ -186,11 +198,12 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decode-iters", type=int, default=50)
+    ap.add_argument("--prewarm", type=float, default=0.5, help="seconds of untimed steps before warm-up")
+    ap.add_argument("--decode-iters", type=int, default=200)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -231,13 +244,19 @@ def main():
         if ev:
             ev[2].record(stream)
 
+    # untimed pre-warm: ~0.5 s of steps so the SM clock leaves idle, then W warm-up steps
+    t_end = time.perf_counter() + args.prewarm
+    while time.perf_counter() < t_end:
+        for _ in range(20):
+            step_once(0)
+        torch.cuda.synchronize(dev)
     for w in range(args.warmup):
         _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
         step_once(w + 1)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(dev)
     clocks.start()
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     launches0 = nt.launch_count()
@@ -249,7 +268,6 @@ def main():
     launches = nt.launch_count() - launches0 - args.steps  # exclude the L2 flushes
     if world > 1:
         dist.barrier()
-    clk = clocks.stop()
     t_train = sum(e[0].elapsed_time(e[1]) for e in events) / args.steps   # ms
     t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / args.steps
     t_step = t_train + t_adam
@@ -298,6 +316,7 @@ def main():
         dev_ev[k][1].record(stream)
     torch.cuda.synchronize(dev)
     t_dec = sum(a.elapsed_time(b) for a, b in dev_ev) / args.decode_iters
+    clk = clocks.stop()  # sampled across the timed training, e2e and decode regions
     texels = CFG0["image"][0] * CFG0["image"][1]
 
     if world > 1:

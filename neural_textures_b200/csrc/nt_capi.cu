@@ -97,6 +97,7 @@ static nt_status validate_network(const NtKernelParams *p)
         const NtFeature &ft = p->features[f];
         NT_REQUIRE(ft.grid && aligned16(ft.grid), "features[%d].grid must be a non-null 16-byte aligned pointer", f);
         NT_REQUIRE(ft.width >= 1 && ft.height >= 1, "features[%d] has empty size %dx%d", f, ft.width, ft.height);
+        NT_REQUIRE(ft.width <= 32767 && ft.height <= 32767, "features[%d] is wider than 32767 texels", f);
         NT_REQUIRE((int64_t)ft.width * ft.height * p->latent_channels < (int64_t)1 << 31,
                    "features[%d] is too large", f);
     }

@@ -117,8 +117,10 @@ __device__ __forceinline__ void catmull_rom_weights(float f, float w[4])
     w[3] = f * f * (f * 0.5f - 0.5f);
 }
 
-// The 4x4 footprint of one sample in one grid: wrapped texel columns / rows and weights.
+// The 4x4 footprint of one sample in one grid: base tap (the [1, 1] texel, unwrapped),
+// wrapped texel columns / rows and weights.
 struct Footprint {
+    int32_t bx, by;
     int32_t xs[4];
     int32_t ys[4];
     float wx[4];
@@ -140,6 +142,8 @@ __device__ __forceinline__ void footprint(float u, float v, int32_t w, int32_t h
 {
     float fx, fy;
     const int32_t bx = cr_base(u, w, fx), by = cr_base(v, h, fy);
+    fp.bx = bx;
+    fp.by = by;
     catmull_rom_weights(fx, fp.wx);
     catmull_rom_weights(fy, fp.wy);
     // bx - 1 >= -1 and bx + 2 <= w + 1 for uv in [0, 1]; one conditional wrap suffices when
@@ -217,6 +221,25 @@ __device__ __forceinline__ void gather_cr_any(const __half *__restrict__ grid, i
         }
 #pragma unroll
         for (int k = 0; k < 16; ++k) out[k] = fmaf(fp.wy[j], row[k], out[k]);
+    }
+}
+
+// Target gather with vector loads for the common channel counts (4, 8, 12, 16).
+__device__ __forceinline__ void gather_target(const __half *__restrict__ t, int32_t w, int32_t c,
+                                              const Footprint &fp, float out[16])
+{
+#pragma unroll
+    for (int k = 0; k < 16; ++k) out[k] = 0.f;
+    if (c == 8) {
+        gather_cr<8>(t, w, fp, out);
+    } else if (c == 12) {
+        gather_cr<12>(t, w, fp, out);
+    } else if (c == 16) {
+        gather_cr<16>(t, w, fp, out);
+    } else if (c == 4) {
+        gather_cr<4>(t, w, fp, out);
+    } else {
+        gather_cr_any(t, w, c, fp, out);
     }
 }
 

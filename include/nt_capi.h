@@ -191,6 +191,42 @@ NT_API nt_status nt_forward_pass_12x16x16(const void *inputs, const void *w0, co
                                    const void *b0, const void *b1, void *outputs,
                                    nt_stream_t stream);
 
+/* ---- BC6H latent block codec (train.cu:20-34, :161-202 hold the reference's BC6 pieces) -- */
+
+/* A strided fp16 surface: element (channel c, row y, texel x) lives at
+ * data[c * channel_stride + y * row_stride + x * texel_stride] (strides in elements), so
+ * planar [C][H][W] latents and channel-interleaved [H][W][C] grids are both addressable.
+ * Channels are coded in triples (a missing third channel holds the bias). */
+typedef struct NtBc6hSurface {
+    void *data;
+    int32_t width;
+    int32_t height;
+    int32_t channels;
+    int64_t channel_stride;
+    int64_t row_stride;
+    int64_t texel_stride;
+} NtBc6hSurface;
+
+/* Bytes of the block array of a surface: ceil(channels/3) x ceil(h/4) x ceil(w/4) x 16,
+ * stored [triple][block row][block column]. */
+NT_API size_t nt_bc6h_blocks_bytes(int32_t width, int32_t height, int32_t channels);
+/* Encode half(value + bias) as BC6H UF16 blocks (bias 4 suits latents in [-4, 4]);
+ * partial edge blocks replicate the last texel. */
+NT_API nt_status nt_bc6h_encode(const NtBc6hSurface *src, void *blocks, float bias,
+                                nt_stream_t stream);
+/* Decode to half(decoded - bias) into the surface (only texels inside it are written). */
+NT_API nt_status nt_bc6h_decode(const void *blocks, const NtBc6hSurface *dst, float bias,
+                                nt_stream_t stream);
+/* Raw decode of num_blocks blocks to 48 fp16 bit patterns each (16 texels x 3 channels),
+ * interpreted as SF16 (is_signed = 1) or UF16. */
+NT_API nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int32_t is_signed,
+                                    void *texels, nt_stream_t stream);
+/* Decode through the GPU texture unit instead: uploads the blocks of one blocks_w x
+ * blocks_h surface into a BC6H CUDA array, fetches every texel with point sampling and
+ * writes [blocks_h*4][blocks_w*4][4] floats.  Synchronous; allocates and frees the array. */
+NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h,
+                                         int32_t is_signed, float *rgba);
+
 /* ---- seeded set-up helpers (not in the reference: it loads EXR files, main.cpp:436-556) -- */
 
 /* Synthetic target: per channel the sigmoid of a sum of 16 seeded sinusoids with

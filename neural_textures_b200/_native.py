@@ -72,8 +72,14 @@ class NtKernelParams(C.Structure):
     ]
 
 
+class NtBc6hSurface(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32), ("channels", C.c_int32),
+                ("channel_stride", C.c_int64), ("row_stride", C.c_int64), ("texel_stride", C.c_int64)]
+
+
 # Every symbol include/nt_capi.h declares: name -> (restype, argtypes)
 _P = C.POINTER(NtKernelParams)
+_S = C.POINTER(NtBc6hSurface)
 SIGNATURES = {
     "nt_version": (C.c_int32, []),
     "nt_get_last_error_string": (C.c_char_p, []),
@@ -91,6 +97,11 @@ SIGNATURES = {
     "nt_generate_target": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32,
                                      C.c_int32, C.c_void_p]),
     "nt_init_latents": (C.c_int, [C.c_void_p, C.c_int64, C.c_uint32, C.c_void_p]),
+    "nt_bc6h_blocks_bytes": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32]),
+    "nt_bc6h_encode": (C.c_int, [_S, C.c_void_p, C.c_float, C.c_void_p]),
+    "nt_bc6h_decode": (C.c_int, [C.c_void_p, _S, C.c_float, C.c_void_p]),
+    "nt_bc6h_decode_raw": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
+    "nt_bc6h_decode_hardware": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 

@@ -87,6 +87,48 @@ def launch_count() -> int:
 
 
 # ---------------------------------------------------------------------------------------
+# BC6H latent block codec
+
+def bc6h_surface(t, layout: str = "planar") -> N.NtBc6hSurface:
+    """Describe an fp16 device tensor as a codec surface: `planar` [C][H][W] or
+    `interleaved` [H][W][C] (the latent-grid layout)."""
+    s = N.NtBc6hSurface()
+    s.data = t.data_ptr()
+    if layout == "planar":
+        C_, H, W = t.shape
+        s.channel_stride, s.row_stride, s.texel_stride = t.stride()
+    elif layout == "interleaved":
+        H, W, C_ = t.shape
+        s.row_stride, s.texel_stride, s.channel_stride = t.stride()
+    else:
+        raise ValueError(f"unknown layout {layout!r}")
+    s.width, s.height, s.channels = W, H, C_
+    return s
+
+
+def bc6h_blocks_bytes(width: int, height: int, channels: int) -> int:
+    return int(load().nt_bc6h_blocks_bytes(width, height, channels))
+
+
+def bc6h_encode(t, layout: str = "planar", bias: float = 4.0, blocks=None, stream=None):
+    """Encode an fp16 surface to BC6H UF16 blocks of (value + bias); returns uint8 blocks."""
+    import torch
+    s = bc6h_surface(t, layout)
+    nbytes = bc6h_blocks_bytes(s.width, s.height, s.channels)
+    if blocks is None:
+        blocks = torch.empty(nbytes, dtype=torch.uint8, device=t.device)
+    check(load().nt_bc6h_encode(C.byref(s), blocks.data_ptr(), bias, _stream(stream)))
+    return blocks
+
+
+def bc6h_decode(blocks, out, layout: str = "planar", bias: float = 4.0, stream=None):
+    """Decode blocks into the fp16 tensor `out` (its shape selects the surface)."""
+    s = bc6h_surface(out, layout)
+    check(load().nt_bc6h_decode(blocks.data_ptr(), C.byref(s), bias, _stream(stream)))
+    return out
+
+
+# ---------------------------------------------------------------------------------------
 # parameter initialisation (host, seeded)
 
 PAD_IN = (32, 64, 64)

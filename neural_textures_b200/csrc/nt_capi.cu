@@ -48,6 +48,9 @@ cudaError_t set_smem_limit(const void *kernel, size_t bytes)
     return e;
 }
 
+cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, bool encode, cudaStream_t st);
+cudaError_t launch_bc6h_raw(const void *blocks, int64_t n, int is_signed, void *out, cudaStream_t st);
+cudaError_t hardware_decode(const void *blocks, int bw, int bh, int is_signed, float *rgba);
 cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t seed, int32_t pbr, cudaStream_t st);
 cudaError_t launch_init_latents(void *grid, int64_t count, uint32_t seed, cudaStream_t st);
 cudaError_t launch_flush(void *scratch, size_t bytes, cudaStream_t st);
@@ -359,6 +362,54 @@ nt_status nt_train_step(const NtKernelParams *p, nt_stream_t stream)
     nt_status st = nt_invoke_training(p, NT_TRAIN_UNCONSTRAINED, stream);
     if (st != NT_OK) return st;
     return nt_invoke_optimize_all(p, stream);
+}
+
+size_t nt_bc6h_blocks_bytes(int32_t width, int32_t height, int32_t channels)
+{
+    if (width < 1 || height < 1 || channels < 1) return 0;
+    return (size_t)((channels + 2) / 3) * (size_t)((height + 3) / 4) * (size_t)((width + 3) / 4) * 16u;
+}
+
+static nt_status validate_surface(const NtBc6hSurface *s, const void *blocks)
+{
+    NT_REQUIRE(s, "surface is null");
+    NT_REQUIRE(s->data && (reinterpret_cast<uintptr_t>(s->data) & 1u) == 0, "surface data must be a 2-byte aligned pointer");
+    NT_REQUIRE(blocks && aligned16(blocks), "blocks must be a 16-byte aligned device pointer");
+    NT_REQUIRE(s->width >= 1 && s->height >= 1 && s->channels >= 1, "surface size must be positive");
+    NT_REQUIRE(s->channel_stride >= 0 && s->row_stride >= 0 && s->texel_stride >= 0, "strides must be non-negative");
+    return NT_OK;
+}
+
+nt_status nt_bc6h_encode(const NtBc6hSurface *src, void *blocks, float bias, nt_stream_t stream)
+{
+    nt_status st = validate_surface(src, blocks);
+    if (st != NT_OK) return st;
+    return check_cuda(launch_bc6h(src, blocks, bias, true, (cudaStream_t)stream), "BC6H encode");
+}
+
+nt_status nt_bc6h_decode(const void *blocks, const NtBc6hSurface *dst, float bias, nt_stream_t stream)
+{
+    nt_status st = validate_surface(dst, blocks);
+    if (st != NT_OK) return st;
+    return check_cuda(launch_bc6h(dst, blocks, bias, false, (cudaStream_t)stream), "BC6H decode");
+}
+
+nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int32_t is_signed, void *texels,
+                             nt_stream_t stream)
+{
+    NT_REQUIRE(blocks && aligned16(blocks), "blocks must be a 16-byte aligned device pointer");
+    NT_REQUIRE(texels, "texels is null");
+    NT_REQUIRE(num_blocks >= 0, "num_blocks must be non-negative");
+    if (num_blocks == 0) return NT_OK;
+    return check_cuda(launch_bc6h_raw(blocks, num_blocks, is_signed, texels, (cudaStream_t)stream), "BC6H raw decode");
+}
+
+nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h, int32_t is_signed,
+                                  float *rgba)
+{
+    NT_REQUIRE(blocks && rgba, "blocks and rgba are required");
+    NT_REQUIRE(blocks_w >= 1 && blocks_h >= 1, "block counts must be positive");
+    return check_cuda(hardware_decode(blocks, blocks_w, blocks_h, is_signed, rgba), "BC6H hardware decode");
 }
 
 nt_status nt_generate_target(void *target, int32_t width, int32_t height, int32_t channels, uint32_t seed,

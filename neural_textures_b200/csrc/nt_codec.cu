@@ -1,0 +1,587 @@
+// nt_codec.cu -- BC6H latent block codec: encode (UF16 of value + bias) and decode.
+//
+// The reference (mavenkim2/neural_textures) has a differentiable float decode of BC6-like
+// blocks (train.cu:161-202) over the format's 2-region partition table (train.cu:20-34) and
+// no integer bitstream.  This file implements the published BC6H bitstream (all 14 modes on
+// decode; modes 1-10 with the best-scoring partition and modes 11-14 on encode) with a
+// deterministic integer encoder; the CPU oracle (oracle/nt_oracle_codec.c) restates the same
+// algorithm and the two must agree bit for bit.  Latent planes are grouped in channel
+// triples (the reference's latent unit is a float3 feature, train.h:39, :59); signed
+// latents are stored as UF16 of (value + bias) because BC6H interpolates half-float bit
+// patterns, which is meaningful only within one sign.
+//
+// One thread per 4x4 block: a warp covers 32 consecutive blocks of a block row, so every
+// texel row of a plane is read (encode) or written (decode) as 256 contiguous bytes, and
+// the 16-byte blocks move as one vector access each.
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "neural_textures/bc6h_format.h"
+#include "nt_capi.h"
+#include "nt_kernels.cuh"
+
+namespace nt {
+
+__device__ const NtBc6hMode c_modes[NT_BC6H_NUM_MODES] = NT_BC6H_MODES_INIT;
+__device__ const uint8_t c_layout[NT_BC6H_NUM_MODES][82] = NT_BC6H_LAYOUT_INIT;
+__device__ const uint16_t c_parts[32] = NT_BC6H_PARTITIONS_INIT;
+__device__ const uint8_t c_anchors[32] = NT_BC6H_ANCHORS_INIT;
+__device__ const uint8_t c_w3[8] = NT_BC6H_WEIGHTS3_INIT;
+__device__ const uint8_t c_w4[16] = NT_BC6H_WEIGHTS4_INIT;
+
+struct Block128 {
+    uint32_t w[4];
+    __device__ __forceinline__ int bit(int k) const { return (w[k >> 5] >> (k & 31)) & 1; }
+    __device__ __forceinline__ int bits(int k, int n) const
+    {
+        // n <= 4 and the field never straddles more than two words
+        const int wi = k >> 5, sh = k & 31;
+        uint64_t v = w[wi];
+        if (wi < 3) v |= (uint64_t)w[wi + 1] << 32;
+        return (int)((v >> sh) & ((1u << n) - 1u));
+    }
+    __device__ __forceinline__ void set(int k, int v)
+    {
+        if (v) w[k >> 5] |= 1u << (k & 31);
+    }
+};
+
+__device__ __forceinline__ int sign_extend(int v, int bits)
+{
+    const unsigned m = 1u << (bits - 1);
+    const unsigned u = (unsigned)v & ((1u << bits) - 1u);
+    return (int)((u ^ m) - m);
+}
+
+__device__ __forceinline__ int unquantize(int comp, int bits, bool is_signed)
+{
+    if (!is_signed) {
+        if (bits >= 15) return comp;
+        if (comp == 0) return 0;
+        if (comp == (1 << bits) - 1) return 0xFFFF;
+        return ((comp << 16) + 0x8000) >> bits;
+    }
+    if (bits >= 16) return comp;
+    const bool s = comp < 0;
+    if (s) comp = -comp;
+    int unq;
+    if (comp == 0)
+        unq = 0;
+    else if (comp >= (1 << (bits - 1)) - 1)
+        unq = 0x7FFF;
+    else
+        unq = ((comp << 15) + 0x4000) >> (bits - 1);
+    return s ? -unq : unq;
+}
+
+__device__ __forceinline__ uint16_t finish_unquantize(int comp, bool is_signed)
+{
+    if (!is_signed) return (uint16_t)((comp * 31) >> 6);
+    comp = comp < 0 ? -(((-comp) * 31) >> 5) : (comp * 31) >> 5;
+    uint16_t s = 0;
+    if (comp < 0) {
+        s = 0x8000;
+        comp = -comp;
+    }
+    return (uint16_t)(s | comp);
+}
+
+__device__ __forceinline__ int mode_index(const Block128 &b)
+{
+    const int m2 = b.w[0] & 3;
+    if (m2 < 2) return m2;
+    const int m5 = b.w[0] & 31;
+#pragma unroll 1
+    for (int i = 2; i < NT_BC6H_NUM_MODES; ++i)
+        if (c_modes[i].mode_value == m5) return i;
+    return -1;
+}
+
+__device__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48])
+{
+    const int mi = mode_index(b);
+    if (mi < 0) {
+#pragma unroll
+        for (int i = 0; i < 48; ++i) out[i] = 0;
+        return;
+    }
+    const NtBc6hMode M = c_modes[mi];
+    int e[4][3];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) e[i][0] = e[i][1] = e[i][2] = 0;
+    int d = 0;
+#pragma unroll 1
+    for (int k = 0; k < M.header_bits; ++k) {
+        const int ent = c_layout[mi][k];
+        const int f = ent >> 4, bit = ent & 15;
+        const int v = b.bit(k);
+        if (f < 12) {
+            const int ei = f / 3, ci = f % 3;
+            // registers only: branch over the 12 fields keeps e[][] out of local memory
+#pragma unroll
+            for (int q = 0; q < 12; ++q)
+                if (q == f) e[q / 3][q % 3] |= v << bit;
+            (void)ei;
+            (void)ci;
+        } else if (f == NT_BC6H_FIELD_D) {
+            d |= v << bit;
+        }
+    }
+    const int ne = 2 * M.regions, epb = M.endpoint_bits;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        if (is_signed) e[0][c] = sign_extend(e[0][c], epb);
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+            if (i >= ne) break;
+            if (is_signed || M.transformed) e[i][c] = sign_extend(e[i][c], M.transformed ? M.delta_bits[c] : epb);
+            if (M.transformed) {
+                e[i][c] = (e[0][c] + e[i][c]) & ((1 << epb) - 1);
+                if (is_signed) e[i][c] = sign_extend(e[i][c], epb);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (i < ne) e[i][c] = unquantize(e[i][c], epb, is_signed);
+    }
+    const int ib = M.regions == 2 ? 3 : 4;
+    const int anchor1 = M.regions == 2 ? c_anchors[d] : -1;
+    const uint16_t pmask = M.regions == 2 ? c_parts[d] : 0;
+    int pos = M.header_bits;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        const int nb = ib - ((px == 0 || px == anchor1) ? 1 : 0);
+        const int idx = b.bits(pos, nb);
+        pos += nb;
+        const int r = (pmask >> px) & 1;
+        const int w = ib == 3 ? c_w3[idx & 7] : c_w4[idx & 15];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int a = r ? e[2][c] : e[0][c], bb = r ? e[3][c] : e[1][c];
+            out[px * 3 + c] = finish_unquantize((a * (64 - w) + bb * w + 32) >> 6, is_signed);
+        }
+    }
+}
+
+// ---- encoder ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int to_domain(uint16_t h)
+{
+    int m = (h & 0x8000) ? 0 : h;
+    if (m > 0x7C00) m = 0;
+    if (m > 0x7BFF) m = 0x7BFF;
+    return (m * 64 + 30) / 31;
+}
+
+__device__ __forceinline__ int quantize_unsigned(int x, int bits)
+{
+    if (bits >= 16) return x;
+    const int qmax = (1 << bits) - 1;
+    int q = (int)(((int64_t)x << bits) >> 16);
+    if (q > qmax) q = qmax;
+    if (q < qmax) {
+        const int d0 = abs(unquantize(q, bits, false) - x);
+        const int d1 = abs(unquantize(q + 1, bits, false) - x);
+        if (d1 < d0) q = q + 1;
+    }
+    return q;
+}
+
+__device__ void fit_endpoints(const int x[16][3], uint32_t mask, int want, int A[3], int B[3])
+{
+    int lo[3] = {65535, 65535, 65535}, hi[3] = {0, 0, 0};
+    int64_t sum[3] = {0, 0, 0};
+    int n = 0;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        if ((int)((mask >> px) & 1) != want) continue;
+        ++n;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            lo[c] = min(lo[c], x[px][c]);
+            hi[c] = max(hi[c], x[px][c]);
+            sum[c] += x[px][c];
+        }
+    }
+    if (n == 0) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) A[c] = B[c] = 0;
+        return;
+    }
+    int k = 0;
+    if (hi[1] - lo[1] > hi[k] - lo[k]) k = 1;
+    if (hi[2] - lo[2] > hi[k] - lo[k]) k = 2;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        int64_t cov = 0;
+        if (c != k) {
+            int64_t sxy = 0;
+#pragma unroll
+            for (int px = 0; px < 16; ++px)
+                if ((int)((mask >> px) & 1) == want) sxy += (int64_t)x[px][c] * x[px][k];
+            const int64_t sk = k == 0 ? sum[0] : (k == 1 ? sum[1] : sum[2]);
+            cov = (int64_t)n * sxy - sum[c] * sk;
+        }
+        if (cov < 0) {
+            A[c] = hi[c];
+            B[c] = lo[c];
+        } else {
+            A[c] = lo[c];
+            B[c] = hi[c];
+        }
+    }
+}
+
+// Evaluate (and pack) one candidate; returns the squared error or -1 when the mode cannot
+// hold the endpoints.
+__device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2][3], const int B[2][3],
+                            Block128 &out)
+{
+    const NtBc6hMode M = c_modes[mi];
+    const int regions = M.regions, epb = M.endpoint_bits, ib = regions == 2 ? 3 : 4;
+    const int ni = 1 << ib;
+    const uint32_t mask = regions == 2 ? c_parts[part] : 0u;
+    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
+    int q[2][2][3], u[2][2][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            q[r][0][c] = r < regions ? quantize_unsigned(A[r][c], epb) : 0;
+            q[r][1][c] = r < regions ? quantize_unsigned(B[r][c], epb) : 0;
+        }
+    int idx[16];
+    int64_t err = 0;
+#pragma unroll 1
+    for (int pass = 0; pass < 2; ++pass) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int c = 0; c < 3; ++c) u[r][i][c] = unquantize(q[r][i][c], epb, false);
+        err = 0;
+#pragma unroll
+        for (int px = 0; px < 16; ++px) {
+            const int r = (mask >> px) & 1;
+            int64_t best = INT64_MAX;
+            int bi = 0;
+#pragma unroll 1
+            for (int kk = 0; kk < ni; ++kk) {
+                const int w = ib == 3 ? c_w3[kk] : c_w4[kk];
+                int64_t dsum = 0;
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    const int a = r ? u[1][0][c] : u[0][0][c], bb = r ? u[1][1][c] : u[0][1][c];
+                    const int v = (a * (64 - w) + bb * w + 32) >> 6;
+                    const int64_t dd = (int64_t)(x[px][c] - v);
+                    dsum += dd * dd;
+                }
+                if (dsum < best) {
+                    best = dsum;
+                    bi = kk;
+                }
+            }
+            idx[px] = bi;
+            err += best;
+        }
+        if (pass == 1) break;
+        bool swapped = false;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            if (r >= regions) break;
+            const int ap = r == 0 ? 0 : anchor1;
+            int aidx = 0;
+#pragma unroll
+            for (int px = 0; px < 16; ++px)
+                if (px == ap) aidx = idx[px];
+            if (aidx >= ni / 2) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    const int t = q[r][0][c];
+                    q[r][0][c] = q[r][1][c];
+                    q[r][1][c] = t;
+                }
+                swapped = true;
+            }
+        }
+        if (!swapped) break;
+    }
+    int e[4][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) e[2 * r + i][c] = q[r][i][c];
+    if (M.transformed) {
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+            if (i >= 2 * regions) break;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int dlt = e[i][c] - e[0][c];
+                const int db = M.delta_bits[c];
+                if (dlt < -(1 << (db - 1)) || dlt > (1 << (db - 1)) - 1) return -1;
+                e[i][c] = dlt;
+            }
+        }
+    }
+    out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
+#pragma unroll 1
+    for (int k = 0; k < M.header_bits; ++k) {
+        const int ent = c_layout[mi][k];
+        const int f = ent >> 4, bit = ent & 15;
+        int v = 0;
+        if (f < 12) {
+#pragma unroll
+            for (int qf = 0; qf < 12; ++qf)
+                if (qf == f) v = ((unsigned)e[qf / 3][qf % 3] >> bit) & 1;
+        } else if (f == NT_BC6H_FIELD_D) {
+            v = (part >> bit) & 1;
+        } else {
+            v = (M.mode_value >> bit) & 1;
+        }
+        out.set(k, v);
+    }
+    int pos = M.header_bits;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        const int nb = ib - ((px == 0 || (regions == 2 && px == anchor1)) ? 1 : 0);
+        for (int bb = 0; bb < nb; ++bb) out.set(pos + bb, (idx[px] >> bb) & 1);
+        pos += nb;
+    }
+    return err;
+}
+
+__device__ void encode_block(const uint16_t tex[48], Block128 &out)
+{
+    int x[16][3];
+#pragma unroll
+    for (int px = 0; px < 16; ++px)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) x[px][c] = to_domain(tex[px * 3 + c]);
+    int64_t best = INT64_MAX;
+    Block128 cand;
+    int A[2][3], B[2][3];
+    fit_endpoints(x, 0u, 0, A[0], B[0]);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) A[1][c] = B[1][c] = 0;
+#pragma unroll 1
+    for (int mi = 10; mi < 14; ++mi) {
+        const int64_t e = try_mode(mi, 0, x, A, B, cand);
+        if (e >= 0 && e < best) {
+            best = e;
+            out = cand;
+        }
+    }
+    int bp = 0;
+    int64_t bcost = INT64_MAX;
+#pragma unroll 1
+    for (int p = 0; p < 32; ++p) {
+        const uint32_t pm = c_parts[p];
+        int64_t cost = 0;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            int lo[3] = {65535, 65535, 65535}, hi[3] = {0, 0, 0};
+#pragma unroll
+            for (int px = 0; px < 16; ++px) {
+                if ((int)((pm >> px) & 1) != r) continue;
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    lo[c] = min(lo[c], x[px][c]);
+                    hi[c] = max(hi[c], x[px][c]);
+                }
+            }
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int64_t ext = (int64_t)hi[c] - lo[c];
+                cost += ext * ext;
+            }
+        }
+        if (cost < bcost) {
+            bcost = cost;
+            bp = p;
+        }
+    }
+    fit_endpoints(x, c_parts[bp], 0, A[0], B[0]);
+    fit_endpoints(x, c_parts[bp], 1, A[1], B[1]);
+#pragma unroll 1
+    for (int mi = 0; mi < 10; ++mi) {
+        const int64_t e = try_mode(mi, bp, x, A, B, cand);
+        if (e >= 0 && e < best) {
+            best = e;
+            out = cand;
+        }
+    }
+    if (best == INT64_MAX) out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
+}
+
+struct CodecLaunch {
+    __half *data;
+    int32_t w, h, channels;
+    int64_t cstride, rstride, tstride;
+    float bias;
+    uint4 *blocks;
+    int32_t bw, bh, ntrip;
+};
+
+__global__ void __launch_bounds__(128) bc6h_encode_kernel(const CodecLaunch p)
+{
+    const int64_t nblk = (int64_t)p.ntrip * p.bh * p.bw;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblk; b += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(b / ((int64_t)p.bh * p.bw));
+        const int by = (int)((b / p.bw) % p.bh), bx = (int)(b % p.bw);
+        uint16_t tex[48];
+        const uint16_t biash = __half_as_ushort(__float2half_rn(p.bias));
+#pragma unroll
+        for (int px = 0; px < 16; ++px) {
+            const int y = min(by * 4 + px / 4, p.h - 1), xx = min(bx * 4 + px % 4, p.w - 1);
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int ch = t * 3 + c;
+                if (ch < p.channels) {
+                    const __half v = p.data[ch * p.cstride + y * p.rstride + xx * p.tstride];
+                    tex[px * 3 + c] = __half_as_ushort(__float2half_rn(__half2float(v) + p.bias));
+                } else {
+                    tex[px * 3 + c] = biash;
+                }
+            }
+        }
+        Block128 out;
+        encode_block(tex, out);
+        p.blocks[b] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
+    }
+}
+
+__global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
+{
+    const int64_t nblk = (int64_t)p.ntrip * p.bh * p.bw;
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblk; b += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(b / ((int64_t)p.bh * p.bw));
+        const int by = (int)((b / p.bw) % p.bh), bx = (int)(b % p.bw);
+        const uint4 raw = p.blocks[b];
+        Block128 blk;
+        blk.w[0] = raw.x;
+        blk.w[1] = raw.y;
+        blk.w[2] = raw.z;
+        blk.w[3] = raw.w;
+        uint16_t tex[48];
+        decode_block(blk, false, tex);
+#pragma unroll
+        for (int px = 0; px < 16; ++px) {
+            const int y = by * 4 + px / 4, xx = bx * 4 + px % 4;
+            if (y >= p.h || xx >= p.w) continue;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int ch = t * 3 + c;
+                if (ch < p.channels)
+                    p.data[ch * p.cstride + y * p.rstride + xx * p.tstride] =
+                        __float2half_rn(__half2float(__ushort_as_half(tex[px * 3 + c])) - p.bias);
+            }
+        }
+    }
+}
+
+// Raw block decode (no bias, no surface): 48 fp16 bit patterns per block, signed or
+// unsigned interpretation (for checking the bitstream against other decoders).
+__global__ void bc6h_decode_raw_kernel(const uint4 *blocks, int64_t n, int is_signed, uint16_t *out)
+{
+    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < n; b += (int64_t)gridDim.x * blockDim.x) {
+        const uint4 raw = blocks[b];
+        Block128 blk;
+        blk.w[0] = raw.x;
+        blk.w[1] = raw.y;
+        blk.w[2] = raw.z;
+        blk.w[3] = raw.w;
+        uint16_t tex[48];
+        decode_block(blk, is_signed != 0, tex);
+        for (int i = 0; i < 48; ++i) out[b * 48 + i] = tex[i];
+    }
+}
+
+static CodecLaunch make_launch(const NtBc6hSurface *s, const void *blocks, float bias)
+{
+    CodecLaunch L;
+    L.data = reinterpret_cast<__half *>(s->data);
+    L.w = s->width;
+    L.h = s->height;
+    L.channels = s->channels;
+    L.cstride = s->channel_stride;
+    L.rstride = s->row_stride;
+    L.tstride = s->texel_stride;
+    L.bias = bias;
+    L.blocks = reinterpret_cast<uint4 *>(const_cast<void *>(blocks));
+    L.bw = (s->width + 3) / 4;
+    L.bh = (s->height + 3) / 4;
+    L.ntrip = (s->channels + 2) / 3;
+    return L;
+}
+
+cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, bool encode, cudaStream_t st)
+{
+    const CodecLaunch L = make_launch(s, blocks, bias);
+    const int64_t nblk = (int64_t)L.ntrip * L.bh * L.bw;
+    const int64_t want = (nblk + 127) / 128;
+    const int grid = (int)(want < 64 * (int64_t)sm_count() ? want : 64 * (int64_t)sm_count());
+    if (encode)
+        bc6h_encode_kernel<<<grid, 128, 0, st>>>(L);
+    else
+        bc6h_decode_kernel<<<grid, 128, 0, st>>>(L);
+    count_launch();
+    return cudaGetLastError();
+}
+
+__global__ void fetch_texels_kernel(cudaTextureObject_t tex, int w, int h, float4 *out)
+{
+    const int x = blockIdx.x * blockDim.x + threadIdx.x, y = blockIdx.y;
+    if (x < w && y < h) out[(size_t)y * w + x] = tex2D<float4>(tex, x + 0.5f, y + 0.5f);
+}
+
+cudaError_t hardware_decode(const void *blocks, int bw, int bh, int is_signed, float *rgba)
+{
+    const int w = bw * 4, h = bh * 4;
+    cudaChannelFormatDesc desc = cudaCreateChannelDesc(
+        16, 16, 16, 0,
+        is_signed ? cudaChannelFormatKindSignedBlockCompressed6H : cudaChannelFormatKindUnsignedBlockCompressed6H);
+    cudaArray_t arr = nullptr;
+    cudaTextureObject_t tex = 0;
+    float4 *dout = nullptr;
+    cudaError_t e = cudaMallocArray(&arr, &desc, w, h);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DToArray(arr, 0, 0, blocks, (size_t)bw * 16, (size_t)bw * 16, bh, cudaMemcpyDefault);
+    if (e == cudaSuccess) {
+        cudaResourceDesc rd = {};
+        rd.resType = cudaResourceTypeArray;
+        rd.res.array.array = arr;
+        cudaTextureDesc td = {};
+        td.addressMode[0] = td.addressMode[1] = cudaAddressModeClamp;
+        td.filterMode = cudaFilterModePoint;
+        td.readMode = cudaReadModeElementType;
+        td.normalizedCoords = 0;
+        e = cudaCreateTextureObject(&tex, &rd, &td, nullptr);
+    }
+    if (e == cudaSuccess) e = cudaMalloc(&dout, (size_t)w * h * sizeof(float4));
+    if (e == cudaSuccess) {
+        fetch_texels_kernel<<<dim3((w + 127) / 128, h), 128>>>(tex, w, h, dout);
+        count_launch();
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(rgba, dout, (size_t)w * h * sizeof(float4), cudaMemcpyDeviceToHost);
+    if (dout) cudaFree(dout);
+    if (tex) cudaDestroyTextureObject(tex);
+    if (arr) cudaFreeArray(arr);
+    return e;
+}
+
+cudaError_t launch_bc6h_raw(const void *blocks, int64_t n, int is_signed, void *out, cudaStream_t st)
+{
+    const int64_t want = (n + 127) / 128;
+    const int grid = (int)(want < 64 * (int64_t)sm_count() ? want : 64 * (int64_t)sm_count());
+    bc6h_decode_raw_kernel<<<grid > 0 ? grid : 1, 128, 0, st>>>(reinterpret_cast<const uint4 *>(blocks), n,
+                                                                 is_signed, reinterpret_cast<uint16_t *>(out));
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace nt

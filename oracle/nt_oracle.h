@@ -110,6 +110,23 @@ void nto_target_params(uint32_t seed, int32_t channel, int32_t k, int32_t *fu, i
 void nto_generate_target(uint16_t *out, int32_t w, int32_t h, int32_t channels, uint32_t seed,
                          int32_t pbr_normals, int32_t threads);
 
+/* ---- BC6H-style latent block codec (nt_oracle_codec.c) ------------------------------- */
+int nto_bc6h_mode_index(const uint8_t block[16]);
+/* out: 16 texels x 3 channels of fp16 bits, texels in raster order */
+void nto_bc6h_decode_block(const uint8_t block[16], int is_signed, uint16_t out[48]);
+/* UF16 encoder: texels are non-negative halves (16 texels x 3 channels) */
+void nto_bc6h_encode_block(const uint16_t texels[48], uint8_t out[16]);
+/* Surfaces: element (channel c, row y, texel x) at data[c*cstride + y*rstride + x*tstride];
+ * channels grouped in triples (a missing third channel encodes as the bias); blocks
+ * [ceil(channels/3)][ceil(h/4)][ceil(w/4)] x 16 B of BC6H UF16 holding value + bias;
+ * partial blocks replicate the edge texels. */
+void nto_bc6h_encode_surface(const uint16_t *data, int32_t w, int32_t h, int32_t channels,
+                             int64_t cstride, int64_t rstride, int64_t tstride, float bias,
+                             uint8_t *blocks, int32_t threads);
+void nto_bc6h_decode_surface(const uint8_t *blocks, int32_t w, int32_t h, int32_t channels,
+                             int64_t cstride, int64_t rstride, int64_t tstride, float bias,
+                             uint16_t *data, int32_t threads);
+
 /* ---- tests/forward_pass_test.cu:45-150 known-answer test ---------------------------- */
 void nto_fwdtest_generate(uint16_t inputs[32 * 12], uint16_t w0[256], uint16_t w1[256],
                           uint16_t b0[16], uint16_t b1[16]);

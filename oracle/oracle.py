@@ -33,7 +33,8 @@ def build(force: bool = False) -> str:
 
 def _stale() -> bool:
     t = os.path.getmtime(LIB_PATH)
-    for f in ("nt_oracle.c", "nt_oracle_codec.c", "nt_oracle.h"):
+    for f in ("nt_oracle.c", "nt_oracle_codec.c", "nt_oracle.h",
+              os.path.join("..", "include", "neural_textures", "bc6h_format.h")):
         if os.path.getmtime(os.path.join(HERE, f)) > t:
             return True
     return False
@@ -295,3 +296,81 @@ def zero_input_rows(W0: np.ndarray, n_inputs: int) -> np.ndarray:
     W = W0.reshape(64, 32).copy()
     W[:, n_inputs:] = 0
     return W.reshape(-1)
+
+
+# ---------------------------------------------------------------------------------------
+# BC6H codec
+
+_u8p = C.POINTER(C.c_uint8)
+
+
+def _codec_lib():
+    L = lib()
+    if not getattr(L, "_codec_bound", False):
+        L.nto_bc6h_mode_index.restype = C.c_int
+        L.nto_bc6h_mode_index.argtypes = [_u8p]
+        L.nto_bc6h_decode_block.argtypes = [_u8p, C.c_int, u16p]
+        L.nto_bc6h_encode_block.argtypes = [u16p, _u8p]
+        L.nto_bc6h_encode_surface.argtypes = [u16p, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
+                                              C.c_int64, C.c_float, _u8p, C.c_int32]
+        L.nto_bc6h_decode_surface.argtypes = [_u8p, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
+                                              C.c_int64, C.c_float, u16p, C.c_int32]
+        L._codec_bound = True
+    return L
+
+
+def bc6h_decode_blocks(blocks: np.ndarray, is_signed: bool) -> np.ndarray:
+    """[n][16] uint8 blocks -> [n][16][3] fp16 bit patterns."""
+    L = _codec_lib()
+    blocks = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 16)
+    out = np.zeros((blocks.shape[0], 16, 3), np.uint16)
+    for i in range(blocks.shape[0]):
+        L.nto_bc6h_decode_block(blocks[i].ctypes.data_as(_u8p), int(is_signed), out[i].ctypes.data_as(u16p))
+    return out
+
+
+def bc6h_mode_index(block: np.ndarray) -> int:
+    return _codec_lib().nto_bc6h_mode_index(np.ascontiguousarray(block, np.uint8).ctypes.data_as(_u8p))
+
+
+def _strides(shape, layout):
+    if layout == "planar":
+        C_, H, W = shape
+        return W, H, C_, H * W, W, 1
+    H, W, C_ = shape
+    return W, H, C_, 1, W * C_, C_
+
+
+def bc6h_encode_surface(data: np.ndarray, layout="planar", bias=4.0, threads=8) -> np.ndarray:
+    """fp16 bits (uint16) surface -> uint8 blocks (same layout conventions as the C ABI)."""
+    L = _codec_lib()
+    data = np.ascontiguousarray(data, np.uint16)
+    W, H, C_, cs, rs, ts = _strides(data.shape, layout)
+    nb = ((C_ + 2) // 3) * ((H + 3) // 4) * ((W + 3) // 4)
+    blocks = np.zeros(nb * 16, np.uint8)
+    L.nto_bc6h_encode_surface(data.ctypes.data_as(u16p), W, H, C_, cs, rs, ts, bias, blocks.ctypes.data_as(_u8p),
+                              threads)
+    return blocks
+
+
+def bc6h_decode_surface(blocks: np.ndarray, shape, layout="planar", bias=4.0, threads=8) -> np.ndarray:
+    L = _codec_lib()
+    out = np.zeros(shape, np.uint16)
+    W, H, C_, cs, rs, ts = _strides(shape, layout)
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    L.nto_bc6h_decode_surface(blocks.ctypes.data_as(_u8p), W, H, C_, cs, rs, ts, bias, out.ctypes.data_as(u16p),
+                              threads)
+    return out
+
+
+def smooth_latents(rng: np.random.Generator, shape, std=0.5, clip=4.0, corr=8) -> np.ndarray:
+    """BASELINE config 3 inputs: Gaussian values (mean 0, std 0.5) with corr x corr
+    box-correlated smoothness (wrap), clipped to +-clip; fp16 bit patterns."""
+    n = rng.standard_normal(shape)
+    for ax in (-1, -2):
+        acc = np.zeros_like(n)
+        for k in range(corr):
+            acc += np.roll(n, k, axis=ax)
+        n = acc
+    n = n / n.std() * std
+    return np.clip(n, -clip, clip).astype(np.float16).view(np.uint16)

@@ -168,6 +168,59 @@ def cpu_train_baseline(O, seconds=12.0):
                       f"+ one Adam pass over all {P} latent params; step time extrapolated to the full batch"}
 
 
+CFG3 = dict(workload="config3_bc6h_16x4096sq", planes=16, size=4096)
+
+
+def run_codec_bench(torch, dev, stream, L, iters, rank, world, dist):
+    """BASELINE config 3 per GPU: 16 fp16 planes of 4096^2 (Gaussian, std 0.5, 8x8 box-
+    correlated, clipped to +-4; generated with torch on the device, set-up only), encoded to
+    BC6H UF16 blocks (channel triples, bias 4) and decoded back.  Inputs exceed L2."""
+    import torch.nn.functional as F
+    from neural_textures_b200 import _native
+    from neural_textures_b200.api import bc6h_surface
+    P, S = CFG3["planes"], CFG3["size"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    planes = torch.empty((P, S, S), dtype=torch.float16, device=dev)
+    for p in range(P):  # one plane at a time keeps the fp32 temporaries small
+        n = torch.randn((1, 1, S, S), generator=g, device=dev)
+        n = F.avg_pool2d(F.pad(n, (7, 0, 7, 0), mode="circular"), 8, stride=1)
+        planes[p] = (n / n.std() * 0.5).clamp_(-4, 4)[0, 0].half()
+    nbytes = int(L.nt_bc6h_blocks_bytes(S, S, P))
+    blocks = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty_like(planes)
+    src = bc6h_surface(planes)
+    dst = bc6h_surface(out)
+    sptr = stream.cuda_stream
+    _native.check(L.nt_bc6h_encode(ctypes.byref(src), blocks.data_ptr(), 4.0, sptr))
+    _native.check(L.nt_bc6h_decode(blocks.data_ptr(), ctypes.byref(dst), 4.0, sptr))
+    torch.cuda.synchronize(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(iters)]
+    for k in range(iters):
+        ev[k][0].record(stream)
+        _native.check(L.nt_bc6h_encode(ctypes.byref(src), blocks.data_ptr(), 4.0, sptr))
+        ev[k][1].record(stream)
+        ev[k][2].record(stream)
+        _native.check(L.nt_bc6h_decode(blocks.data_ptr(), ctypes.byref(dst), 4.0, sptr))
+        ev[k][3].record(stream)
+    torch.cuda.synchronize(dev)
+    t_enc = sum(e[0].elapsed_time(e[1]) for e in ev) / iters
+    t_dec = sum(e[2].elapsed_time(e[3]) for e in ev) / iters
+    err = (out.float() - planes.float())
+    rmse = float(err.pow(2).mean().sqrt())
+    if world > 1:
+        t = torch.tensor([t_enc, t_dec], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_enc, t_dec = t.tolist()
+    nblk = nbytes // 16
+    alg_bytes = P * S * S * 2 + nbytes  # planes read + blocks written (encode); reverse for decode
+    return {"workload": CFG3["workload"], "blocks_per_gpu": nblk,
+            "encode_blocks_per_s": world * nblk / (t_enc * 1e-3), "decode_blocks_per_s": world * nblk / (t_dec * 1e-3),
+            "encode_ms": t_enc, "decode_ms": t_dec, "algorithmic_bytes_per_pass": alg_bytes,
+            "decode_hbm_gbs": alg_bytes / (t_dec * 1e-3) / 1e9, "encode_hbm_gbs": alg_bytes / (t_enc * 1e-3) / 1e9,
+            "rmse": rmse, "format": "BC6H UF16 of value + 4, channel triples"}
+
+
 def run_reference(args):
     """--impl reference: the CPU port of the reference algorithm on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
@@ -203,6 +256,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prewarm", type=float, default=0.5, help="seconds of untimed steps before warm-up")
+    ap.add_argument("--codec-iters", type=int, default=5, help="timed BC6H encode / decode passes (0: skip)")
     ap.add_argument("--decode-iters", type=int, default=200)
     args = ap.parse_args()
     if args.impl == "reference":
@@ -316,7 +370,12 @@ def main():
         dev_ev[k][1].record(stream)
     torch.cuda.synchronize(dev)
     t_dec = sum(a.elapsed_time(b) for a, b in dev_ev) / args.decode_iters
-    clk = clocks.stop()  # sampled across the timed training, e2e and decode regions
+
+    # ---- config 3 codec: 16 latent planes of 4096^2 fp16 per GPU -------------------------
+    codec = None
+    if args.codec_iters > 0:
+        codec = run_codec_bench(torch, dev, stream, L, args.codec_iters, rank, world, dist)
+    clk = clocks.stop()  # sampled across the timed training, e2e, decode and codec regions
     texels = CFG0["image"][0] * CFG0["image"][1]
 
     if world > 1:
@@ -361,6 +420,9 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if codec:
+        codec["decode_hbm_frac"] = codec["decode_hbm_gbs"] / pk["hbm"]
+        line["codec"] = codec
     if not args.no_cpu_baseline:
         from oracle import oracle as O
         O.build()

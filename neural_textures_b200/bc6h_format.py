@@ -164,11 +164,67 @@ def emit_header() -> str:
     return "\n".join(lines)
 
 
+def _runs(mode_index: int):
+    """Header fields of a mode as runs (field, first block bit, first field bit, length) of
+    consecutive block bits holding consecutive ascending field bits."""
+    runs = []
+    for k, (f, b) in enumerate(layout_bits(mode_index)):
+        if f == FIELD_M:
+            continue
+        if runs and runs[-1][0] == f and runs[-1][1] + runs[-1][3] == k and runs[-1][2] + runs[-1][3] == b:
+            runs[-1][3] += 1
+        else:
+            runs.append([f, k, b, 1])
+    return runs
+
+
+def emit_unpack() -> str:
+    """CUDA device code that extracts the endpoint and partition fields of every mode with
+    straight-line shifts (no table walk); generated from the same layout tables."""
+    check_tables()
+    out = [
+        "// GENERATED by `python -m neural_textures_b200.bc6h_format` from neural_textures_b200/bc6h_format.py.",
+        "// Straight-line BC6H header unpacking: one case per mode, each field assembled from runs",
+        "// of consecutive block bits (lo = block bits 0..63, hi = 64..127).",
+        "#pragma once",
+        "#include <stdint.h>",
+        "",
+        "namespace nt {",
+        "",
+        "__device__ __forceinline__ uint32_t bc6h_bits(uint64_t lo, uint64_t hi, int k, int n)",
+        "{",
+        "    const uint64_t v = k >= 64 ? (hi >> (k - 64)) : (k + n <= 64 ? (lo >> k) : ((lo >> k) | (hi << (64 - k))));",
+        "    return (uint32_t)(v & ((1ull << n) - 1ull));",
+        "}",
+        "",
+        "// e[endpoint][channel] raw stored values, d partition; returns false for reserved modes",
+        "__device__ __forceinline__ void bc6h_unpack_header(int mi, uint64_t lo, uint64_t hi, int (&e)[4][3], int &d)",
+        "{",
+        "#pragma unroll",
+        "    for (int i = 0; i < 4; ++i) e[i][0] = e[i][1] = e[i][2] = 0;",
+        "    d = 0;",
+        "    switch (mi) {",
+    ]
+    for i in range(len(MODES)):
+        out.append(f"    case {i}:")
+        for f, k, b, n in _runs(i):
+            tgt = "d" if f == FIELD_D else f"e[{f // 3}][{f % 3}]"
+            shift = f" << {b}" if b else ""
+            out.append(f"        {tgt} |= (int)(bc6h_bits(lo, hi, {k}, {n}){shift});")
+        out.append("        break;")
+    out += ["    default:", "        break;", "    }", "}", "", "}  // namespace nt", ""]
+    return "\n".join(out)
+
+
 def main():
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     path = os.path.join(root, "include", "neural_textures", "bc6h_format.h")
     with open(path, "w") as f:
         f.write(emit_header())
+    print(path)
+    path = os.path.join(root, "neural_textures_b200", "csrc", "nt_bc6h_unpack.cuh")
+    with open(path, "w") as f:
+        f.write(emit_unpack())
     print(path)
 
 

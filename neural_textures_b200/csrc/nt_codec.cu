@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "neural_textures/bc6h_format.h"
+#include "nt_bc6h_unpack.cuh"
 #include "nt_capi.h"
 #include "nt_kernels.cuh"
 
@@ -107,26 +108,9 @@ __device__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48]
     }
     const NtBc6hMode M = c_modes[mi];
     int e[4][3];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) e[i][0] = e[i][1] = e[i][2] = 0;
     int d = 0;
-#pragma unroll 1
-    for (int k = 0; k < M.header_bits; ++k) {
-        const int ent = c_layout[mi][k];
-        const int f = ent >> 4, bit = ent & 15;
-        const int v = b.bit(k);
-        if (f < 12) {
-            const int ei = f / 3, ci = f % 3;
-            // registers only: branch over the 12 fields keeps e[][] out of local memory
-#pragma unroll
-            for (int q = 0; q < 12; ++q)
-                if (q == f) e[q / 3][q % 3] |= v << bit;
-            (void)ei;
-            (void)ci;
-        } else if (f == NT_BC6H_FIELD_D) {
-            d |= v << bit;
-        }
-    }
+    bc6h_unpack_header(mi, (uint64_t)b.w[0] | ((uint64_t)b.w[1] << 32), (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32),
+                       e, d);
     const int ne = 2 * M.regions, epb = M.endpoint_bits;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
@@ -232,6 +216,29 @@ __device__ void fit_endpoints(const int x[16][3], uint32_t mask, int want, int A
     }
 }
 
+// Palette index nearest to the projection of x onto a -> b (same arithmetic as the CPU
+// oracle: int64 sums, round-to-nearest conversions, one IEEE division).
+__device__ __forceinline__ int project_index(const int x[3], const int a[3], const int b[3], int ib)
+{
+    int64_t dot = 0, len2 = 0;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        const int64_t d = (int64_t)b[c] - a[c];
+        dot += ((int64_t)x[c] - a[c]) * d;
+        len2 += d * d;
+    }
+    if (len2 == 0) return 0;
+    const float t = __fdiv_rn(__fmul_rn(__ll2float_rn(dot), 64.0f), __ll2float_rn(len2));
+    const int ni = 1 << ib;
+    int k0 = 0;
+#pragma unroll 1
+    for (int k = 1; k < ni; ++k) {
+        const float mid = 0.5f * (float)(ib == 3 ? c_w3[k - 1] + c_w3[k] : c_w4[k - 1] + c_w4[k]);
+        if (t > mid) k0 = k;
+    }
+    return k0;
+}
+
 // Evaluate (and pack) one candidate; returns the squared error or -1 when the mode cannot
 // hold the endpoints.
 __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2][3], const int B[2][3],
@@ -264,16 +271,24 @@ __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2]
 #pragma unroll
         for (int px = 0; px < 16; ++px) {
             const int r = (mask >> px) & 1;
+            int a3[3], b3[3];
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                a3[c] = r ? u[1][0][c] : u[0][0][c];
+                b3[c] = r ? u[1][1][c] : u[0][1][c];
+            }
+            const int k0 = project_index(x[px], a3, b3, ib);
             int64_t best = INT64_MAX;
             int bi = 0;
-#pragma unroll 1
-            for (int kk = 0; kk < ni; ++kk) {
+#pragma unroll
+            for (int dk = -1; dk <= 1; ++dk) {
+                const int kk = k0 + dk;
+                if (kk < 0 || kk >= ni) continue;
                 const int w = ib == 3 ? c_w3[kk] : c_w4[kk];
                 int64_t dsum = 0;
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
-                    const int a = r ? u[1][0][c] : u[0][0][c], bb = r ? u[1][1][c] : u[0][1][c];
-                    const int v = (a * (64 - w) + bb * w + 32) >> 6;
+                    const int v = (a3[c] * (64 - w) + b3[c] * w + 32) >> 6;
                     const int64_t dd = (int64_t)(x[px][c] - v);
                     dsum += dd * dd;
                 }
@@ -424,16 +439,41 @@ struct CodecLaunch {
     float bias;
     uint4 *blocks;
     int32_t bw, bh, ntrip;
+    int32_t rows4;  // planar, 8-byte aligned rows of whole blocks: 4 texels move as one uint2
 };
 
+// grid: (ceil(block columns / 128), block rows, channel triples); one thread per block
 __global__ void __launch_bounds__(128) bc6h_encode_kernel(const CodecLaunch p)
 {
-    const int64_t nblk = (int64_t)p.ntrip * p.bh * p.bw;
-    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblk; b += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(b / ((int64_t)p.bh * p.bw));
-        const int by = (int)((b / p.bw) % p.bh), bx = (int)(b % p.bw);
+    const int bx = blockIdx.x * blockDim.x + threadIdx.x, by = blockIdx.y, t = blockIdx.z;
+    if (bx < p.bw) do {
+        const int64_t b = ((int64_t)t * p.bh + by) * p.bw + bx;
         uint16_t tex[48];
         const uint16_t biash = __half_as_ushort(__float2half_rn(p.bias));
+        if (p.rows4) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int ch = t * 3 + c;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    uint2 raw = make_uint2(0u, 0u);
+                    if (ch < p.channels)
+                        raw = __ldg(reinterpret_cast<const uint2 *>(p.data + ch * p.cstride +
+                                                                    (int64_t)(by * 4 + r) * p.rstride + bx * 4));
+                    const uint16_t v[4] = {(uint16_t)(raw.x & 0xffff), (uint16_t)(raw.x >> 16), (uint16_t)(raw.y & 0xffff),
+                                           (uint16_t)(raw.y >> 16)};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        tex[(r * 4 + i) * 3 + c] =
+                            ch < p.channels ? __half_as_ushort(__float2half_rn(__half2float(__ushort_as_half(v[i])) + p.bias))
+                                            : biash;
+                }
+            }
+            Block128 out;
+            encode_block(tex, out);
+            p.blocks[b] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
+            continue;
+        }
 #pragma unroll
         for (int px = 0; px < 16; ++px) {
             const int y = min(by * 4 + px / 4, p.h - 1), xx = min(bx * 4 + px % 4, p.w - 1);
@@ -451,15 +491,15 @@ __global__ void __launch_bounds__(128) bc6h_encode_kernel(const CodecLaunch p)
         Block128 out;
         encode_block(tex, out);
         p.blocks[b] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
-    }
+    } while (0);
 }
 
+// grid: (ceil(block columns / 128), block rows, channel triples); one thread per block
 __global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
 {
-    const int64_t nblk = (int64_t)p.ntrip * p.bh * p.bw;
-    for (int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblk; b += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(b / ((int64_t)p.bh * p.bw));
-        const int by = (int)((b / p.bw) % p.bh), bx = (int)(b % p.bw);
+    const int bx = blockIdx.x * blockDim.x + threadIdx.x, by = blockIdx.y, t = blockIdx.z;
+    if (bx < p.bw) do {
+        const int64_t b = ((int64_t)t * p.bh + by) * p.bw + bx;
         const uint4 raw = p.blocks[b];
         Block128 blk;
         blk.w[0] = raw.x;
@@ -468,6 +508,24 @@ __global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
         blk.w[3] = raw.w;
         uint16_t tex[48];
         decode_block(blk, false, tex);
+        if (p.rows4) {
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int ch = t * 3 + c;
+                if (ch >= p.channels) break;
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    uint16_t v[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        v[i] = __half_as_ushort(
+                            __float2half_rn(__half2float(__ushort_as_half(tex[(r * 4 + i) * 3 + c])) - p.bias));
+                    *reinterpret_cast<uint2 *>(p.data + ch * p.cstride + (int64_t)(by * 4 + r) * p.rstride + bx * 4) =
+                        make_uint2(v[0] | ((uint32_t)v[1] << 16), v[2] | ((uint32_t)v[3] << 16));
+                }
+            }
+            continue;
+        }
 #pragma unroll
         for (int px = 0; px < 16; ++px) {
             const int y = by * 4 + px / 4, xx = bx * 4 + px % 4;
@@ -480,7 +538,7 @@ __global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
                         __float2half_rn(__half2float(__ushort_as_half(tex[px * 3 + c])) - p.bias);
             }
         }
-    }
+    } while (0);
 }
 
 // Raw block decode (no bias, no surface): 48 fp16 bit patterns per block, signed or
@@ -515,15 +573,16 @@ static CodecLaunch make_launch(const NtBc6hSurface *s, const void *blocks, float
     L.bw = (s->width + 3) / 4;
     L.bh = (s->height + 3) / 4;
     L.ntrip = (s->channels + 2) / 3;
+    L.rows4 = s->texel_stride == 1 && s->width % 4 == 0 && s->height % 4 == 0 && s->row_stride % 4 == 0 &&
+              s->channel_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(s->data) & 7u) == 0;
     return L;
 }
 
 cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, bool encode, cudaStream_t st)
 {
     const CodecLaunch L = make_launch(s, blocks, bias);
-    const int64_t nblk = (int64_t)L.ntrip * L.bh * L.bw;
-    const int64_t want = (nblk + 127) / 128;
-    const int grid = (int)(want < 64 * (int64_t)sm_count() ? want : 64 * (int64_t)sm_count());
+    if (L.bh > 65535 || L.ntrip > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((L.bw + 127) / 128, L.bh, L.ntrip);
     if (encode)
         bc6h_encode_kernel<<<grid, 128, 0, st>>>(L);
     else

@@ -220,6 +220,29 @@ static void fit_endpoints(const int x[16][3], uint16_t mask, int want, int A[3],
     }
 }
 
+/* Palette index nearest to the projection of x onto the segment a -> b: t = 64 dot / |b-a|^2
+ * (int64 sums converted to float with round-to-nearest, one correctly rounded division),
+ * then the number of weight midpoints below t.  Only indices k0 - 1 .. k0 + 1 are then
+ * evaluated exactly. */
+static int project_index(const int x[3], const int a[3], const int b[3], int ib)
+{
+    int64_t dot = 0, len2 = 0;
+    for (int c = 0; c < 3; ++c) {
+        const int64_t d = (int64_t)b[c] - a[c];
+        dot += ((int64_t)x[c] - a[c]) * d;
+        len2 += d * d;
+    }
+    if (len2 == 0) return 0;
+    const float t = ((float)dot * 64.0f) / (float)len2;
+    const int ni = 1 << ib;
+    int k0 = 0;
+    for (int k = 1; k < ni; ++k) {
+        const float mid = 0.5f * (float)((ib == 3 ? W3[k - 1] + W3[k] : W4[k - 1] + W4[k]));
+        if (t > mid) k0 = k;
+    }
+    return k0;
+}
+
 static int64_t try_mode(int mi, int part, const int x[16][3], int A[2][3], int B[2][3], uint8_t out[16])
 {
     const NtBc6hMode *M = &MODES[mi];
@@ -242,9 +265,11 @@ static int64_t try_mode(int mi, int part, const int x[16][3], int A[2][3], int B
         err = 0;
         for (int px = 0; px < 16; ++px) {
             const int r = (mask >> px) & 1;
+            const int k0 = project_index(x[px], u[r][0], u[r][1], ib);
             int64_t best = INT64_MAX;
             int bi = 0;
-            for (int k = 0; k < ni; ++k) {
+            for (int k = k0 - 1; k <= k0 + 1; ++k) {
+                if (k < 0 || k >= ni) continue;
                 const int w = ib == 3 ? W3[k] : W4[k];
                 int64_t dsum = 0;
                 for (int c = 0; c < 3; ++c) {

@@ -227,6 +227,15 @@ NT_API nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int3
 NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h,
                                          int32_t is_signed, float *rgba);
 
+/* ---- tensor-core self-test (no reference counterpart) ---------------------------------- */
+
+/* Runs the tcgen05 operand layouts of the fused kernels on small known matrices (device
+ * pointers): a [128][32], b [64][32], h [128][64] fp16 row-major; writes d1 = a b^T
+ * ([128][64] fp32) and d2 = h^T a ([64][32] fp32); *status (device int) gets bit 0 set if
+ * the tensor core did not complete within the bounded wait. */
+NT_API nt_status nt_umma_selftest(const void *a, const void *b, const void *h, float *d1, float *d2,
+                                  int32_t *status, nt_stream_t stream);
+
 /* ---- seeded set-up helpers (not in the reference: it loads EXR files, main.cpp:436-556) -- */
 
 /* Synthetic target: per channel the sigmoid of a sum of 16 seeded sinusoids with

@@ -102,6 +102,7 @@ SIGNATURES = {
     "nt_bc6h_decode": (C.c_int, [C.c_void_p, _S, C.c_float, C.c_void_p]),
     "nt_bc6h_decode_raw": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "nt_bc6h_decode_hardware": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
+    "nt_umma_selftest": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 

@@ -236,6 +236,12 @@ NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, i
 NT_API nt_status nt_umma_selftest(const void *a, const void *b, const void *h, float *d1, float *d2,
                                   int32_t *status, nt_stream_t stream);
 
+/* Device status word of the training kernels (no reference counterpart: the reference has
+ * no bounded waits).  Bit 0 is set when a bounded wait inside a kernel gave up; the kernel
+ * then stops issuing work and returns.  Synchronises with the device; clear != 0 resets
+ * the word. */
+NT_API nt_status nt_read_device_status(uint32_t *status, int32_t clear);
+
 /* ---- seeded set-up helpers (not in the reference: it loads EXR files, main.cpp:436-556) -- */
 
 /* Synthetic target: per channel the sigmoid of a sum of 16 seeded sinusoids with

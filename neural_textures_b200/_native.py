@@ -103,6 +103,7 @@ SIGNATURES = {
     "nt_bc6h_decode_raw": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "nt_bc6h_decode_hardware": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
     "nt_umma_selftest": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
+    "nt_read_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 

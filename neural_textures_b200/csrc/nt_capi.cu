@@ -245,8 +245,9 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
                p->lattice_width, p->lattice_height);
     NT_REQUIRE(p->sample_stride_x > 0.f && p->sample_stride_y > 0.f, "sample strides must be positive");
     for (int l = 0; l < 3; ++l)
-        NT_REQUIRE(p->network_weight_gradients[l] && p->network_bias_gradients[l],
-                   "network gradient buffers of layer %d are required", l);
+        NT_REQUIRE(p->network_weight_gradients[l] && aligned16(p->network_weight_gradients[l]) &&
+                       p->network_bias_gradients[l],
+                   "network gradient buffers of layer %d are required (weights 16-byte aligned)", l);
     if (type == NT_TRAIN_UNCONSTRAINED)
         for (int f = 0; f < NT_NUM_FEATURES; ++f)
             NT_REQUIRE(p->features[f].gradients && aligned16(p->features[f].gradients),

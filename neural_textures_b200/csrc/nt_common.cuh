@@ -103,10 +103,18 @@ __device__ __forceinline__ void texel_uv(int32_t x, int32_t y, int32_t w, int32_
 // ---------------------------------------------------------------------------------------
 // Catmull-Rom footprint
 
+// Wrap c into [0, n).  The filter taps and footprint windows stay within one period of the
+// grid, so one conditional correction in each direction is the common path; the modulo
+// only runs for coordinates further out.
 __device__ __forceinline__ int32_t wrap_coord(int32_t c, int32_t n)
 {
-    int32_t r = c % n;
-    return r < 0 ? r + n : r;
+    int32_t r = c < 0 ? c + n : c;
+    r = r >= n ? r - n : r;
+    if ((uint32_t)r >= (uint32_t)n) {
+        r = c % n;
+        r = r < 0 ? r + n : r;
+    }
+    return r;
 }
 
 __device__ __forceinline__ void catmull_rom_weights(float f, float w[4])

@@ -65,6 +65,10 @@ struct AdamLaunch {
 
 // Returns the number of CTAs used (0 on launch failure; cudaGetLastError holds the error).
 cudaError_t launch_train(const TrainLaunch &p, int channels, cudaStream_t stream);
+// tcgen05 / TMEM training kernel (16 x 8 tiles; recomputes tiles_x / tiles_y itself)
+cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream);
+// Training engine: 1 = tcgen05 (default), 0 = per-warp mma.sync (NT_TRAIN_ENGINE=mma)
+int train_engine();
 cudaError_t launch_decode(const DecodeLaunch &p, int channels, cudaStream_t stream);
 cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream);
 int sm_count();

@@ -23,6 +23,8 @@
 //    Texels on a window border also receive contributions from neighbouring tiles; the
 //    reductions make those sums exact.
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
 #include "nt_mlp_smem.cuh"
 
@@ -704,8 +706,18 @@ static cudaError_t launch_train_t(const TrainLaunch &p, cudaStream_t stream)
     return cudaGetLastError();
 }
 
+int train_engine()
+{
+    static const int engine = [] {
+        const char *e = getenv("NT_TRAIN_ENGINE");
+        return (e && strcmp(e, "mma") == 0) ? 0 : 1;
+    }();
+    return engine;
+}
+
 cudaError_t launch_train(const TrainLaunch &p, int channels, cudaStream_t stream)
 {
+    if (train_engine() == 1) return launch_train_tc(p, channels, stream);
     const bool wide = p.net.cout > 8;
     if (channels == 8) return wide ? launch_train_t<8, 2>(p, stream) : launch_train_t<8, 1>(p, stream);
     if (channels == 12) return wide ? launch_train_t<12, 2>(p, stream) : launch_train_t<12, 1>(p, stream);

@@ -1,0 +1,801 @@
+// nt_train_tc.cu -- fused training pass on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Same contract as the mma.sync kernel in nt_train.cu (TrainLoopPass / TrainLoop,
+// mavenkim2/neural_textures train.cu:818-915, :979-983; mlp.h:101-257 backward; the latent
+// scatter of train.cu:460-509): one jittered sample per lattice cell, weighted L2 loss,
+// weight / bias / latent gradients accumulated (x 1 / num_samples) into fp32 buffers.
+//
+// Work decomposition.  A CTA of 8 warps owns one tile of 16 x 8 lattice cells (128
+// samples, M = 128, sample s = TMEM lane s) at a time; two CTAs share an SM, so one CTA's
+// gathers and epilogues overlap the other's tensor-core products.  Thread t works on sample
+// t % 128; the two threads of a sample split the gathers (latent grids / target and
+// positional features) and the epilogue columns (warps w and w + 4 read the same TMEM
+// lanes).  Per tile:
+//     gather -> F1 -> E1 -> F2 -> E2 -> F3 -> E3 (loss) -> B3 -> E4 -> B2 -> E5 -> B1 -> E6
+// Fk / Bk are tensor-core products that thread 0 issues after a CTA barrier (operands in
+// shared memory, fenced to the async proxy); Ek are epilogues (TMEM -> registers -> fp16
+// operand tiles in shared memory).
+//
+// Tensor-core products per tile (fp16 x fp16 -> fp32; operands in the no-swizzle
+// core-matrix layout of nt_umma.cuh):
+//   F1  Z1   = X  W1e^T          M128 N64  K=XW   (X carries a constant-1 column, W1e the
+//                                                  bias b1 in that column)
+//   F2  Z2   = H1e W2e^T         M128 N64  K80    (H1e = [relu(Z1) | 1 | 0...])
+//   F3  Y    = H2e W3e^T         M128 N16  K80
+//   B3  dH2  = dY W3             M128 N64  K16    (W3e read MN-major: no transpose)
+//       dW3^T += H2e^T dY        M128 N16  K128   (row 64 of the result is db3)
+//   B2  dH1  = dZ2 W2            M128 N64  K64
+//       dW2  += dZ2^T H1e        M64  N72  K128   (column 64 is db2)
+//   B1  dX   = dZ1 W1            M128 NX   K64
+//       dW1  += dZ1^T X          M64  N=XW K128   (column 2C + 8 is db1)
+// The weight-gradient accumulators stay in TMEM for the whole kernel and each CTA adds
+// them to global memory once at the end (float4 reductions).  The activation tiles are
+// stored once as [samples][features] and read K-major by the forward products and
+// MN-major by the gradient products.
+//
+// Latent gradients: dX rows go to shared memory and a column sweep over the tile's
+// footprint window accumulates them per texel before one float4 reduction per 4 channels
+// (per-tap vector atomics when a window does not fit).
+//
+// Every wait is bounded.  A timeout sets bit 0 of the device status word (read back by
+// nt_read_device_status); the CTA agrees on it at its next barrier, stops issuing work,
+// waits (bounded) for the products in flight and releases its tensor memory.
+#include <climits>
+
+#include "nt_kernels.cuh"
+#include "nt_mma.cuh"
+#include "nt_umma.cuh"
+
+namespace nt {
+
+__device__ unsigned int g_device_status;  // bit 0: a bounded wait of a training kernel gave up
+
+namespace tc {
+
+constexpr int kTileW = 16, kTileH = 8, kTileN = 128;
+constexpr int kThreadsTC = 256;
+constexpr int kMaxWinW = 40;  // widest footprint window the sweep handles (texels)
+constexpr int kHC = 10;       // core-matrix chunks per H row: 64 activations, 1, 0 x 15
+constexpr int kHW = kHC * 8;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColW1 = 0, kColW2 = 64, kColW3 = 160, kColTile = 192;
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+template <int C>
+struct Cfg {
+    static constexpr int kBias1 = 2 * C + 8;                 // column of the constant 1 in X
+    static constexpr int XC = ((kBias1 + 1 + 15) / 16) * 2;  // chunks of 8 halves per X row
+    static constexpr int XW = XC * 8;                        // 32 (C = 8) or 48 (C = 12)
+    static constexpr int LC = C / 4;                         // X chunks holding the 2C latents
+    static constexpr int NX = ((2 * C + 15) / 16) * 16;      // dX columns produced by B1
+    static constexpr int DXS = 2 * C + 4;                    // fp32 dX row stride (floats)
+};
+
+struct Window {
+    int32_t x0, w, span, ok;
+    int32_t cand_x[kMaxWinW];  // lo | hi << 16 of the candidate lattice columns
+};
+
+template <int C>
+struct Smem {
+    alignas(128) uint8_t W1[64 * Cfg<C>::XW * 2];  // [out][in | b1 | 0]
+    alignas(128) uint8_t W2[64 * kHW * 2];         // [out][in | b2 | 0]
+    alignas(128) uint8_t W3[16 * kHW * 2];         // [out (zero rows past cout)][in | b3 | 0]
+    alignas(128) uint8_t X[kTileN * Cfg<C>::XW * 2];
+    alignas(128) uint8_t H1[kTileN * kHW * 2];  // H1e, then dZ1 (in place)
+    alignas(128) uint8_t H2[kTileN * kHW * 2];  // H2e, then dZ2 (in place), then dX (fp32)
+    alignas(128) uint8_t DY[kTileN * 16 * 2];   // follows H2: the M = 128 read of H2 runs 768 B past it
+    short2 base[2][kTileN];
+    float wts[2][kTileN][8];
+    int32_t part[2][4][4][kTileW];  // [grid][col min, col max, row min, row max][warp][index]
+    int32_t colext[2][2][kTileW];
+    int32_t rowmin[2][kTileH];
+    Window win[2];
+    alignas(8) uint64_t done;
+    uint32_t tmem_base;
+    float red[kThreadsTC / 32];
+};
+
+__device__ __forceinline__ void st16(uint8_t *base, uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
+{
+    *reinterpret_cast<uint4 *>(base + off) = make_uint4(a, b, c, d);
+}
+
+// ---- weights: shared-memory operand images with the biases folded in -------------------
+
+template <int C>
+__device__ __forceinline__ void stage_weights_tc(Smem<C> &w, const NetView &net, int tid)
+{
+    using K = Cfg<C>;
+    constexpr int n1 = 64 * K::XC, n2 = 64 * kHC, n3 = 16 * kHC;
+    for (int i = tid; i < n1 + n2 + n3; i += kThreadsTC) {
+        int o, j, kch, nin, pad, which;
+        if (i < n1) {
+            o = i / K::XC, j = i % K::XC, kch = K::XC, nin = K::kBias1, pad = 32, which = 0;
+        } else if (i < n1 + n2) {
+            o = (i - n1) / kHC, j = (i - n1) % kHC, kch = kHC, nin = 64, pad = 64, which = 1;
+        } else {
+            o = (i - n1 - n2) / kHC, j = (i - n1 - n2) % kHC, kch = kHC, nin = 64, pad = 64, which = 2;
+        }
+        const __half *src = net.W[which], *bias = net.b[which];
+        uint8_t *dst = which == 0 ? w.W1 : (which == 1 ? w.W2 : w.W3);
+        const bool row_ok = which != 2 || o < net.cout;
+        uint32_t v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            __half x[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                const int in = 8 * j + 2 * e + q;
+                x[q] = __float2half(0.f);
+                if (row_ok) {
+                    if (in < nin) x[q] = src[o * pad + in];
+                    else if (in == nin) x[q] = bias[o];
+                }
+            }
+            v[e] = (uint32_t)__half_as_ushort(x[0]) | ((uint32_t)__half_as_ushort(x[1]) << 16);
+        }
+        st16(dst, umma::cm_offset(o, 8 * j, kch), v[0], v[1], v[2], v[3]);
+    }
+}
+
+// ---- footprint windows of a tile (for the latent-gradient sweep) ------------------------
+
+// Per-warp min / max of the footprint bases per lattice column (lanes L and L + 16 share a
+// column) and per lattice row (half-warp).
+__device__ __forceinline__ void extents_partial(int32_t (&part)[4][4][kTileW], int bx, int by, bool valid, int ws,
+                                                int lane)
+{
+    int cmin = valid ? bx : INT_MAX, cmax = valid ? bx : INT_MIN;
+    cmin = min(cmin, __shfl_xor_sync(0xffffffffu, cmin, 16));
+    cmax = max(cmax, __shfl_xor_sync(0xffffffffu, cmax, 16));
+    int rmin = valid ? by : INT_MAX, rmax = valid ? by : INT_MIN;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+        rmin = min(rmin, __shfl_xor_sync(0xffffffffu, rmin, o));
+        rmax = max(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
+    }
+    if (lane < 16) {
+        part[0][ws][lane] = cmin;
+        part[1][ws][lane] = cmax;
+    }
+    if ((lane & 15) == 0) {
+        part[2][ws][lane >> 4] = rmin;
+        part[3][ws][lane >> 4] = rmax;
+    }
+}
+
+// One warp: column / row extents of grid gi over the 4 warp partials, window origin and
+// width, candidate lattice-column range of every window column.
+template <int C>
+__device__ __forceinline__ void finalize_window_tc(Smem<C> &s, int gi, int lane)
+{
+    int lo_v = INT_MAX, hi_v = INT_MIN;
+    if (lane < 16) {
+        for (int w = 0; w < 4; ++w) {
+            lo_v = min(lo_v, s.part[gi][0][w][lane]);
+            hi_v = max(hi_v, s.part[gi][1][w][lane]);
+        }
+        s.colext[gi][0][lane] = lo_v;
+        s.colext[gi][1][lane] = hi_v;
+    } else if (lane < 16 + kTileH) {
+        const int e = lane - 16, w = e >> 1, half = e & 1;
+        lo_v = s.part[gi][2][w][half];
+        hi_v = s.part[gi][3][w][half];
+        s.rowmin[gi][e] = lo_v;
+    }
+    const bool narrow = lo_v == INT_MAX || (long long)hi_v - lo_v <= 1;
+    const bool all_narrow = __all_sync(0xffffffffu, narrow);
+    int mn = lo_v, mx = hi_v;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+        mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    const int cmin = __shfl_sync(0xffffffffu, mn, 0), cmax = __shfl_sync(0xffffffffu, mx, 0);
+    const int rmin = __shfl_sync(0xffffffffu, mn, 16), rmax = __shfl_sync(0xffffffffu, mx, 16);
+    __syncwarp();
+    Window &W = s.win[gi];
+    const bool nonempty = cmin <= cmax && rmin <= rmax;
+    const long long ww = nonempty ? (long long)cmax - cmin + 4 : 0;
+    const bool ok = nonempty && ww <= kMaxWinW && all_narrow;
+    if (lane == 0) {
+        W.x0 = cmin - 1;
+        W.w = ok ? (int)ww : 0;
+        W.ok = ok;
+    }
+    int span = 0;
+    if (ok) {
+        for (int idx = lane; idx < (int)ww; idx += 32) {
+            const int tx = cmin - 1 + idx;
+            int lo = kTileW, hi = -1;
+            for (int c = 0; c < kTileW; ++c) {
+                if (s.colext[gi][0][c] <= tx + 1 && s.colext[gi][1][c] >= tx - 2) {
+                    lo = min(lo, c);
+                    hi = max(hi, c);
+                }
+            }
+            W.cand_x[idx] = lo | (hi << 16);
+            span = max(span, hi - lo + 1);
+        }
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) span = max(span, __shfl_xor_sync(0xffffffffu, span, o));
+    if (lane == 0) W.span = span;
+}
+
+// ---- latent-gradient column sweep (see nt_train.cu for the derivation) -------------------
+
+template <int C>
+__device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, int ty, const float (&row)[C])
+{
+    bool any = false;
+#pragma unroll
+    for (int c = 0; c < C; ++c) any |= row[c] != 0.f;
+    if (!any) return;
+    const int gw = p.gw[gi], gh = p.gh[gi];
+    const float sc = p.inv_num_samples;
+    float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)wrap_coord(ty, gh) * gw + wrap_coord(tx, gw)) * C);
+#pragma unroll
+    for (int q = 0; q < C / 4; ++q)
+        atomicAdd(dst + q, make_float4(row[4 * q] * sc, row[4 * q + 1] * sc, row[4 * q + 2] * sc, row[4 * q + 3] * sc));
+}
+
+template <int C, int L>
+__device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p, int r)
+{
+    constexpr int kRows = 2, kChunks = kTileH / kRows, DXS = Cfg<C>::DXS;
+    const float *dx = reinterpret_cast<const float *>(s.H2);
+    const int nt0 = s.win[0].w * kChunks;
+    const int ntot = nt0 + s.win[1].w * kChunks;
+    for (int k = r; k < ntot; k += kThreadsTC) {
+        const int gi = k < nt0 ? 0 : 1;
+        const Window &W = s.win[gi];
+        const int kk = gi ? k - nt0 : k;
+        const int chunk = kk / W.w, lx = kk % W.w;
+        const int tx = W.x0 + lx;
+        const int cx = W.cand_x[lx];
+        const int lo = cx & 0xffff, hi = cx >> 16;
+        if (hi < lo) continue;
+        float R[5][C];
+#pragma unroll
+        for (int m = 0; m < 5; ++m)
+#pragma unroll
+            for (int c = 0; c < C; ++c) R[m][c] = 0.f;
+        int fy_cur = INT_MIN;
+#pragma unroll
+        for (int rr = 0; rr < kRows; ++rr) {
+            const int cj = chunk * kRows + rr;
+            const int rmin = s.rowmin[gi][cj];
+            if (rmin == INT_MAX) continue;
+            const int fy = rmin - 1;
+            if (fy_cur == INT_MIN) fy_cur = fy;
+            while (fy > fy_cur) {
+                flush_row<C>(p, gi, tx, fy_cur, R[0]);
+#pragma unroll
+                for (int m = 0; m < 4; ++m)
+#pragma unroll
+                    for (int c = 0; c < C; ++c) R[m][c] = R[m + 1][c];
+#pragma unroll
+                for (int c = 0; c < C; ++c) R[4][c] = 0.f;
+                ++fy_cur;
+            }
+#pragma unroll
+            for (int b = 0; b < L; ++b) {
+                const int ci = min(lo + b, kTileW - 1);
+                const bool inr = lo + b <= hi;
+                const int sidx = cj * kTileW + ci;
+                const short2 bs = s.base[gi][sidx];
+                const int kx = tx - bs.x + 1;
+                const float wxv = (inr && (unsigned)kx <= 3u) ? s.wts[gi][sidx][kx & 3] : 0.f;
+                const float4 wy = *reinterpret_cast<const float4 *>(&s.wts[gi][sidx][4]);
+                const bool e1 = bs.y - 1 - fy != 0;
+                float wxd[C];
+                const float4 *d4 = reinterpret_cast<const float4 *>(dx + sidx * DXS + gi * C);
+#pragma unroll
+                for (int q = 0; q < C / 4; ++q) {
+                    const float4 d = d4[q];
+                    wxd[4 * q + 0] = wxv * d.x;
+                    wxd[4 * q + 1] = wxv * d.y;
+                    wxd[4 * q + 2] = wxv * d.z;
+                    wxd[4 * q + 3] = wxv * d.w;
+                }
+                const float wyv[5] = {e1 ? 0.f : wy.x, e1 ? wy.x : wy.y, e1 ? wy.y : wy.z, e1 ? wy.z : wy.w,
+                                      e1 ? wy.w : 0.f};
+#pragma unroll
+                for (int m = 0; m < 5; ++m)
+#pragma unroll
+                    for (int c = 0; c < C; ++c) R[m][c] = fmaf(wyv[m], wxd[c], R[m][c]);
+            }
+        }
+        if (fy_cur == INT_MIN) continue;
+#pragma unroll
+        for (int m = 0; m < 5; ++m) flush_row<C>(p, gi, tx, fy_cur + m, R[m]);
+    }
+}
+
+// Per-sample, per-tap vector atomics (windows the sweep does not handle).
+template <int C>
+__device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLaunch &p, int gi, int r)
+{
+    const float *dxr = reinterpret_cast<const float *>(s.H2) + r * Cfg<C>::DXS + gi * C;
+    const int gw = p.gw[gi], gh = p.gh[gi];
+    const short2 b = s.base[gi][r];
+    const float scale = p.inv_num_samples;
+    for (int j = 0; j < 4; ++j) {
+        const int yy = wrap_coord(b.y - 1 + j, gh);
+        for (int i = 0; i < 4; ++i) {
+            const int xx = wrap_coord(b.x - 1 + i, gw);
+            const float wgt = s.wts[gi][r][i] * s.wts[gi][r][4 + j] * scale;
+            float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)yy * gw + xx) * C);
+#pragma unroll
+            for (int q = 0; q < C / 4; ++q)
+                atomicAdd(dst + q, make_float4(wgt * dxr[4 * q], wgt * dxr[4 * q + 1], wgt * dxr[4 * q + 2],
+                                               wgt * dxr[4 * q + 3]));
+        }
+    }
+}
+
+// ---- epilogue helpers -------------------------------------------------------------------
+
+// TMEM row (32 columns from taddr) -> relu -> fp16 -> 4 chunks of an H row.
+__device__ __forceinline__ void relu_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
+{
+    uint32_t v[32];
+    umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
+    umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+    umma::wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            h[e] = pack_half2(fmaxf(__uint_as_float(v[8 * q + 2 * e]), 0.f),
+                              fmaxf(__uint_as_float(v[8 * q + 2 * e + 1]), 0.f));
+        st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
+    }
+}
+
+// TMEM row (32 columns) masked by the ReLU of the activation row stored at the same place
+// in H, rounded to fp16 and written over it.
+__device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
+{
+    uint32_t v[32];
+    umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
+    umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+    uint4 a[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) a[q] = *reinterpret_cast<const uint4 *>(H + umma::cm_offset(r, 8 * (chunk0 + q), kHC));
+    umma::wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t aw[4] = {a[q].x, a[q].y, a[q].z, a[q].w};
+        uint32_t h[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __half2 act = *reinterpret_cast<const __half2 *>(&aw[e]);
+            const float g0 = __low2float(act) > 0.f ? __uint_as_float(v[8 * q + 2 * e]) : 0.f;
+            const float g1 = __high2float(act) > 0.f ? __uint_as_float(v[8 * q + 2 * e + 1]) : 0.f;
+            h[e] = pack_half2(g0, g1);
+        }
+        st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
+    }
+}
+
+// ---- tensor-core products -------------------------------------------------------------------
+
+// Descriptor whose start address advances by `bytes` (the address field holds addr >> 4 and
+// every operand lies below 256 KB, so the field never carries into its neighbours).
+__device__ __forceinline__ uint64_t dadv(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
+
+template <int C>
+struct Descs {
+    uint64_t x, h1, h2, dy, w1, w2, w3;  // K-major views (LBO 128)
+    uint64_t x_mn, h1_mn, h2_mn, dy_mn, w1_mn, w2_mn, w3_mn;  // MN-major views
+};
+
+template <int C>
+__device__ __forceinline__ Descs<C> make_descs(const Smem<C> &s)
+{
+    using K = Cfg<C>;
+    using umma::desc;
+    constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
+    Descs<C> d;
+    d.x = desc(smem_addr(s.X), 128, XG);
+    d.h1 = desc(smem_addr(s.H1), 128, HG);
+    d.h2 = desc(smem_addr(s.H2), 128, HG);
+    d.dy = desc(smem_addr(s.DY), 128, 256);
+    d.w1 = desc(smem_addr(s.W1), 128, XG);
+    d.w2 = desc(smem_addr(s.W2), 128, HG);
+    d.w3 = desc(smem_addr(s.W3), 128, HG);
+    d.x_mn = desc(smem_addr(s.X), XG, 128);
+    d.h1_mn = desc(smem_addr(s.H1), HG, 128);
+    d.h2_mn = desc(smem_addr(s.H2), HG, 128);
+    d.dy_mn = desc(smem_addr(s.DY), 256, 128);
+    d.w1_mn = desc(smem_addr(s.W1), XG, 128);
+    d.w2_mn = desc(smem_addr(s.W2), HG, 128);
+    d.w3_mn = desc(smem_addr(s.W3), HG, 128);
+    return d;
+}
+
+// Issue the products of one stage (thread 0 only) and commit them to `done`.
+template <int C>
+__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done)
+{
+    using K = Cfg<C>;
+    using umma::idesc_f16;
+    using umma::mma_f16;
+    constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
+    const uint32_t R = tmem + kColTile;
+    const uint32_t acc0 = first ? 0u : 1u;  // the first tile of the CTA starts the gradient sums
+    switch (stage) {
+    case 0:  // F1
+#pragma unroll
+        for (int ks = 0; ks < K::XC / 2; ++ks)
+            mma_f16(R, dadv(d.x, ks * 256), dadv(d.w1, ks * 256), idesc_f16(128, 64, 0, 0), ks > 0);
+        break;
+    case 1:  // F2
+#pragma unroll
+        for (int ks = 0; ks < kHC / 2; ++ks)
+            mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w2, ks * 256), idesc_f16(128, 64, 0, 0), ks > 0);
+        break;
+    case 2:  // F3
+#pragma unroll
+        for (int ks = 0; ks < kHC / 2; ++ks)
+            mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w3, ks * 256), idesc_f16(128, 16, 0, 0), ks > 0);
+        break;
+    case 3:  // B3: dH2 = dY W3; dW3^T += H2e^T dY
+        mma_f16(R, d.dy, d.w3_mn, idesc_f16(128, 64, 0, 1), 0);
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(tmem + kColW3, dadv(d.h2_mn, ks * 2 * HG), dadv(d.dy_mn, ks * 512), idesc_f16(128, 16, 1, 1),
+                    ks > 0 ? 1u : acc0);
+        break;
+    case 4:  // B2: dH1 = dZ2 W2; dW2 += dZ2^T H1e
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+            mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w2_mn, ks * 2 * HG), idesc_f16(128, 64, 0, 1), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
+                    ks > 0 ? 1u : acc0);
+        break;
+    default:  // B1: dX = dZ1 W1; dW1 += dZ1^T X
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+            mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w1_mn, ks * 2 * XG), idesc_f16(128, K::NX, 0, 1), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(tmem + kColW1, dadv(d.h1_mn, ks * 2 * HG), dadv(d.x_mn, ks * 2 * XG), idesc_f16(64, K::XW, 1, 1),
+                    ks > 0 ? 1u : acc0);
+        break;
+    }
+    umma::commit(done);
+}
+
+// Stage boundary: the operands written since the last one become visible to the tensor
+// core, the CTA agrees on failure, thread 0 issues the stage, every thread waits for it.
+// Returns false (the same answer on every thread) when the CTA must stop; a wait that
+// times out is recorded and reaches the other threads at the next barrier.
+template <int C>
+__device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done,
+                                          uint32_t &ph, bool &failed, int tid)
+{
+    umma::fence_async_smem();
+    umma::fence_before();
+    if (__syncthreads_or(failed)) {
+        failed = true;
+        return false;
+    }
+    umma::fence_after();
+    if (tid == 0) issue_stage<C>(stage, d, tmem, first, done);
+    if (!umma::mbar_wait(done, ph, kSpinLimit)) {
+        failed = true;
+        atomicOr(&g_device_status, 1u);
+        umma::mbar_wait(done, ph, kSpinLimit);  // one more bounded wait for the products in flight
+    }
+    ph ^= 1u;
+    umma::fence_after();
+    return true;
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------
+
+template <int C>
+__global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaunch p)
+{
+    using K = Cfg<C>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Smem<C> &s = *reinterpret_cast<Smem<C> *>(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r = tid & (kTileN - 1), half = tid >> 7;  // sample, role
+
+    stage_weights_tc<C>(s, p.net, tid);
+    if (warp == 0) umma::alloc(smem_addr(&s.tmem_base), kTmemCols);
+    if (tid == 0) {
+        umma::mbar_init(smem_addr(&s.done), 1);
+        umma::mbar_fence_init();
+    }
+    umma::fence_async_smem();
+    umma::fence_before();
+    __syncthreads();
+    umma::fence_after();
+    const uint32_t tmem = s.tmem_base;
+    const uint32_t Rl = tmem + kColTile + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's lanes
+    const uint32_t done = smem_addr(&s.done);
+    const Descs<C> d = make_descs<C>(s);
+    const int ntiles = p.tiles_x * p.tiles_y;
+    const int cout = p.net.cout;
+    uint32_t ph = 0;
+    bool failed = false, first = true;
+    float sse = 0.f;
+
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int ix = (tile % p.tiles_x) * kTileW + (r & (kTileW - 1));
+        const int iy = (tile / p.tiles_x) * kTileH + (r >> 4);
+        const bool valid = ix < p.sampler.lattice_w && iy < p.sampler.lattice_h;
+        float tgt[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) tgt[k] = 0.f;
+
+        // ---- gather: half 0 = both latent grids (+ footprints), half 1 = target + posenc --
+        {
+            float u = 0.f, v = 0.f;
+            if (valid) sample_uv(p.sampler, ix, iy, u, v);
+            if (half == 0) {
+                uint32_t packed[K::LC * 4];
+#pragma unroll
+                for (int k = 0; k < K::LC * 4; ++k) packed[k] = 0u;
+#pragma unroll
+                for (int gi = 0; gi < 2; ++gi) {
+                    Footprint fp;
+                    footprint(u, v, p.gw[gi], p.gh[gi], fp);
+                    if (valid) {
+                        float f[C];
+                        gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
+#pragma unroll
+                        for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
+                    }
+                    if (!p.finalize) {
+                        s.base[gi][r] = make_short2((short)fp.bx, (short)fp.by);
+                        float4 *wr = reinterpret_cast<float4 *>(s.wts[gi][r]);
+                        wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
+                        wr[1] = make_float4(fp.wy[0], fp.wy[1], fp.wy[2], fp.wy[3]);
+                        extents_partial(s.part[gi], fp.bx, fp.by, valid, warp, lane);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < K::LC; ++j)
+                    st16(s.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                         packed[4 * j + 3]);
+            } else {
+                uint32_t packed[4] = {0u, 0u, 0u, 0u};
+                if (valid) {
+                    float pe[8];
+                    posenc(u, v, pe);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) packed[k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
+                    Footprint fp;
+                    footprint(u, v, p.sampler.image_w, p.sampler.image_h, fp);
+                    gather_target(p.target, p.sampler.image_w, cout, fp, tgt);
+                }
+                static_assert(K::XC == K::LC + 2 || K::XC == K::LC + 3, "X row: latents, posenc, 1, [0]");
+                st16(s.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
+                st16(s.X, umma::cm_offset(r, 8 * (K::LC + 1), K::XC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+                if constexpr (K::XC > K::LC + 2)
+                    st16(s.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
+            }
+        }
+        if (!run_stage<C>(0, d, tmem, first, done, ph, failed, tid)) break;  // F1
+        // the window finalisation overlaps F1 (the barrier above published the partials)
+        if (!p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
+
+        // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
+        relu_store32(Rl + 32 * half, s.H1, r, 4 * half);
+        if (half)
+            st16(s.H1, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+        else
+            st16(s.H1, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
+        if (!run_stage<C>(1, d, tmem, first, done, ph, failed, tid)) break;  // F2
+
+        // ---- E2: H2e ------------------------------------------------------------------------
+        relu_store32(Rl + 32 * half, s.H2, r, 4 * half);
+        if (half)
+            st16(s.H2, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+        else
+            st16(s.H2, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
+        if (!run_stage<C>(2, d, tmem, first, done, ph, failed, tid)) break;  // F3
+
+        // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
+        if (half) {
+            uint32_t v[16];
+            umma::ld16(Rl, v);
+            umma::wait_ld();
+            uint32_t out[8];
+#pragma unroll
+            for (int c2 = 0; c2 < 8; ++c2) {
+                float dd[2] = {0.f, 0.f};
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int c = 2 * c2 + e;
+                    if (valid && c < cout) {
+                        const float y = round_half(__uint_as_float(v[c]));
+                        const float err = y - tgt[c];
+                        sse = fmaf(p.cw[c] * err, err, sse);
+                        dd[e] = 2.f * p.cw[c] * err;
+                    }
+                }
+                out[c2] = pack_half2(dd[0], dd[1]);
+            }
+            st16(s.DY, umma::cm_offset(r, 0, 2), out[0], out[1], out[2], out[3]);
+            st16(s.DY, umma::cm_offset(r, 8, 2), out[4], out[5], out[6], out[7]);
+        }
+        if (!run_stage<C>(3, d, tmem, first, done, ph, failed, tid)) break;  // B3
+
+        // ---- E4: dZ2 = dH2 * [H2 > 0] (in place of H2) -----------------------------------
+        mask_store32(Rl + 32 * half, s.H2, r, 4 * half);
+        if (!run_stage<C>(4, d, tmem, first, done, ph, failed, tid)) break;  // B2
+
+        // ---- E5: dZ1 = dH1 * [H1 > 0] (in place of H1) -----------------------------------
+        mask_store32(Rl + 32 * half, s.H1, r, 4 * half);
+        if (!run_stage<C>(5, d, tmem, first, done, ph, failed, tid)) break;  // B1
+
+        // ---- E6: dX -> shared (fp32 rows over the dead H2 tile) -> latent gradients ------
+        if (!p.finalize) {
+            {
+                // dX columns [half * C, half * C + C): the latents of grid `half`
+                uint32_t v[32];
+                umma::ld16(Rl, *reinterpret_cast<uint32_t(*)[16]>(v));
+                if constexpr (K::NX > 16) umma::ld16(Rl + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+                umma::wait_ld();
+                float *dxr = reinterpret_cast<float *>(s.H2) + r * K::DXS + half * C;
+#pragma unroll
+                for (int q = 0; q < C / 4; ++q) {
+                    float f[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        f[e] = __uint_as_float(half ? v[C + 4 * q + e] : v[4 * q + e]);
+                    *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(f[0], f[1], f[2], f[3]);
+                }
+            }
+            if (__syncthreads_or(failed)) {
+                failed = true;
+                break;
+            }
+            const bool both = s.win[0].ok && s.win[1].ok;
+            const int span = max(s.win[0].span, s.win[1].span);
+            if (both && span <= 5) {
+                sweep_tc<C, 5>(s, p, tid);
+            } else if (both && span <= 10) {
+                sweep_tc<C, 10>(s, p, tid);
+            } else if (valid) {
+                scatter_taps_tc<C>(s, p, half, r);
+            }
+        }
+        first = false;
+        umma::fence_before();
+        // the next tile overwrites the footprints, the windows, X and H
+        if (__syncthreads_or(failed)) {
+            failed = true;
+            break;
+        }
+    }
+
+    // every product of this CTA (the weight-gradient accumulators included) has completed:
+    // each stage was waited for before the loop moved on
+
+    // ---- flush the weight / bias gradients (x 1 / num_samples) --------------------------
+    const float sc = p.inv_num_samples;
+    if (!first && !failed) {
+        const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
+        if (half == 0) {
+            // dW1 (M = 64: row 16 (warp & 3) + lane for lane < 16) and dW3^T (M = 128)
+            const int o = 16 * (warp & 3) + lane;
+#pragma unroll
+            for (int c0 = 0; c0 < K::XW; c0 += 16) {
+                uint32_t v[16];
+                umma::ld16(tmem + kColW1 + lanes + c0, v);
+                umma::wait_ld();
+                if (lane < 16) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int in = c0 + 4 * q;
+                        if (in + 3 < K::kBias1)
+                            atomicAdd(reinterpret_cast<float4 *>(p.gW[0] + o * 32 + in),
+                                      make_float4(__uint_as_float(v[4 * q]) * sc, __uint_as_float(v[4 * q + 1]) * sc,
+                                                  __uint_as_float(v[4 * q + 2]) * sc,
+                                                  __uint_as_float(v[4 * q + 3]) * sc));
+                        else if (in == K::kBias1)
+                            atomicAdd(p.gb[0] + o, __uint_as_float(v[4 * q]) * sc);
+                    }
+                }
+            }
+            const int f = 32 * (warp & 3) + lane;  // hidden feature of dW3^T
+            uint32_t v[16];
+            umma::ld16(tmem + kColW3 + lanes, v);
+            umma::wait_ld();
+#pragma unroll
+            for (int o3 = 0; o3 < 16; ++o3) {
+                if (o3 >= cout) continue;
+                const float g = __uint_as_float(v[o3]) * sc;
+                if (f < 64) atomicAdd(p.gW[2] + o3 * 64 + f, g);
+                else if (f == 64) atomicAdd(p.gb[2] + o3, g);
+            }
+        } else {  // dW2 (M = 64, 72 columns)
+            const int o = 16 * (warp & 3) + lane;
+#pragma unroll
+            for (int c0 = 0; c0 < 72; c0 += 8) {
+                uint32_t v[8];
+                umma::ld8(tmem + kColW2 + lanes + c0, v);
+                umma::wait_ld();
+                if (lane < 16) {
+                    if (c0 < 64) {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q)
+                            atomicAdd(reinterpret_cast<float4 *>(p.gW[1] + o * 64 + c0 + 4 * q),
+                                      make_float4(__uint_as_float(v[4 * q]) * sc, __uint_as_float(v[4 * q + 1]) * sc,
+                                                  __uint_as_float(v[4 * q + 2]) * sc,
+                                                  __uint_as_float(v[4 * q + 3]) * sc));
+                    } else {
+                        atomicAdd(p.gb[1] + o, __uint_as_float(v[0]) * sc);
+                    }
+                }
+            }
+        }
+    }
+    if (p.loss_accum) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sse += __shfl_xor_sync(0xffffffffu, sse, o);
+        if (lane == 0) s.red[warp] = sse;
+    }
+    umma::fence_before();
+    __syncthreads();
+    if (p.loss_accum && tid == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < kThreadsTC / 32; ++w) tot += s.red[w];
+        atomicAdd(p.loss_accum, tot);
+    }
+    if (warp == 0) {
+        umma::fence_after();
+        umma::dealloc(tmem, kTmemCols);
+    }
+}
+
+template <int C>
+static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
+{
+    const size_t smem = sizeof(Smem<C>);
+    static_assert(sizeof(Smem<C>) <= 113 * 1024, "two CTAs per SM");
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C>), smem);
+    if (e != cudaSuccess) return e;
+    p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
+    p.tiles_y = (p.sampler.lattice_h + kTileH - 1) / kTileH;
+    const int ntiles = p.tiles_x * p.tiles_y;
+    const int cap = 2 * sm_count();
+    const int grid = ntiles < cap ? ntiles : cap;
+    train_tc_kernel<C><<<grid, kThreadsTC, smem, stream>>>(p);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace tc
+
+cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream)
+{
+    if (channels == 8) return tc::launch_t<8>(p, stream);
+    if (channels == 12) return tc::launch_t<12>(p, stream);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace nt
+
+extern "C" nt_status nt_read_device_status(uint32_t *status, int32_t clear)
+{
+    if (!status) return NT_ERR_INVALID_ARG;
+    if (cudaMemcpyFromSymbol(status, nt::g_device_status, sizeof(uint32_t)) != cudaSuccess) return NT_ERR_CUDA;
+    if (clear) {
+        const uint32_t zero = 0;
+        if (cudaMemcpyToSymbol(nt::g_device_status, &zero, sizeof(uint32_t)) != cudaSuccess) return NT_ERR_CUDA;
+    }
+    return NT_OK;
+}

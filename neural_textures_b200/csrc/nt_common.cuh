@@ -163,50 +163,63 @@ __device__ __forceinline__ void footprint(float u, float v, int32_t w, int32_t h
     }
 }
 
-// Catmull-Rom gather of C channels (C = 8 or 12; channel-interleaved fp16 grid), fp32
-// accumulation: row sums first, then the weighted sum of rows (same order as the oracle).
+// Packed fp32 fused multiply-add (sm_100 fma.rn.f32x2): per lane exactly fmaf(a, b, c).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
+{
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(r)
+        : "l"(*reinterpret_cast<unsigned long long *>(&a)), "l"(*reinterpret_cast<unsigned long long *>(&b)),
+          "l"(*reinterpret_cast<unsigned long long *>(&c)));
+    return *reinterpret_cast<float2 *>(&r);
+}
+
+// Catmull-Rom gather of C channels (C = 4, 8, 12 or 16; channel-interleaved fp16 grid),
+// fp32 accumulation: row sums first, then the weighted sum of rows (same order as the
+// oracle).  Channel pairs go through the packed fp32 FMA, which rounds each lane like fmaf.
 template <int C>
 __device__ __forceinline__ void gather_cr(const __half *__restrict__ grid, int32_t w,
                                           const Footprint &fp, float out[C])
 {
     static_assert(C % 4 == 0, "channel count must be a multiple of 4");
+    float2 acc[C / 2];
 #pragma unroll
-    for (int k = 0; k < C; ++k) out[k] = 0.f;
+    for (int k = 0; k < C / 2; ++k) acc[k] = make_float2(0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        float row[C];
+        float2 row[C / 2];
 #pragma unroll
-        for (int k = 0; k < C; ++k) row[k] = 0.f;
+        for (int k = 0; k < C / 2; ++k) row[k] = make_float2(0.f, 0.f);
         const __half *rp = grid + (size_t)fp.ys[j] * (size_t)w * C;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const __half *tp = rp + (size_t)fp.xs[i] * C;
+            const float2 wx2 = make_float2(fp.wx[i], fp.wx[i]);
             if constexpr (C % 8 == 0) {
 #pragma unroll
                 for (int q = 0; q < C / 8; ++q) {
                     const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(tp) + q);
                     const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = unpack_half2(r[e]);
-                        row[q * 8 + 2 * e] = fmaf(fp.wx[i], f.x, row[q * 8 + 2 * e]);
-                        row[q * 8 + 2 * e + 1] = fmaf(fp.wx[i], f.y, row[q * 8 + 2 * e + 1]);
-                    }
+                    for (int e = 0; e < 4; ++e) row[q * 4 + e] = ffma2(wx2, unpack_half2(r[e]), row[q * 4 + e]);
                 }
             } else {
 #pragma unroll
                 for (int q = 0; q < C / 4; ++q) {
                     const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(tp) + q);
-                    const float2 a = unpack_half2(raw.x), b = unpack_half2(raw.y);
-                    row[q * 4 + 0] = fmaf(fp.wx[i], a.x, row[q * 4 + 0]);
-                    row[q * 4 + 1] = fmaf(fp.wx[i], a.y, row[q * 4 + 1]);
-                    row[q * 4 + 2] = fmaf(fp.wx[i], b.x, row[q * 4 + 2]);
-                    row[q * 4 + 3] = fmaf(fp.wx[i], b.y, row[q * 4 + 3]);
+                    row[q * 2 + 0] = ffma2(wx2, unpack_half2(raw.x), row[q * 2 + 0]);
+                    row[q * 2 + 1] = ffma2(wx2, unpack_half2(raw.y), row[q * 2 + 1]);
                 }
             }
         }
+        const float2 wy2 = make_float2(fp.wy[j], fp.wy[j]);
 #pragma unroll
-        for (int k = 0; k < C; ++k) out[k] = fmaf(fp.wy[j], row[k], out[k]);
+        for (int k = 0; k < C / 2; ++k) acc[k] = ffma2(wy2, row[k], acc[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < C / 2; ++k) {
+        out[2 * k] = acc[k].x;
+        out[2 * k + 1] = acc[k].y;
     }
 }
 

@@ -41,6 +41,7 @@
 // nt_read_device_status); the CTA agrees on it at its next barrier, stops issuing work,
 // waits (bounded) for the products in flight and releases its tensor memory.
 #include <climits>
+#include <cmath>
 
 #include "nt_kernels.cuh"
 #include "nt_mma.cuh"
@@ -71,8 +72,14 @@ struct Cfg {
     static constexpr int DXS = 2 * C + 4;                    // fp32 dX row stride (floats)
 };
 
+// Tensor-core latent scatter: per grid, the window is at most sc_w(g) texels wide and
+// sc_h(g) texels high (else the tile takes the column sweep).
+__host__ __device__ constexpr int sc_w(int g) { return g ? 16 : 32; }
+__host__ __device__ constexpr int sc_h(int g) { return g ? 8 : 12; }
+
 struct Window {
     int32_t x0, w, span, ok;
+    int32_t y0, h, tc;  // window rows; tc: fits the tensor-core scatter
     int32_t cand_x[kMaxWinW];  // lo | hi << 16 of the candidate lattice columns
 };
 
@@ -81,10 +88,24 @@ struct Smem {
     alignas(128) uint8_t W1[64 * Cfg<C>::XW * 2];  // [out][in | b1 | 0]
     alignas(128) uint8_t W2[64 * kHW * 2];         // [out][in | b2 | 0]
     alignas(128) uint8_t W3[16 * kHW * 2];         // [out (zero rows past cout)][in | b3 | 0]
-    alignas(128) uint8_t X[kTileN * Cfg<C>::XW * 2];
-    alignas(128) uint8_t H1[kTileN * kHW * 2];  // H1e, then dZ1 (in place)
-    alignas(128) uint8_t H2[kTileN * kHW * 2];  // H2e, then dZ2 (in place), then dX (fp32)
-    alignas(128) uint8_t DY[kTileN * 16 * 2];   // follows H2: the M = 128 read of H2 runs 768 B past it
+    union {
+        struct {  // the network's operand tiles
+            alignas(128) uint8_t X[kTileN * Cfg<C>::XW * 2];
+            alignas(128) uint8_t H1[kTileN * kHW * 2];  // H1e, then dZ1 (in place)
+            alignas(128) uint8_t H2[kTileN * kHW * 2];  // H2e, then dZ2 (in place), then dX (fp32)
+            alignas(128) uint8_t DY[kTileN * 16 * 2];   // follows H2: the M = 128 read of H2 runs 768 B past it
+        } m;
+        struct {  // latent scatter operands: Q_g = wy dX over window rows, A_g = wx over window columns
+            alignas(128) uint8_t Q0[kTileN * sc_h(0) * 16];  // followed by Q1: the M = 128 read runs 512 B past it
+            alignas(128) uint8_t Q1[kTileN * sc_h(1) * 16];
+            alignas(128) uint8_t A0[kTileN * sc_w(0) * 2];
+            alignas(128) uint8_t A1[kTileN * sc_w(1) * 2];
+        } q;
+        struct {  // the scattered window sums, fp32 [row][column (+1 pad)][channel]
+            float g0[sc_h(0) * (sc_w(0) + 1) * 8];
+            float g1[sc_h(1) * (sc_w(1) + 1) * 8];
+        } f;
+    } t;
     short2 base[2][kTileN];
     float wts[2][kTileN][8];
     int32_t part[2][4][4][kTileW];  // [grid][col min, col max, row min, row max][warp][index]
@@ -166,7 +187,7 @@ __device__ __forceinline__ void extents_partial(int32_t (&part)[4][4][kTileW], i
 }
 
 // One warp: column / row extents of grid gi over the 4 warp partials, window origin and
-// width, candidate lattice-column range of every window column.
+// size, and whether the window suits the column sweep / the tensor-core scatter.
 template <int C>
 __device__ __forceinline__ void finalize_window_tc(Smem<C> &s, int gi, int lane)
 {
@@ -199,15 +220,27 @@ __device__ __forceinline__ void finalize_window_tc(Smem<C> &s, int gi, int lane)
     const bool nonempty = cmin <= cmax && rmin <= rmax;
     const long long ww = nonempty ? (long long)cmax - cmin + 4 : 0;
     const bool ok = nonempty && ww <= kMaxWinW && all_narrow;
+    const long long wh = nonempty ? (long long)rmax - rmin + 4 : 0;
     if (lane == 0) {
         W.x0 = cmin - 1;
-        W.w = ok ? (int)ww : 0;
+        W.w = (int)ww;
         W.ok = ok;
+        W.y0 = rmin - 1;
+        W.h = nonempty ? (int)wh : 0;
+        W.tc = nonempty && ww <= sc_w(gi) && wh <= sc_h(gi);
     }
+}
+
+// One warp: candidate lattice-column range of every window column of grid gi and the
+// longest range (only the column sweep needs them).
+template <int C>
+__device__ __forceinline__ void window_cands(Smem<C> &s, int gi, int lane)
+{
+    Window &W = s.win[gi];
     int span = 0;
-    if (ok) {
-        for (int idx = lane; idx < (int)ww; idx += 32) {
-            const int tx = cmin - 1 + idx;
+    if (W.ok) {
+        for (int idx = lane; idx < W.w; idx += 32) {
+            const int tx = W.x0 + idx;
             int lo = kTileW, hi = -1;
             for (int c = 0; c < kTileW; ++c) {
                 if (s.colext[gi][0][c] <= tx + 1 && s.colext[gi][1][c] >= tx - 2) {
@@ -245,7 +278,7 @@ template <int C, int L>
 __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p, int r)
 {
     constexpr int kRows = 2, kChunks = kTileH / kRows, DXS = Cfg<C>::DXS;
-    const float *dx = reinterpret_cast<const float *>(s.H2);
+    const float *dx = reinterpret_cast<const float *>(s.t.m.H2);
     const int nt0 = s.win[0].w * kChunks;
     const int ntot = nt0 + s.win[1].w * kChunks;
     for (int k = r; k < ntot; k += kThreadsTC) {
@@ -318,7 +351,7 @@ __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p,
 template <int C>
 __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLaunch &p, int gi, int r)
 {
-    const float *dxr = reinterpret_cast<const float *>(s.H2) + r * Cfg<C>::DXS + gi * C;
+    const float *dxr = reinterpret_cast<const float *>(s.t.m.H2) + r * Cfg<C>::DXS + gi * C;
     const int gw = p.gw[gi], gh = p.gh[gi];
     const short2 b = s.base[gi][r];
     const float scale = p.inv_num_samples;
@@ -382,6 +415,103 @@ __device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, 
     }
 }
 
+// ---- tensor-core latent scatter -------------------------------------------------------------
+//
+// dG[y][x][c] = sum_s wy_s(y) wx_s(x) dX_s[c] over the tile's window is the product
+// G^T[(y, c)][x] = sum_s Q[s][(y, c)] A[s][x] with Q[s][(y, c)] = wy_s(y) dX_s[c] (zero outside
+// the sample's 4 rows) and A[s][x] = wx_s(x) (zero outside its 4 columns), both fp16 rows
+// of one sample, read MN-major.  Channel-interleaved grids with C = 8 make (y, c) exactly
+// one 16-byte core-matrix row per window row.
+
+// Operand rows of sample r for grid g (compile-time grid so the row lengths are constants).
+template <int C, int G>
+__device__ __forceinline__ void scatter_rows(Smem<C> &s, int r, bool valid, const float (&dx)[C])
+{
+    static_assert(C == 8, "the tensor-core scatter packs one window row per 16-byte chunk");
+    constexpr int NQ = sc_h(G), NA = sc_w(G) / 8;
+    uint8_t *Q = G ? s.t.q.Q1 : s.t.q.Q0;
+    uint8_t *A = G ? s.t.q.A1 : s.t.q.A0;
+#pragma unroll
+    for (int y = 0; y < NQ; ++y) st16(Q, umma::cm_offset(r, 8 * y, NQ), 0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int k = 0; k < NA; ++k) st16(A, umma::cm_offset(r, 8 * k, NA), 0u, 0u, 0u, 0u);
+    if (!valid) return;  // dX is zero there, and the footprint may lie outside the window
+    const Window &W = s.win[G];
+    const short2 b = s.base[G][r];
+    const int oy = b.y - 1 - W.y0, ox = b.x - 1 - W.x0;
+    const float4 wx = *reinterpret_cast<const float4 *>(&s.wts[G][r][0]);
+    const float4 wy = *reinterpret_cast<const float4 *>(&s.wts[G][r][4]);
+    const float wyv[4] = {wy.x, wy.y, wy.z, wy.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        st16(Q, umma::cm_offset(r, 8 * (oy + j), NQ), pack_half2(wyv[j] * dx[0], wyv[j] * dx[1]),
+             pack_half2(wyv[j] * dx[2], wyv[j] * dx[3]), pack_half2(wyv[j] * dx[4], wyv[j] * dx[5]),
+             pack_half2(wyv[j] * dx[6], wyv[j] * dx[7]));
+    const float wxv[4] = {wx.x, wx.y, wx.z, wx.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        *reinterpret_cast<__half *>(A + umma::cm_offset(r, ox + i, NA)) = __float2half_rn(wxv[i]);
+}
+
+// TMEM -> fp32 staging of the window sums (thread: one (row, channel) lane, 16 columns).
+template <int C>
+__device__ __forceinline__ void scatter_stage_out(Smem<C> &s, uint32_t tmem, int warp, int lane, int half)
+{
+    const int q = warp & 3;
+    const uint32_t lanes = (uint32_t)(32 * q) << 16;
+    {  // grid 0: M = 128, lane m = 8 y + c, columns x; half h takes x in [16 h, 16 h + 16)
+        uint32_t v[16];
+        umma::ld16(tmem + kColTile + lanes + 16 * half, v);
+        umma::wait_ld();
+        const int m = 32 * q + lane, y = m >> 3, c = m & 7;
+        if (y < sc_h(0)) {
+            float *o = s.t.f.g0 + (y * (sc_w(0) + 1) + 16 * half) * 8 + c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[8 * j] = __uint_as_float(v[j]);
+        }
+    }
+    if (half) {  // grid 1: M = 64, row m = 16 q + lane (lanes 0..15), columns x
+        uint32_t v[16];
+        umma::ld16(tmem + kColTile + sc_w(0) + lanes, v);
+        umma::wait_ld();
+        const int m = 16 * q + lane, y = m >> 3, c = m & 7;
+        if (lane < 16) {
+            float *o = s.t.f.g1 + (y * (sc_w(1) + 1)) * 8 + c;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) o[8 * j] = __uint_as_float(v[j]);
+        }
+    }
+}
+
+// Staged window sums -> global latent gradients (x 1 / num_samples), one float4 reduction
+// per 4 channels of every window texel.
+template <int C>
+__device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaunch &p, int tid)
+{
+    constexpr int n0 = sc_h(0) * sc_w(0) * 2, n1 = sc_h(1) * sc_w(1) * 2;  // (row, column, quad) slots
+    static_assert((n0 + n1) % kThreadsTC == 0, "whole slots per thread");
+    const float sc = p.inv_num_samples;
+#pragma unroll
+    for (int it = 0; it < (n0 + n1) / kThreadsTC; ++it) {
+        const int k = tid + it * kThreadsTC;
+        const int g = k < n0 ? 0 : 1;
+        const int kk = g ? k - n0 : k;
+        const int q = kk & 1;
+        const int x = g ? (kk >> 1) & (sc_w(1) - 1) : (kk >> 1) & (sc_w(0) - 1);
+        const int y = g ? kk >> 5 : kk >> 6;
+        const Window &W = s.win[g];
+        if (x >= W.w || y >= W.h) continue;
+        const float *src = (g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * 8 : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * 8) + 4 * q;
+        const float4 v = *reinterpret_cast<const float4 *>(src);
+        if (v.x == 0.f && v.y == 0.f && v.z == 0.f && v.w == 0.f) continue;
+        const int gw = p.gw[g], gh = p.gh[g];
+        float4 *dst = reinterpret_cast<float4 *>(p.ggrid[g] +
+                                                 ((size_t)wrap_coord(W.y0 + y, gh) * gw + wrap_coord(W.x0 + x, gw)) * C) +
+                      q;
+        atomicAdd(dst, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc));
+    }
+}
+
 // ---- tensor-core products -------------------------------------------------------------------
 
 // Descriptor whose start address advances by `bytes` (the address field holds addr >> 4 and
@@ -392,6 +522,7 @@ template <int C>
 struct Descs {
     uint64_t x, h1, h2, dy, w1, w2, w3;  // K-major views (LBO 128)
     uint64_t x_mn, h1_mn, h2_mn, dy_mn, w1_mn, w2_mn, w3_mn;  // MN-major views
+    uint64_t q0, q1, a0, a1;  // latent scatter operands (MN-major)
 };
 
 template <int C>
@@ -401,20 +532,24 @@ __device__ __forceinline__ Descs<C> make_descs(const Smem<C> &s)
     using umma::desc;
     constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
     Descs<C> d;
-    d.x = desc(smem_addr(s.X), 128, XG);
-    d.h1 = desc(smem_addr(s.H1), 128, HG);
-    d.h2 = desc(smem_addr(s.H2), 128, HG);
-    d.dy = desc(smem_addr(s.DY), 128, 256);
+    d.x = desc(smem_addr(s.t.m.X), 128, XG);
+    d.h1 = desc(smem_addr(s.t.m.H1), 128, HG);
+    d.h2 = desc(smem_addr(s.t.m.H2), 128, HG);
+    d.dy = desc(smem_addr(s.t.m.DY), 128, 256);
     d.w1 = desc(smem_addr(s.W1), 128, XG);
     d.w2 = desc(smem_addr(s.W2), 128, HG);
     d.w3 = desc(smem_addr(s.W3), 128, HG);
-    d.x_mn = desc(smem_addr(s.X), XG, 128);
-    d.h1_mn = desc(smem_addr(s.H1), HG, 128);
-    d.h2_mn = desc(smem_addr(s.H2), HG, 128);
-    d.dy_mn = desc(smem_addr(s.DY), 256, 128);
+    d.x_mn = desc(smem_addr(s.t.m.X), XG, 128);
+    d.h1_mn = desc(smem_addr(s.t.m.H1), HG, 128);
+    d.h2_mn = desc(smem_addr(s.t.m.H2), HG, 128);
+    d.dy_mn = desc(smem_addr(s.t.m.DY), 256, 128);
     d.w1_mn = desc(smem_addr(s.W1), XG, 128);
     d.w2_mn = desc(smem_addr(s.W2), HG, 128);
     d.w3_mn = desc(smem_addr(s.W3), HG, 128);
+    d.q0 = desc(smem_addr(s.t.q.Q0), sc_h(0) * 128, 128);
+    d.q1 = desc(smem_addr(s.t.q.Q1), sc_h(1) * 128, 128);
+    d.a0 = desc(smem_addr(s.t.q.A0), sc_w(0) / 8 * 128, 128);
+    d.a1 = desc(smem_addr(s.t.q.A1), sc_w(1) / 8 * 128, 128);
     return d;
 }
 
@@ -459,6 +594,16 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
         for (int ks = 0; ks < kTileN / 16; ++ks)
             mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
                     ks > 0 ? 1u : acc0);
+        break;
+    case 6:  // latent scatter: G0^T = Q0^T A0 (M128 N32), G1^T = Q1^T A1 (M64 N16), K = 128 samples
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(R, dadv(d.q0, ks * 2 * sc_h(0) * 128), dadv(d.a0, ks * 2 * sc_w(0) / 8 * 128),
+                    idesc_f16(128, sc_w(0), 1, 1), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(R + sc_w(0), dadv(d.q1, ks * 2 * sc_h(1) * 128), dadv(d.a1, ks * 2 * sc_w(1) / 8 * 128),
+                    idesc_f16(64, sc_w(1), 1, 1), ks > 0);
         break;
     default:  // B1: dX = dZ1 W1; dW1 += dZ1^T X
 #pragma unroll
@@ -531,8 +676,9 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     float sse = 0.f;
 
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const int ix = (tile % p.tiles_x) * kTileW + (r & (kTileW - 1));
-        const int iy = (tile / p.tiles_x) * kTileH + (r >> 4);
+        const int cx0 = (tile % p.tiles_x) * kTileW, cy0 = (tile / p.tiles_x) * kTileH;
+        const int ix = cx0 + (r & (kTileW - 1));
+        const int iy = cy0 + (r >> 4);
         const bool valid = ix < p.sampler.lattice_w && iy < p.sampler.lattice_h;
         float tgt[16];
 #pragma unroll
@@ -566,7 +712,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 }
 #pragma unroll
                 for (int j = 0; j < K::LC; ++j)
-                    st16(s.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                    st16(s.t.m.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
                          packed[4 * j + 3]);
             } else {
                 uint32_t packed[4] = {0u, 0u, 0u, 0u};
@@ -580,33 +726,33 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     gather_target(p.target, p.sampler.image_w, cout, fp, tgt);
                 }
                 static_assert(K::XC == K::LC + 2 || K::XC == K::LC + 3, "X row: latents, posenc, 1, [0]");
-                st16(s.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
-                st16(s.X, umma::cm_offset(r, 8 * (K::LC + 1), K::XC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+                st16(s.t.m.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
+                st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 1), K::XC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
                 if constexpr (K::XC > K::LC + 2)
-                    st16(s.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
+                    st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
             }
         }
         if (!run_stage<C>(0, d, tmem, first, done, ph, failed, tid)) break;  // F1
-        // the window finalisation overlaps F1 (the barrier above published the partials)
-        if (!p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
-        relu_store32(Rl + 32 * half, s.H1, r, 4 * half);
+        relu_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
         if (half)
-            st16(s.H1, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+            st16(s.t.m.H1, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
         else
-            st16(s.H1, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
+            st16(s.t.m.H1, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
         if (!run_stage<C>(1, d, tmem, first, done, ph, failed, tid)) break;  // F2
 
         // ---- E2: H2e ------------------------------------------------------------------------
-        relu_store32(Rl + 32 * half, s.H2, r, 4 * half);
+        relu_store32(Rl + 32 * half, s.t.m.H2, r, 4 * half);
         if (half)
-            st16(s.H2, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
+            st16(s.t.m.H2, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
         else
-            st16(s.H2, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
+            st16(s.t.m.H2, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
         if (!run_stage<C>(2, d, tmem, first, done, ph, failed, tid)) break;  // F3
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
+        // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
+        if (!half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
         if (half) {
             uint32_t v[16];
             umma::ld16(Rl, v);
@@ -627,37 +773,58 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 }
                 out[c2] = pack_half2(dd[0], dd[1]);
             }
-            st16(s.DY, umma::cm_offset(r, 0, 2), out[0], out[1], out[2], out[3]);
-            st16(s.DY, umma::cm_offset(r, 8, 2), out[4], out[5], out[6], out[7]);
+            st16(s.t.m.DY, umma::cm_offset(r, 0, 2), out[0], out[1], out[2], out[3]);
+            st16(s.t.m.DY, umma::cm_offset(r, 8, 2), out[4], out[5], out[6], out[7]);
         }
         if (!run_stage<C>(3, d, tmem, first, done, ph, failed, tid)) break;  // B3
 
         // ---- E4: dZ2 = dH2 * [H2 > 0] (in place of H2) -----------------------------------
-        mask_store32(Rl + 32 * half, s.H2, r, 4 * half);
+        mask_store32(Rl + 32 * half, s.t.m.H2, r, 4 * half);
         if (!run_stage<C>(4, d, tmem, first, done, ph, failed, tid)) break;  // B2
 
         // ---- E5: dZ1 = dH1 * [H1 > 0] (in place of H1) -----------------------------------
-        mask_store32(Rl + 32 * half, s.H1, r, 4 * half);
+        mask_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
         if (!run_stage<C>(5, d, tmem, first, done, ph, failed, tid)) break;  // B1
 
         // ---- E6: dX -> shared (fp32 rows over the dead H2 tile) -> latent gradients ------
         if (!p.finalize) {
+            // dX columns [half * C, half * C + C): the latents of grid `half`
+            float dxv[C];
             {
-                // dX columns [half * C, half * C + C): the latents of grid `half`
                 uint32_t v[32];
                 umma::ld16(Rl, *reinterpret_cast<uint32_t(*)[16]>(v));
                 if constexpr (K::NX > 16) umma::ld16(Rl + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
                 umma::wait_ld();
-                float *dxr = reinterpret_cast<float *>(s.H2) + r * K::DXS + half * C;
 #pragma unroll
-                for (int q = 0; q < C / 4; ++q) {
-                    float f[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        f[e] = __uint_as_float(half ? v[C + 4 * q + e] : v[4 * q + e]);
-                    *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(f[0], f[1], f[2], f[3]);
-                }
+                for (int e = 0; e < C; ++e) dxv[e] = __uint_as_float(half ? v[C + e] : v[e]);
             }
+            bool tc_scatter = false;
+            if constexpr (C == 8) tc_scatter = s.win[0].tc && s.win[1].tc;
+            if (tc_scatter) {
+                if constexpr (C == 8) {
+                    if (half) scatter_rows<C, 1>(s, r, valid, dxv);
+                    else scatter_rows<C, 0>(s, r, valid, dxv);
+                }
+                if (!run_stage<C>(6, d, tmem, first, done, ph, failed, tid)) break;  // scatter product
+                scatter_stage_out<C>(s, tmem, warp, lane, half);
+                if (__syncthreads_or(failed)) {
+                    failed = true;
+                    break;
+                }
+                scatter_reduce<C>(s, p, tid);
+                first = false;
+                umma::fence_before();
+                if (__syncthreads_or(failed)) {
+                    failed = true;
+                    break;
+                }
+                continue;
+            }
+            float *dxr = reinterpret_cast<float *>(s.t.m.H2) + r * K::DXS + half * C;
+#pragma unroll
+            for (int q = 0; q < C / 4; ++q)
+                *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(dxv[4 * q], dxv[4 * q + 1], dxv[4 * q + 2], dxv[4 * q + 3]);
+            if (warp < 2) window_cands<C>(s, warp, lane);
             if (__syncthreads_or(failed)) {
                 failed = true;
                 break;

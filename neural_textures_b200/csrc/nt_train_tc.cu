@@ -371,26 +371,31 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
 
 // ---- epilogue helpers -------------------------------------------------------------------
 
-// TMEM row (32 columns from taddr) -> relu -> fp16 -> 4 chunks of an H row.
+// TMEM row (32 columns from taddr) -> fp16 -> relu -> 4 chunks of an H row.  Rounding is
+// monotonic and keeps 0, so relu(round(x)) has the bits of round(relu(x)) up to the sign
+// of zero, which no later product or mask can see.
 __device__ __forceinline__ void relu_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
 {
     uint32_t v[32];
     umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
     umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
     umma::wait_ld();
+    const __half2 zero = __float2half2_rn(0.f);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         uint32_t h[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            h[e] = pack_half2(fmaxf(__uint_as_float(v[8 * q + 2 * e]), 0.f),
-                              fmaxf(__uint_as_float(v[8 * q + 2 * e + 1]), 0.f));
+        for (int e = 0; e < 4; ++e) {
+            const __half2 x = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+            const __half2 y = __hmax2(x, zero);
+            h[e] = *reinterpret_cast<const uint32_t *>(&y);
+        }
         st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
     }
 }
 
-// TMEM row (32 columns) masked by the ReLU of the activation row stored at the same place
-// in H, rounded to fp16 and written over it.
+// TMEM row (32 columns) rounded to fp16 and masked by the ReLU of the activation row stored
+// at the same place in H (lanes where the activation is not > 0 become +0), written over it.
 __device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
 {
     uint32_t v[32];
@@ -400,16 +405,16 @@ __device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, 
 #pragma unroll
     for (int q = 0; q < 4; ++q) a[q] = *reinterpret_cast<const uint4 *>(H + umma::cm_offset(r, 8 * (chunk0 + q), kHC));
     umma::wait_ld();
+    const __half2 zero = __float2half2_rn(0.f);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         const uint32_t aw[4] = {a[q].x, a[q].y, a[q].z, a[q].w};
         uint32_t h[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const __half2 act = *reinterpret_cast<const __half2 *>(&aw[e]);
-            const float g0 = __low2float(act) > 0.f ? __uint_as_float(v[8 * q + 2 * e]) : 0.f;
-            const float g1 = __high2float(act) > 0.f ? __uint_as_float(v[8 * q + 2 * e + 1]) : 0.f;
-            h[e] = pack_half2(g0, g1);
+            const __half2 g = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+            const unsigned m = __hgt2_mask(*reinterpret_cast<const __half2 *>(&aw[e]), zero);
+            h[e] = *reinterpret_cast<const uint32_t *>(&g) & m;
         }
         st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
     }
@@ -646,7 +651,9 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
 
 // ---- the kernel ---------------------------------------------------------------------------------
 
-template <int C>
+// C: latent channels per grid; TC: target channels when they have a vector gather (4, 8,
+// 12 or 16), 0 for the generic per-channel gather.
+template <int C, int TC>
 __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaunch p)
 {
     using K = Cfg<C>;
@@ -723,7 +730,10 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     for (int k = 0; k < 4; ++k) packed[k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
                     Footprint fp;
                     footprint(u, v, p.sampler.image_w, p.sampler.image_h, fp);
-                    gather_target(p.target, p.sampler.image_w, cout, fp, tgt);
+                    if constexpr (TC > 0)
+                        gather_cr<TC>(p.target, p.sampler.image_w, fp, tgt);
+                    else
+                        gather_cr_any(p.target, p.sampler.image_w, cout, fp, tgt);
                 }
                 static_assert(K::XC == K::LC + 2 || K::XC == K::LC + 3, "X row: latents, posenc, 1, [0]");
                 st16(s.t.m.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
@@ -928,19 +938,19 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     }
 }
 
-template <int C>
+template <int C, int TC>
 static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 {
     const size_t smem = sizeof(Smem<C>);
     static_assert(sizeof(Smem<C>) <= 113 * 1024, "two CTAs per SM");
-    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C>), smem);
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC>), smem);
     if (e != cudaSuccess) return e;
     p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
     p.tiles_y = (p.sampler.lattice_h + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = 2 * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;
-    train_tc_kernel<C><<<grid, kThreadsTC, smem, stream>>>(p);
+    train_tc_kernel<C, TC><<<grid, kThreadsTC, smem, stream>>>(p);
     count_launch();
     return cudaGetLastError();
 }
@@ -949,8 +959,9 @@ static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 
 cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream)
 {
-    if (channels == 8) return tc::launch_t<8>(p, stream);
-    if (channels == 12) return tc::launch_t<12>(p, stream);
+    const int cout = p.net.cout;
+    if (channels == 8) return cout == 8 ? tc::launch_t<8, 8>(p, stream) : tc::launch_t<8, 0>(p, stream);
+    if (channels == 12) return cout == 12 ? tc::launch_t<12, 12>(p, stream) : tc::launch_t<12, 0>(p, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -27,9 +27,9 @@ __device__ __forceinline__ float adam_one(float w, float g, float &m, float &v, 
 constexpr int kAdamThreads = 256;
 constexpr int kAdamPerThread = 8;
 
-__global__ void __launch_bounds__(kAdamThreads) adam_kernel(const AdamLaunch p)
+// One chunk (kAdamThreads x kAdamPerThread consecutive entries of one segment).
+__device__ __forceinline__ void adam_chunk(const AdamLaunch &p, int b)
 {
-    const int b = blockIdx.x;
     int si = 0;
 #pragma unroll 1
     while (si + 1 < p.nseg && b >= p.seg[si + 1].first_block) ++si;
@@ -41,18 +41,19 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const AdamLaunch p)
                      ((reinterpret_cast<uintptr_t>(s.m) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.v) & 15) == 0);
     if (vec) {
+        // all five streams are requested before any value is used (one memory round trip)
         const float4 g0 = *reinterpret_cast<const float4 *>(s.g + i0);
         const float4 g1 = *reinterpret_cast<const float4 *>(s.g + i0 + 4);
-        float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        uint4 wraw = *reinterpret_cast<const uint4 *>(s.w + i0);
+        const float4 m0 = *reinterpret_cast<const float4 *>(s.m + i0);
+        const float4 m1 = *reinterpret_cast<const float4 *>(s.m + i0 + 4);
+        const float4 v0 = *reinterpret_cast<const float4 *>(s.v + i0);
+        const float4 v1 = *reinterpret_cast<const float4 *>(s.v + i0 + 4);
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         bool any = false;
 #pragma unroll
         for (int e = 0; e < 8; ++e) any |= gv[e] != 0.f;
-        if (!any) return;
-        uint4 wraw = *reinterpret_cast<const uint4 *>(s.w + i0);
-        float4 m0 = *reinterpret_cast<const float4 *>(s.m + i0);
-        float4 m1 = *reinterpret_cast<const float4 *>(s.m + i0 + 4);
-        float4 v0 = *reinterpret_cast<const float4 *>(s.v + i0);
-        float4 v1 = *reinterpret_cast<const float4 *>(s.v + i0 + 4);
+        if (!any) return;  // nothing to update, nothing to zero
         float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
         float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         __half *wh = reinterpret_cast<__half *>(&wraw);
@@ -81,6 +82,8 @@ __global__ void __launch_bounds__(kAdamThreads) adam_kernel(const AdamLaunch p)
         }
     }
 }
+
+__global__ void __launch_bounds__(kAdamThreads) adam_kernel(const AdamLaunch p) { adam_chunk(p, blockIdx.x); }
 
 cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream)
 {

@@ -116,6 +116,7 @@ static cudaError_t launch_decode_t(const DecodeLaunch &p, cudaStream_t stream)
 
 cudaError_t launch_decode(const DecodeLaunch &p, int channels, cudaStream_t stream)
 {
+    if (decode_engine() == 1) return launch_decode_tc(p, channels, stream);
     const bool wide = p.net.cout > 8;
     if (channels == 8) return wide ? launch_decode_t<8, 2>(p, stream) : launch_decode_t<8, 1>(p, stream);
     if (channels == 12) return wide ? launch_decode_t<12, 2>(p, stream) : launch_decode_t<12, 1>(p, stream);

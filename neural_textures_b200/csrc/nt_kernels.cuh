@@ -69,6 +69,12 @@ cudaError_t launch_train(const TrainLaunch &p, int channels, cudaStream_t stream
 cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream);
 // Training engine: 1 = tcgen05 (default), 0 = per-warp mma.sync (NT_TRAIN_ENGINE=mma)
 int train_engine();
+// tcgen05 / TMEM decode kernel (16 x 8 tiles; recomputes tiles_x / tiles_y itself)
+cudaError_t launch_decode_tc(const DecodeLaunch &p, int channels, cudaStream_t stream);
+// Decode engine: 1 = tcgen05 (default), 0 = per-warp mma.sync (NT_DECODE_ENGINE=mma)
+int decode_engine();
+// Status word of the decode kernel's bounded waits (host read, optionally cleared).
+cudaError_t read_decode_status(uint32_t *status, bool clear);
 cudaError_t launch_decode(const DecodeLaunch &p, int channels, cudaStream_t stream);
 cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream);
 int sm_count();

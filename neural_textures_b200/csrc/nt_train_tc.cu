@@ -45,6 +45,7 @@
 
 #include "nt_kernels.cuh"
 #include "nt_mma.cuh"
+#include "nt_tc_common.cuh"
 #include "nt_umma.cuh"
 
 namespace nt {
@@ -53,24 +54,10 @@ __device__ unsigned int g_device_status;  // bit 0: a bounded wait of a training
 
 namespace tc {
 
-constexpr int kTileW = 16, kTileH = 8, kTileN = 128;
 constexpr int kThreadsTC = 256;
 constexpr int kMaxWinW = 40;  // widest footprint window the sweep handles (texels)
-constexpr int kHC = 10;       // core-matrix chunks per H row: 64 activations, 1, 0 x 15
-constexpr int kHW = kHC * 8;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kColW1 = 0, kColW2 = 64, kColW3 = 160, kColTile = 192;
-constexpr uint32_t kSpinLimit = 1u << 22;
-
-template <int C>
-struct Cfg {
-    static constexpr int kBias1 = 2 * C + 8;                 // column of the constant 1 in X
-    static constexpr int XC = ((kBias1 + 1 + 15) / 16) * 2;  // chunks of 8 halves per X row
-    static constexpr int XW = XC * 8;                        // 32 (C = 8) or 48 (C = 12)
-    static constexpr int LC = C / 4;                         // X chunks holding the 2C latents
-    static constexpr int NX = ((2 * C + 15) / 16) * 16;      // dX columns produced by B1
-    static constexpr int DXS = 2 * C + 4;                    // fp32 dX row stride (floats)
-};
 
 // Tensor-core latent scatter: per grid, the window is at most sc_w(g) texels wide and
 // sc_h(g) texels high (else the tile takes the column sweep).
@@ -116,49 +103,6 @@ struct Smem {
     uint32_t tmem_base;
     float red[kThreadsTC / 32];
 };
-
-__device__ __forceinline__ void st16(uint8_t *base, uint32_t off, uint32_t a, uint32_t b, uint32_t c, uint32_t d)
-{
-    *reinterpret_cast<uint4 *>(base + off) = make_uint4(a, b, c, d);
-}
-
-// ---- weights: shared-memory operand images with the biases folded in -------------------
-
-template <int C>
-__device__ __forceinline__ void stage_weights_tc(Smem<C> &w, const NetView &net, int tid)
-{
-    using K = Cfg<C>;
-    constexpr int n1 = 64 * K::XC, n2 = 64 * kHC, n3 = 16 * kHC;
-    for (int i = tid; i < n1 + n2 + n3; i += kThreadsTC) {
-        int o, j, kch, nin, pad, which;
-        if (i < n1) {
-            o = i / K::XC, j = i % K::XC, kch = K::XC, nin = K::kBias1, pad = 32, which = 0;
-        } else if (i < n1 + n2) {
-            o = (i - n1) / kHC, j = (i - n1) % kHC, kch = kHC, nin = 64, pad = 64, which = 1;
-        } else {
-            o = (i - n1 - n2) / kHC, j = (i - n1 - n2) % kHC, kch = kHC, nin = 64, pad = 64, which = 2;
-        }
-        const __half *src = net.W[which], *bias = net.b[which];
-        uint8_t *dst = which == 0 ? w.W1 : (which == 1 ? w.W2 : w.W3);
-        const bool row_ok = which != 2 || o < net.cout;
-        uint32_t v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            __half x[2];
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-                const int in = 8 * j + 2 * e + q;
-                x[q] = __float2half(0.f);
-                if (row_ok) {
-                    if (in < nin) x[q] = src[o * pad + in];
-                    else if (in == nin) x[q] = bias[o];
-                }
-            }
-            v[e] = (uint32_t)__half_as_ushort(x[0]) | ((uint32_t)__half_as_ushort(x[1]) << 16);
-        }
-        st16(dst, umma::cm_offset(o, 8 * j, kch), v[0], v[1], v[2], v[3]);
-    }
-}
 
 // ---- footprint windows of a tile (for the latent-gradient sweep) ------------------------
 
@@ -371,29 +315,6 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
 
 // ---- epilogue helpers -------------------------------------------------------------------
 
-// TMEM row (32 columns from taddr) -> fp16 -> relu -> 4 chunks of an H row.  Rounding is
-// monotonic and keeps 0, so relu(round(x)) has the bits of round(relu(x)) up to the sign
-// of zero, which no later product or mask can see.
-__device__ __forceinline__ void relu_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
-{
-    uint32_t v[32];
-    umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
-    umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-    umma::wait_ld();
-    const __half2 zero = __float2half2_rn(0.f);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        uint32_t h[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const __half2 x = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
-            const __half2 y = __hmax2(x, zero);
-            h[e] = *reinterpret_cast<const uint32_t *>(&y);
-        }
-        st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
-    }
-}
-
 // TMEM row (32 columns) rounded to fp16 and masked by the ReLU of the activation row stored
 // at the same place in H (lanes where the activation is not > 0 become +0), written over it.
 __device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
@@ -519,9 +440,6 @@ __device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaun
 
 // ---- tensor-core products -------------------------------------------------------------------
 
-// Descriptor whose start address advances by `bytes` (the address field holds addr >> 4 and
-// every operand lies below 256 KB, so the field never carries into its neighbours).
-__device__ __forceinline__ uint64_t dadv(uint64_t d, uint32_t bytes) { return d + (uint64_t)(bytes >> 4); }
 
 template <int C>
 struct Descs {
@@ -662,7 +580,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int r = tid & (kTileN - 1), half = tid >> 7;  // sample, role
 
-    stage_weights_tc<C>(s, p.net, tid);
+    stage_weights_tc<C>(s, p.net, tid, kThreadsTC);
     if (warp == 0) umma::alloc(smem_addr(&s.tmem_base), kTmemCols);
     if (tid == 0) {
         umma::mbar_init(smem_addr(&s.done), 1);
@@ -970,10 +888,13 @@ cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t str
 extern "C" nt_status nt_read_device_status(uint32_t *status, int32_t clear)
 {
     if (!status) return NT_ERR_INVALID_ARG;
-    if (cudaMemcpyFromSymbol(status, nt::g_device_status, sizeof(uint32_t)) != cudaSuccess) return NT_ERR_CUDA;
+    uint32_t train = 0, decode = 0;
+    if (cudaMemcpyFromSymbol(&train, nt::g_device_status, sizeof(uint32_t)) != cudaSuccess) return NT_ERR_CUDA;
+    if (nt::read_decode_status(&decode, clear != 0) != cudaSuccess) return NT_ERR_CUDA;
     if (clear) {
         const uint32_t zero = 0;
         if (cudaMemcpyToSymbol(nt::g_device_status, &zero, sizeof(uint32_t)) != cudaSuccess) return NT_ERR_CUDA;
     }
+    *status = train | decode;
     return NT_OK;
 }

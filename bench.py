@@ -399,7 +399,7 @@ def main():
         "config": {"workload": CFG1["workload"], "global_batch": B * world, "samples_per_gpu": B,
                    "latents": "512^2x8 + 256^2x8 fp16", "mlp": "32-64-64-8", "parallelism": f"materials x{world}",
                    "l2": "flushed (256 MB write) before every timed step"},
-        "roofline": {"kernel": "train_kernel", "bound": "tensor", "achieved": achieved_tf, "peak": pk["tensor"],
+        "roofline": {"kernel": "nt::tc::train_tc_kernel (tcgen05)", "bound": "tensor", "achieved": achieved_tf, "peak": pk["tensor"],
                      "unit": "TFLOP/s", "frac": achieved_tf / pk["tensor"],
                      "traffic": tr.get("train_kernel", {}).get("bytes_per_launch"),
                      "peak_source": pk["source"] + " burst bf16",
@@ -422,6 +422,8 @@ def main():
     }
     if codec:
         codec["decode_hbm_frac"] = codec["decode_hbm_gbs"] / pk["hbm"]
+        codec["decode_traffic"] = tr.get("bc6h_decode_kernel", {}).get("bytes_per_launch")
+        codec["encode_traffic"] = tr.get("bc6h_encode_kernel", {}).get("bytes_per_launch")
         line["codec"] = codec
     if not args.no_cpu_baseline:
         from oracle import oracle as O

@@ -142,6 +142,18 @@ typedef struct NtKernelParams {
     uint32_t seed;                   /* 0 reproduces the reference's per-sample seeds */
 
     float *loss_accum;               /* optional: += sum over samples and channels of err^2 */
+
+    /* Row sharding of one material over several calls (no reference counterpart; all zero
+     * means the whole material).  nt_invoke_training trains lattice rows
+     * [lattice_row0, lattice_row0 + lattice_rows) only (lattice_rows 0: all rows); num_samples
+     * stays the whole lattice, so every call scales by the global batch.  Source s (0, 1: the
+     * latent grids with their gradients, 2: the target) may hold only stored_rows[s] rows of
+     * its full height, starting at full row row_origin[s] and wrapping: full row r lives at
+     * stored row (r - row_origin[s]) mod height (stored_rows 0: the full height, origin 0).
+     * The stored rows must cover every row the trained samples' footprints reach; a row
+     * outside them is skipped and sets bit 1 of the device status word. */
+    int32_t lattice_row0, lattice_rows;
+    int32_t row_origin[3], stored_rows[3];
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */

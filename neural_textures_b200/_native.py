@@ -69,6 +69,10 @@ class NtKernelParams(C.Structure):
         ("step", C.c_int32),
         ("seed", C.c_uint32),
         ("loss_accum", C.c_void_p),
+        ("lattice_row0", C.c_int32),
+        ("lattice_rows", C.c_int32),
+        ("row_origin", C.c_int32 * 3),
+        ("stored_rows", C.c_int32 * 3),
     ]
 
 

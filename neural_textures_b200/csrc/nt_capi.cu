@@ -222,6 +222,10 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(step)
     NT_FIELD(seed)
     NT_FIELD(loss_accum)
+    NT_FIELD(lattice_row0)
+    NT_FIELD(lattice_rows)
+    NT_FIELD(row_origin)
+    NT_FIELD(stored_rows)
 #undef NT_FIELD
     return (size_t)-1;
 }
@@ -281,6 +285,24 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
     L.inv_num_samples = 1.0f / (float)p->num_samples;
     L.loss_accum = p->loss_accum;
     L.finalize = type == NT_TRAIN_FINALIZE;
+    // row sharding (all zero: the whole material)
+    NT_REQUIRE(p->lattice_row0 >= 0 && p->lattice_rows >= 0 &&
+                   (int64_t)p->lattice_row0 + p->lattice_rows <= p->lattice_height,
+               "lattice rows [%d, %d + %d) are outside the %d-row lattice", p->lattice_row0, p->lattice_row0,
+               p->lattice_rows, p->lattice_height);
+    L.lat_row0 = p->lattice_row0;
+    L.lat_rows = p->lattice_rows ? p->lattice_rows : p->lattice_height - p->lattice_row0;
+    bool sharded = p->lattice_row0 != 0 || L.lat_rows != p->lattice_height;
+    for (int s = 0; s < 3; ++s) {
+        const int h = s < 2 ? p->features[s].height : p->image_height;
+        NT_REQUIRE(p->stored_rows[s] >= 0 && p->stored_rows[s] <= h && p->row_origin[s] >= 0 && p->row_origin[s] < h,
+                   "source %d: stored rows %d from row %d do not fit its %d rows", s, p->stored_rows[s],
+                   p->row_origin[s], h);
+        L.org[s] = p->stored_rows[s] ? p->row_origin[s] : 0;
+        L.rows[s] = p->stored_rows[s] ? p->stored_rows[s] : h;
+        sharded = sharded || L.rows[s] != h;
+    }
+    NT_REQUIRE(!sharded || train_engine() == 1, "row sharding needs the tcgen05 training engine (NT_TRAIN_ENGINE=mma is set)");
     L.tiles_x = (p->lattice_width + kTileSide - 1) / kTileSide;
     L.tiles_y = (p->lattice_height + kTileSide - 1) / kTileSide;
     return check_cuda(launch_train(L, p->latent_channels, (cudaStream_t)stream), "training kernel");

@@ -33,6 +33,10 @@ struct TrainLaunch {
     float *loss_accum;
     int32_t finalize;
     int32_t tiles_x, tiles_y;
+    // Row sharding: lattice rows [lat_row0, lat_row0 + lat_rows) are trained; source s
+    // (0, 1: latent grids, 2: target) stores rows_s rows from full row org[s] (wrapping).
+    int32_t lat_row0, lat_rows;
+    int32_t org[3], rows[3];
 };
 
 struct DecodeLaunch {

@@ -104,6 +104,33 @@ struct Smem {
     float red[kThreadsTC / 32];
 };
 
+// ---- row sharding ----------------------------------------------------------------------
+//
+// Source s (0, 1: latent grids, 2: target) may hold only p.rows[s] rows, starting at full
+// row p.org[s] and wrapping.  A row outside them is never read or written: it is skipped
+// and bit 1 of the device status word is set (the caller's shard plan is wrong).
+
+__device__ __forceinline__ int stored_row(const TrainLaunch &p, int src, int row, int h)
+{
+    const int r = wrap_coord(row - p.org[src], h);
+    if (r >= p.rows[src]) {
+        atomicOr(&g_device_status, 2u);
+        return -1;
+    }
+    return r;
+}
+
+// Footprint rows -> stored rows; a missing row gets weight 0 (and is flagged).
+__device__ __forceinline__ void shard_rows(const TrainLaunch &p, int src, int h, Footprint &fp)
+{
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int r = stored_row(p, src, fp.by - 1 + j, h);
+        fp.ys[j] = r < 0 ? 0 : r;
+        if (r < 0) fp.wy[j] = 0.f;
+    }
+}
+
 // ---- footprint windows of a tile (for the latent-gradient sweep) ------------------------
 
 // Per-warp min / max of the footprint bases per lattice column (lanes L and L + 16 share a
@@ -212,7 +239,9 @@ __device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, 
     if (!any) return;
     const int gw = p.gw[gi], gh = p.gh[gi];
     const float sc = p.inv_num_samples;
-    float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)wrap_coord(ty, gh) * gw + wrap_coord(tx, gw)) * C);
+    const int sy = stored_row(p, gi, ty, gh);
+    if (sy < 0) return;
+    float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)sy * gw + wrap_coord(tx, gw)) * C);
 #pragma unroll
     for (int q = 0; q < C / 4; ++q)
         atomicAdd(dst + q, make_float4(row[4 * q] * sc, row[4 * q + 1] * sc, row[4 * q + 2] * sc, row[4 * q + 3] * sc));
@@ -300,7 +329,8 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
     const short2 b = s.base[gi][r];
     const float scale = p.inv_num_samples;
     for (int j = 0; j < 4; ++j) {
-        const int yy = wrap_coord(b.y - 1 + j, gh);
+        const int yy = stored_row(p, gi, b.y - 1 + j, gh);
+        if (yy < 0) continue;
         for (int i = 0; i < 4; ++i) {
             const int xx = wrap_coord(b.x - 1 + i, gw);
             const float wgt = s.wts[gi][r][i] * s.wts[gi][r][4 + j] * scale;
@@ -431,9 +461,9 @@ __device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaun
         const float4 v = *reinterpret_cast<const float4 *>(src);
         if (v.x == 0.f && v.y == 0.f && v.z == 0.f && v.w == 0.f) continue;
         const int gw = p.gw[g], gh = p.gh[g];
-        float4 *dst = reinterpret_cast<float4 *>(p.ggrid[g] +
-                                                 ((size_t)wrap_coord(W.y0 + y, gh) * gw + wrap_coord(W.x0 + x, gw)) * C) +
-                      q;
+        const int sy = stored_row(p, g, W.y0 + y, gh);
+        if (sy < 0) continue;
+        float4 *dst = reinterpret_cast<float4 *>(p.ggrid[g] + ((size_t)sy * gw + wrap_coord(W.x0 + x, gw)) * C) + q;
         atomicAdd(dst, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc));
     }
 }
@@ -603,8 +633,8 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int cx0 = (tile % p.tiles_x) * kTileW, cy0 = (tile / p.tiles_x) * kTileH;
         const int ix = cx0 + (r & (kTileW - 1));
-        const int iy = cy0 + (r >> 4);
-        const bool valid = ix < p.sampler.lattice_w && iy < p.sampler.lattice_h;
+        const int iy = p.lat_row0 + cy0 + (r >> 4);  // full lattice row (sharded calls train a band)
+        const bool valid = ix < p.sampler.lattice_w && iy < p.lat_row0 + p.lat_rows && iy < p.sampler.lattice_h;
         float tgt[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) tgt[k] = 0.f;
@@ -621,6 +651,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 for (int gi = 0; gi < 2; ++gi) {
                     Footprint fp;
                     footprint(u, v, p.gw[gi], p.gh[gi], fp);
+                    if (valid) shard_rows(p, gi, p.gh[gi], fp);
                     if (valid) {
                         float f[C];
                         gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
@@ -648,6 +679,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     for (int k = 0; k < 4; ++k) packed[k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
                     Footprint fp;
                     footprint(u, v, p.sampler.image_w, p.sampler.image_h, fp);
+                    shard_rows(p, 2, p.sampler.image_h, fp);
                     if constexpr (TC > 0)
                         gather_cr<TC>(p.target, p.sampler.image_w, fp, tgt);
                     else
@@ -864,7 +896,7 @@ static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
     cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC>), smem);
     if (e != cudaSuccess) return e;
     p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
-    p.tiles_y = (p.sampler.lattice_h + kTileH - 1) / kTileH;
+    p.tiles_y = (p.lat_rows + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = 2 * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;

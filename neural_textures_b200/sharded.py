@@ -1,0 +1,353 @@
+"""Row-sharded training of one material over several GPUs (BASELINE config 4b).
+
+The reference trains one material on one device (main.cpp:1071-1077).  Here a material
+too large for one GPU's share of work is split into bands of lattice rows, one per rank;
+each rank stores, for every latent grid and for the target, only the band of rows its
+samples reach, plus HALO rows on each side:
+
+    stored rows of a grid = [halo above | owned band | halo below]
+
+A training step on rank r is
+  1. the training pass over its lattice rows (nt_invoke_training with lattice_row0 /
+     lattice_rows and per-source row_origin / stored_rows);
+  2. the gradients its samples left in the halo rows go to the neighbours that own those
+     rows (two point-to-point phases over NCCL: halo above -> rank r - 1, halo below ->
+     rank r + 1), which add them to their bands;
+  3. one allreduce (sum) of the MLP weight and bias gradients, kept in one flat buffer;
+  4. Adam over the MLP (identical on every rank) and over the owned band of each grid;
+  5. the updated band edges go back to the neighbours' halo rows.
+So the result equals the single-GPU step up to the order of floating-point additions.
+Every rank posts the same collectives in the same order.
+
+The exchanges come in two forms: DistComm runs them over torch.distributed (NCCL on GPUs,
+gloo on CPU), LocalShards runs several shards in one process (tests on one GPU).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native as N
+from ._native import check, load
+from .api import PAD_IN, PAD_OUT, _stream, he_normal_weights, zero_padded_inputs
+
+HALO = 3  # filter reach beyond a band: taps at -2.5 .. +1.5 rows of the band's sample range
+
+
+@dataclass(frozen=True)
+class Band:
+    """Rows of one source (height `height`) held by one rank."""
+    height: int
+    lo: int        # first owned row
+    hi: int        # one past the last owned row
+    halo: int      # halo rows above and below (0: unsharded)
+
+    @property
+    def origin(self) -> int:
+        return (self.lo - self.halo) % self.height
+
+    @property
+    def stored(self) -> int:
+        return self.hi - self.lo + 2 * self.halo
+
+    @property
+    def owned(self) -> int:
+        return self.hi - self.lo
+
+    def stored_rows_of_full(self) -> np.ndarray:
+        """Full row index of every stored row."""
+        return (self.origin + np.arange(self.stored)) % self.height
+
+
+def lattice_band(rank: int, world: int, lattice_h: int) -> tuple[int, int]:
+    return rank * lattice_h // world, (rank + 1) * lattice_h // world
+
+
+def source_band(rank: int, world: int, lattice_h: int, height: int) -> Band:
+    """Rows of a source of `height` rows that the samples of rank's lattice band reach.
+
+    Sample rows of lattice band [a, b) lie in [a, b) * height / lattice_h of the source (the
+    sample stride is image_h / lattice_h and a source of height h spans the image), so the
+    owned rows are that range rounded to the nearest row; consecutive ranks' bands then
+    partition the source."""
+    a, b = lattice_band(rank, world, lattice_h)
+    rnd = lambda x: (2 * x * height + lattice_h) // (2 * lattice_h)
+    lo, hi = rnd(a), rnd(b)
+    if world == 1:
+        return Band(height, 0, height, 0)
+    if hi - lo < HALO or hi - lo + 2 * HALO > height:
+        raise ValueError(f"rank {rank}: band of {hi - lo} rows of a {height}-row source cannot be sharded "
+                         f"{world} ways with a {HALO}-row halo")
+    return Band(height, lo, hi, HALO)
+
+
+class ShardedTexture:
+    """Device state of one rank's band of a material: stored rows of both latent grids (fp16)
+    with fp32 gradients and Adam moments, the stored rows of the target, and a full copy of
+    the network (its gradients in one flat fp32 buffer, the allreduce operand)."""
+
+    def __init__(self, rank: int, world: int, image_w: int, image_h: int, grid_sizes, latent_channels: int,
+                 output_channels: int, lattice, device="cuda", latent_lr: float = 1e-2, network_lr: float = 5e-3,
+                 beta1: float = 0.9, beta2: float = 0.99, eps: float = 1e-8):
+        import torch
+        self.torch = torch
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.image_w, self.image_h = image_w, image_h
+        self.C, self.cout = latent_channels, output_channels
+        self.grid_sizes = [tuple(g) for g in grid_sizes]
+        self.lattice = tuple(lattice)
+        self.lat_band = lattice_band(rank, world, self.lattice[1])
+        self.bands = [source_band(rank, world, self.lattice[1], h) for (_, h) in self.grid_sizes]
+        self.tband = source_band(rank, world, self.lattice[1], image_h)
+        f16, f32 = torch.float16, torch.float32
+        z = lambda shape, dt: torch.zeros(shape, dtype=dt, device=self.device)
+        self.grids = [z((b.stored, w, self.C), f16) for b, (w, _) in zip(self.bands, self.grid_sizes)]
+        self.ggrads = [z(g.shape, f32) for g in self.grids]
+        self.gm1 = [z(g.shape, f32) for g in self.grids]
+        self.gm2 = [z(g.shape, f32) for g in self.grids]
+        self.target = z((self.tband.stored, image_w, self.cout), f16)
+        self.W = [z(PAD_OUT[l] * PAD_IN[l], f16) for l in range(3)]
+        self.b = [z(64, f16), z(64, f16), z(self.cout, f16)]
+        # network gradients: one flat buffer (each piece 16-byte aligned), views per layer
+        sizes = [w.numel() for w in self.W] + [b.numel() for b in self.b]
+        offs, o = [], 0
+        for n in sizes:
+            offs.append(o)
+            o += (n + 3) // 4 * 4
+        self.net_grad = z(o, f32)
+        self.gW = [self.net_grad[offs[l]:offs[l] + sizes[l]] for l in range(3)]
+        self.gb = [self.net_grad[offs[3 + l]:offs[3 + l] + sizes[3 + l]] for l in range(3)]
+        self.mW = [z(w.shape, f32) for w in self.W]
+        self.vW = [z(w.shape, f32) for w in self.W]
+        self.mb = [z(b.shape, f32) for b in self.b]
+        self.vb = [z(b.shape, f32) for b in self.b]
+        self.loss_accum = z(1, f32)
+        self.latent_adam = (beta1, beta2, latent_lr, eps)
+        self.network_adam = (beta1, beta2, network_lr, eps)
+        self.channel_weights = [1.0] * self.cout
+        self.seed = 0
+        self.step = 0
+
+    # -- initialisation: the same material as NeuralTexture.init(seed), cut to the stored rows --
+    def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False, stream=None):
+        torch = self.torch
+        L = load()
+        for i, (band, (w, h)) in enumerate(zip(self.bands, self.grid_sizes)):
+            full = torch.empty((h, w, self.C), dtype=torch.float16, device=self.device)
+            check(L.nt_init_latents(full.data_ptr(), full.numel(), seed * 7919 + i + 1, _stream(stream)))
+            rows = torch.from_numpy(band.stored_rows_of_full()).to(self.device)
+            self.grids[i].copy_(full.index_select(0, rows))
+            del full
+        Ws = he_normal_weights(seed, self.cout)
+        Ws[0] = zero_padded_inputs(Ws[0], 2 * self.C + 8)
+        for l in range(3):
+            self.W[l].copy_(torch.from_numpy(Ws[l]).to(self.device))
+            self.b[l].zero_()
+        full = torch.empty((self.image_h, self.image_w, self.cout), dtype=torch.float16, device=self.device)
+        ts = seed if target_seed is None else target_seed
+        check(L.nt_generate_target(full.data_ptr(), self.image_w, self.image_h, self.cout, ts, int(pbr_normals),
+                                   _stream(stream)))
+        rows = torch.from_numpy(self.tband.stored_rows_of_full()).to(self.device)
+        self.target.copy_(full.index_select(0, rows))
+        del full
+        for t in self.ggrads + self.gm1 + self.gm2 + self.mW + self.vW + self.mb + self.vb + [self.net_grad]:
+            t.zero_()
+        self.step = 0
+
+    # -- parameter blocks ------------------------------------------------------------------------
+    def _common(self, p: N.NtKernelParams):
+        p.latent_channels, p.output_channels = self.C, self.cout
+        for l in range(3):
+            p.network_weights[l] = self.W[l].data_ptr()
+            p.network_weight_gradients[l] = self.gW[l].data_ptr()
+            p.network_weight_moment1[l] = self.mW[l].data_ptr()
+            p.network_weight_moment2[l] = self.vW[l].data_ptr()
+            p.network_biases[l] = self.b[l].data_ptr()
+            p.network_bias_gradients[l] = self.gb[l].data_ptr()
+            p.network_bias_moment1[l] = self.mb[l].data_ptr()
+            p.network_bias_moment2[l] = self.vb[l].data_ptr()
+        (p.network_adam.beta1, p.network_adam.beta2, p.network_adam.learning_rate,
+         p.network_adam.epsilon) = self.network_adam
+        (p.feature_adam.beta1, p.feature_adam.beta2, p.feature_adam.learning_rate,
+         p.feature_adam.epsilon) = self.latent_adam
+        p.image_width, p.image_height = self.image_w, self.image_h
+        p.lattice_width, p.lattice_height = self.lattice
+        p.sample_stride_x = self.image_w / self.lattice[0]
+        p.sample_stride_y = self.image_h / self.lattice[1]
+        p.num_samples = self.lattice[0] * self.lattice[1]
+        p.step = self.step
+        p.seed = self.seed
+
+    def train_params(self) -> N.NtKernelParams:
+        """Training pass over this rank's lattice rows; sources addressed by full row."""
+        p = N.NtKernelParams()
+        self._common(p)
+        for i in range(2):
+            f = p.features[i]
+            f.grid, f.gradients = self.grids[i].data_ptr(), self.ggrads[i].data_ptr()
+            f.moment1, f.moment2 = self.gm1[i].data_ptr(), self.gm2[i].data_ptr()
+            f.width, f.height = self.grid_sizes[i]
+            p.row_origin[i] = self.bands[i].origin
+            p.stored_rows[i] = self.bands[i].stored if self.world > 1 else 0
+        p.row_origin[2] = self.tband.origin
+        p.stored_rows[2] = self.tband.stored if self.world > 1 else 0
+        p.target = self.target.data_ptr()
+        for c in range(self.cout):
+            p.channel_loss_weights[c] = self.channel_weights[c]
+        p.lattice_row0 = self.lat_band[0]
+        p.lattice_rows = self.lat_band[1] - self.lat_band[0]
+        p.loss_accum = self.loss_accum.data_ptr()
+        return p
+
+    def adam_params(self) -> N.NtKernelParams:
+        """Adam over the network and the owned band of each grid (halo rows excluded)."""
+        p = N.NtKernelParams()
+        self._common(p)
+        for i in range(2):
+            band, f = self.bands[i], p.features[i]
+            h0 = band.halo
+            f.grid = self.grids[i][h0:].data_ptr()
+            f.gradients = self.ggrads[i][h0:].data_ptr()
+            f.moment1 = self.gm1[i][h0:].data_ptr()
+            f.moment2 = self.gm2[i][h0:].data_ptr()
+            f.width, f.height = self.grid_sizes[i][0], band.owned
+        p.target = self.target.data_ptr()
+        return p
+
+    # -- views -------------------------------------------------------------------------------------
+    def band_view(self, tensors, i: int):
+        b = self.bands[i]
+        return tensors[i][b.halo:b.halo + b.owned]
+
+    def halo_above(self, tensors, i: int):
+        return tensors[i][:self.bands[i].halo]
+
+    def halo_below(self, tensors, i: int):
+        b = self.bands[i]
+        return tensors[i][b.halo + b.owned:]
+
+    def band_first(self, tensors, i: int):
+        b = self.bands[i]
+        return tensors[i][b.halo:2 * b.halo]
+
+    def band_last(self, tensors, i: int):
+        b = self.bands[i]
+        return tensors[i][b.owned:b.owned + b.halo]
+
+    # -- the step ------------------------------------------------------------------------------------
+    def train_pass(self, stream=None):
+        check(load().nt_invoke_training(C.byref(self.train_params()), N.NT_TRAIN_UNCONSTRAINED, _stream(stream)))
+
+    def adam(self, stream=None):
+        check(load().nt_invoke_optimize_all(C.byref(self.adam_params()), _stream(stream)))
+
+
+# ---- communication -----------------------------------------------------------------------------------
+
+class DistComm:
+    """Exchanges over torch.distributed (one process per rank)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+
+    def sendrecv(self, send, dst: int, recv, src: int):
+        dist = self.dist
+        ops = [dist.P2POp(dist.isend, send.contiguous(), dst, self.group),
+               dist.P2POp(dist.irecv, recv, src, self.group)]
+        for r in dist.batch_isend_irecv(ops):
+            r.wait()
+
+    def allreduce(self, t):
+        self.dist.all_reduce(t, group=self.group)
+
+
+def exchange_gradients(shard: ShardedTexture, comm):
+    """Halo gradients -> owners (added to their bands); halo gradients cleared."""
+    r, n = shard.rank, shard.world
+    if n == 1:
+        return
+    for i in range(2):
+        buf = shard.torch.empty_like(shard.band_last(shard.ggrads, i))
+        comm.sendrecv(shard.halo_above(shard.ggrads, i), (r - 1) % n, buf, (r + 1) % n)
+        shard.band_last(shard.ggrads, i).add_(buf)
+        buf = shard.torch.empty_like(shard.band_first(shard.ggrads, i))
+        comm.sendrecv(shard.halo_below(shard.ggrads, i), (r + 1) % n, buf, (r - 1) % n)
+        shard.band_first(shard.ggrads, i).add_(buf)
+        shard.halo_above(shard.ggrads, i).zero_()
+        shard.halo_below(shard.ggrads, i).zero_()
+
+
+def exchange_latents(shard: ShardedTexture, comm):
+    """Updated band edges -> the neighbours' halo rows."""
+    r, n = shard.rank, shard.world
+    if n == 1:
+        return
+    for i in range(2):
+        comm.sendrecv(shard.band_first(shard.grids, i), (r - 1) % n, shard.halo_below(shard.grids, i), (r + 1) % n)
+        comm.sendrecv(shard.band_last(shard.grids, i), (r + 1) % n, shard.halo_above(shard.grids, i), (r - 1) % n)
+
+
+def train_step(shard: ShardedTexture, comm, stream=None):
+    """One data-parallel step of the sharded material (every rank calls it)."""
+    shard.train_pass(stream)
+    exchange_gradients(shard, comm)
+    if shard.world > 1:
+        comm.allreduce(shard.net_grad)
+    shard.adam(stream)
+    exchange_latents(shard, comm)
+    shard.step += 1
+
+
+class LocalShards:
+    """All ranks of a sharded material in one process (several bands on one device): the
+    same exchanges as DistComm, done with copies.  Used to test the sharded step against
+    the unsharded one on a single GPU."""
+
+    def __init__(self, shards: list[ShardedTexture]):
+        self.shards = shards
+
+    def step(self, stream=None):
+        self.gradients(stream)
+        self.apply(stream)
+
+    def gradients(self, stream=None):
+        """Training passes, halo gradients to their owners, network gradients summed."""
+        sh = self.shards
+        n = len(sh)
+        for s in sh:
+            s.train_pass(stream)
+        for i in range(2):
+            above = [s.halo_above(s.ggrads, i).clone() for s in sh]
+            below = [s.halo_below(s.ggrads, i).clone() for s in sh]
+            for r, s in enumerate(sh):
+                s.band_last(s.ggrads, i).add_(above[(r + 1) % n])
+                s.band_first(s.ggrads, i).add_(below[(r - 1) % n])
+                s.halo_above(s.ggrads, i).zero_()
+                s.halo_below(s.ggrads, i).zero_()
+        total = sum(s.net_grad for s in sh)
+        for s in sh:
+            s.net_grad.copy_(total)
+
+    def apply(self, stream=None):
+        """Adam on every band and the network, then the halo rows refreshed."""
+        sh = self.shards
+        n = len(sh)
+        for s in sh:
+            s.adam(stream)
+        for i in range(2):
+            first = [s.band_first(s.grids, i).clone() for s in sh]
+            last = [s.band_last(s.grids, i).clone() for s in sh]
+            for r, s in enumerate(sh):
+                s.halo_below(s.grids, i).copy_(first[(r + 1) % n])
+                s.halo_above(s.grids, i).copy_(last[(r - 1) % n])
+        for s in sh:
+            s.step += 1
+
+    def gather(self, tensors_of, i: int):
+        """Full-height tensor of grid i assembled from the owned bands."""
+        return self.shards[0].torch.cat([s.band_view(tensors_of(s), i) for s in self.shards], 0)

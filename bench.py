@@ -35,6 +35,8 @@ CFG1 = dict(workload="config1_train_1024sq_8ch", image=(1024, 1024), grids=((512
             cout=8, lattice=(512, 512))
 CFG0 = dict(workload="config0_decode_1024sq_8ch", image=(1024, 1024), grids=((512, 512), (256, 256)), C=8,
             cout=8)
+CFG4B = dict(workload="config4b_sharded_16384sq_12ch", image=(16384, 16384), grids=((4096, 4096), (2048, 2048)),
+             C=12, cout=12, lattice=(2048, 2048))
 L2_FLUSH_BYTES = 256 << 20
 
 # algorithmic work per unit (basis of roofline.achieved)
@@ -248,6 +250,45 @@ def run_reference(args):
     return 0
 
 
+def run_config4b(torch, dist, dev, stream, rank, world, steps, warmup):
+    """BASELINE config 4b: one 16384^2 12-channel material, latent grids 4096^2x12 and
+    2048^2x12 split into row bands (one per rank), 4,194,304 samples per step across all
+    ranks; each step = training pass on the band, halo exchanges with the neighbours and
+    one allreduce of the network gradients over NCCL, Adam.  Strong scaling: the total
+    batch is fixed.  Each rank's state (>= 1.2 GB at 8 ranks) is far above the L2."""
+    from neural_textures_b200.sharded import DistComm, ShardedTexture, train_step
+    sh = ShardedTexture(rank, world, *CFG4B["image"], CFG4B["grids"], CFG4B["C"], CFG4B["cout"], CFG4B["lattice"],
+                        device=dev)
+    sh.init(seed=11)
+    comm = DistComm() if world > 1 else None
+    for _ in range(warmup):
+        train_step(sh, comm, stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        train_step(sh, comm, stream)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) / steps  # ms per step on this rank
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = tt.item()
+        dist.barrier()
+    B = CFG4B["lattice"][0] * CFG4B["lattice"][1]
+    out = {"workload": CFG4B["workload"], "value": B / (t * 1e-3), "unit": "samples/s", "ms_per_step": t,
+           "steps": steps, "warmup": warmup, "scaling": "strong", "global_batch": B,
+           "latents": "4096^2x12 + 2048^2x12 fp16, row bands per rank", "mlp": "32-64-64-12",
+           "parallelism": f"row shards x{world}: halo exchange (NCCL send/recv) + network-gradient allreduce",
+           "l2": "state per rank far above L2 (no flush)"}
+    del sh
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -258,6 +299,7 @@ def main():
     ap.add_argument("--prewarm", type=float, default=0.5, help="seconds of untimed steps before warm-up")
     ap.add_argument("--codec-iters", type=int, default=5, help="timed BC6H encode / decode passes (0: skip)")
     ap.add_argument("--decode-iters", type=int, default=200)
+    ap.add_argument("--sharded-steps", type=int, default=20, help="timed config-4b sharded steps (0: skip)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -375,7 +417,10 @@ def main():
     codec = None
     if args.codec_iters > 0:
         codec = run_codec_bench(torch, dev, stream, L, args.codec_iters, rank, world, dist)
-    clk = clocks.stop()  # sampled across the timed training, e2e, decode and codec regions
+    cfg4b = None
+    if args.sharded_steps > 0:
+        cfg4b = run_config4b(torch, dist, dev, stream, rank, world, args.sharded_steps, 10)
+    clk = clocks.stop()  # sampled across the timed training, e2e, decode, codec and config-4b regions
     texels = CFG0["image"][0] * CFG0["image"][1]
 
     if world > 1:
@@ -425,6 +470,8 @@ def main():
         codec["decode_traffic"] = tr.get("bc6h_decode_kernel", {}).get("bytes_per_launch")
         codec["encode_traffic"] = tr.get("bc6h_encode_kernel", {}).get("bytes_per_launch")
         line["codec"] = codec
+    if cfg4b:
+        line["config4b"] = cfg4b
     if not args.no_cpu_baseline:
         from oracle import oracle as O
         O.build()

@@ -255,10 +255,14 @@ class DistComm:
         self.dist = dist
         self.group = group
 
-    def sendrecv(self, send, dst: int, recv, src: int):
+    def exchange(self, sends, recvs):
+        """One batched group: sends [(tensor, dst)], recvs [(tensor, src)].  Every rank posts
+        its operations in the same order, so the k-th send to a peer meets that peer's k-th
+        receive from this rank (which keeps two ranks, where both neighbours are the same
+        peer, unambiguous)."""
         dist = self.dist
-        ops = [dist.P2POp(dist.isend, send.contiguous(), dst, self.group),
-               dist.P2POp(dist.irecv, recv, src, self.group)]
+        ops = [dist.P2POp(dist.isend, t, d, self.group) for t, d in sends]
+        ops += [dist.P2POp(dist.irecv, t, s, self.group) for t, s in recvs]
         for r in dist.batch_isend_irecv(ops):
             r.wait()
 
@@ -266,30 +270,46 @@ class DistComm:
         self.dist.all_reduce(t, group=self.group)
 
 
-def exchange_gradients(shard: ShardedTexture, comm):
+def _rx(shard, key, like):
+    """Receive buffer kept on the shard across steps."""
+    bufs = shard.__dict__.setdefault("_rx", {})
+    if key not in bufs:
+        bufs[key] = shard.torch.empty_like(like)
+    return bufs[key]
+
+
+def exchange_gradients(shard, comm):
     """Halo gradients -> owners (added to their bands); halo gradients cleared."""
     r, n = shard.rank, shard.world
     if n == 1:
         return
+    up, dn = (r - 1) % n, (r + 1) % n
+    sends, recvs, adds = [], [], []
     for i in range(2):
-        buf = shard.torch.empty_like(shard.band_last(shard.ggrads, i))
-        comm.sendrecv(shard.halo_above(shard.ggrads, i), (r - 1) % n, buf, (r + 1) % n)
-        shard.band_last(shard.ggrads, i).add_(buf)
-        buf = shard.torch.empty_like(shard.band_first(shard.ggrads, i))
-        comm.sendrecv(shard.halo_below(shard.ggrads, i), (r + 1) % n, buf, (r - 1) % n)
-        shard.band_first(shard.ggrads, i).add_(buf)
+        sends += [(shard.halo_above(shard.ggrads, i), up), (shard.halo_below(shard.ggrads, i), dn)]
+        a, b = _rx(shard, ("g", i, 0), shard.band_last(shard.ggrads, i)), _rx(shard, ("g", i, 1),
+                                                                              shard.band_first(shard.ggrads, i))
+        recvs += [(a, dn), (b, up)]  # dn's halo above = my last rows; up's halo below = my first rows
+        adds += [(shard.band_last(shard.ggrads, i), a), (shard.band_first(shard.ggrads, i), b)]
+    comm.exchange(sends, recvs)
+    for dst, src in adds:
+        dst.add_(src)
+    for i in range(2):
         shard.halo_above(shard.ggrads, i).zero_()
         shard.halo_below(shard.ggrads, i).zero_()
 
 
-def exchange_latents(shard: ShardedTexture, comm):
+def exchange_latents(shard, comm):
     """Updated band edges -> the neighbours' halo rows."""
     r, n = shard.rank, shard.world
     if n == 1:
         return
+    up, dn = (r - 1) % n, (r + 1) % n
+    sends, recvs = [], []
     for i in range(2):
-        comm.sendrecv(shard.band_first(shard.grids, i), (r - 1) % n, shard.halo_below(shard.grids, i), (r + 1) % n)
-        comm.sendrecv(shard.band_last(shard.grids, i), (r + 1) % n, shard.halo_above(shard.grids, i), (r - 1) % n)
+        sends += [(shard.band_first(shard.grids, i), up), (shard.band_last(shard.grids, i), dn)]
+        recvs += [(shard.halo_below(shard.grids, i), dn), (shard.halo_above(shard.grids, i), up)]
+    comm.exchange(sends, recvs)
 
 
 def train_step(shard: ShardedTexture, comm, stream=None):

@@ -99,7 +99,7 @@ struct Smem {
     int32_t colext[2][2][kTileW];
     int32_t rowmin[2][kTileH];
     Window win[2];
-    alignas(8) uint64_t done;
+    alignas(8) uint64_t done, dwdone;  // stage products; weight-gradient products of B3 / B2 / B1
     uint32_t tmem_base;
     float red[kThreadsTC / 32];
 };
@@ -347,7 +347,10 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
 
 // TMEM row (32 columns) rounded to fp16 and masked by the ReLU of the activation row stored
 // at the same place in H (lanes where the activation is not > 0 become +0), written over it.
-__device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0)
+// `wbar` / `wph`: products that still read H (the weight gradients) are waited for right
+// before the stores, so the TMEM and shared loads overlap them.
+__device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0, uint32_t wbar,
+                                             uint32_t wph, bool &failed)
 {
     uint32_t v[32];
     umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
@@ -366,6 +369,10 @@ __device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, 
             const __half2 g = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
             const unsigned m = __hgt2_mask(*reinterpret_cast<const __half2 *>(&aw[e]), zero);
             h[e] = *reinterpret_cast<const uint32_t *>(&g) & m;
+        }
+        if (q == 0 && !umma::mbar_wait(wbar, wph, kSpinLimit)) {
+            failed = true;
+            atomicOr(&g_device_status, 1u);
         }
         st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
     }
@@ -508,7 +515,8 @@ __device__ __forceinline__ Descs<C> make_descs(const Smem<C> &s)
 
 // Issue the products of one stage (thread 0 only) and commit them to `done`.
 template <int C>
-__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done)
+__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done,
+                                            uint32_t dwdone)
 {
     using K = Cfg<C>;
     using umma::idesc_f16;
@@ -534,20 +542,24 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
         break;
     case 3:  // B3: dH2 = dY W3; dW3^T += H2e^T dY
         mma_f16(R, d.dy, d.w3_mn, idesc_f16(128, 64, 0, 1), 0);
+        umma::commit(done);  // the epilogue needs dH2 only; the weight gradients follow
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
             mma_f16(tmem + kColW3, dadv(d.h2_mn, ks * 2 * HG), dadv(d.dy_mn, ks * 512), idesc_f16(128, 16, 1, 1),
                     ks > 0 ? 1u : acc0);
-        break;
+        umma::commit(dwdone);
+        return;
     case 4:  // B2: dH1 = dZ2 W2; dW2 += dZ2^T H1e
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
             mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w2_mn, ks * 2 * HG), idesc_f16(128, 64, 0, 1), ks > 0);
+        umma::commit(done);
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
             mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
                     ks > 0 ? 1u : acc0);
-        break;
+        umma::commit(dwdone);
+        return;
     case 6:  // latent scatter: G0^T = Q0^T A0 (M128 N32), G1^T = Q1^T A1 (M64 N16), K = 128 samples
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
@@ -562,11 +574,13 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
             mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w1_mn, ks * 2 * XG), idesc_f16(128, K::NX, 0, 1), ks > 0);
+        umma::commit(done);
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
             mma_f16(tmem + kColW1, dadv(d.h1_mn, ks * 2 * HG), dadv(d.x_mn, ks * 2 * XG), idesc_f16(64, K::XW, 1, 1),
                     ks > 0 ? 1u : acc0);
-        break;
+        umma::commit(dwdone);
+        return;
     }
     umma::commit(done);
 }
@@ -577,7 +591,7 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
 // times out is recorded and reaches the other threads at the next barrier.
 template <int C>
 __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done,
-                                          uint32_t &ph, bool &failed, int tid)
+                                          uint32_t dwdone, uint32_t &ph, bool &failed, int tid)
 {
     umma::fence_async_smem();
     umma::fence_before();
@@ -586,7 +600,7 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
         return false;
     }
     umma::fence_after();
-    if (tid == 0) issue_stage<C>(stage, d, tmem, first, done);
+    if (tid == 0) issue_stage<C>(stage, d, tmem, first, done, dwdone);
     if (!umma::mbar_wait(done, ph, kSpinLimit)) {
         failed = true;
         atomicOr(&g_device_status, 1u);
@@ -614,6 +628,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     if (warp == 0) umma::alloc(smem_addr(&s.tmem_base), kTmemCols);
     if (tid == 0) {
         umma::mbar_init(smem_addr(&s.done), 1);
+        umma::mbar_init(smem_addr(&s.dwdone), 1);
         umma::mbar_fence_init();
     }
     umma::fence_async_smem();
@@ -622,7 +637,8 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     umma::fence_after();
     const uint32_t tmem = s.tmem_base;
     const uint32_t Rl = tmem + kColTile + ((uint32_t)(32 * (warp & 3)) << 16);  // this warp's lanes
-    const uint32_t done = smem_addr(&s.done);
+    const uint32_t done = smem_addr(&s.done), dwdone = smem_addr(&s.dwdone);
+    uint32_t dph = 0;  // parity of the next weight-gradient completion
     const Descs<C> d = make_descs<C>(s);
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cout = p.net.cout;
@@ -692,7 +708,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
             }
         }
-        if (!run_stage<C>(0, d, tmem, first, done, ph, failed, tid)) break;  // F1
+        if (!run_stage<C>(0, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // F1
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
         relu_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
@@ -700,7 +716,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             st16(s.t.m.H1, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
         else
             st16(s.t.m.H1, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
-        if (!run_stage<C>(1, d, tmem, first, done, ph, failed, tid)) break;  // F2
+        if (!run_stage<C>(1, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // F2
 
         // ---- E2: H2e ------------------------------------------------------------------------
         relu_store32(Rl + 32 * half, s.t.m.H2, r, 4 * half);
@@ -708,7 +724,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             st16(s.t.m.H2, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
         else
             st16(s.t.m.H2, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
-        if (!run_stage<C>(2, d, tmem, first, done, ph, failed, tid)) break;  // F3
+        if (!run_stage<C>(2, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // F3
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
         // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
@@ -736,17 +752,25 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             st16(s.t.m.DY, umma::cm_offset(r, 0, 2), out[0], out[1], out[2], out[3]);
             st16(s.t.m.DY, umma::cm_offset(r, 8, 2), out[4], out[5], out[6], out[7]);
         }
-        if (!run_stage<C>(3, d, tmem, first, done, ph, failed, tid)) break;  // B3
+        if (!run_stage<C>(3, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // B3
 
         // ---- E4: dZ2 = dH2 * [H2 > 0] (in place of H2) -----------------------------------
-        mask_store32(Rl + 32 * half, s.t.m.H2, r, 4 * half);
-        if (!run_stage<C>(4, d, tmem, first, done, ph, failed, tid)) break;  // B2
+        mask_store32(Rl + 32 * half, s.t.m.H2, r, 4 * half, dwdone, dph, failed);  // after dW3 (reads H2)
+        dph ^= 1u;
+        if (!run_stage<C>(4, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // B2
 
         // ---- E5: dZ1 = dH1 * [H1 > 0] (in place of H1) -----------------------------------
-        mask_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
-        if (!run_stage<C>(5, d, tmem, first, done, ph, failed, tid)) break;  // B1
+        mask_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half, dwdone, dph, failed);  // after dW2 (reads H1)
+        dph ^= 1u;
+        if (!run_stage<C>(5, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // B1
 
         // ---- E6: dX -> shared (fp32 rows over the dead H2 tile) -> latent gradients ------
+        // dW1 (reads X and dZ1) must finish before anything below or the next tile writes them
+        if (!umma::mbar_wait(dwdone, dph, kSpinLimit)) {
+            failed = true;
+            atomicOr(&g_device_status, 1u);
+        }
+        dph ^= 1u;
         if (!p.finalize) {
             // dX columns [half * C, half * C + C): the latents of grid `half`
             float dxv[C];
@@ -765,7 +789,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     if (half) scatter_rows<C, 1>(s, r, valid, dxv);
                     else scatter_rows<C, 0>(s, r, valid, dxv);
                 }
-                if (!run_stage<C>(6, d, tmem, first, done, ph, failed, tid)) break;  // scatter product
+                if (!run_stage<C>(6, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // scatter product
                 scatter_stage_out<C>(s, tmem, warp, lane, half);
                 if (__syncthreads_or(failed)) {
                     failed = true;

@@ -87,18 +87,35 @@ __device__ __forceinline__ uint16_t finish_unquantize(int comp, bool is_signed)
     return (uint16_t)(s | comp);
 }
 
+// Mode index of each 5-bit mode value (-1: reserved), built from the mode table.
+struct ModeOf5 {
+    int8_t v[32];
+};
+constexpr ModeOf5 make_mode_of5()
+{
+    constexpr NtBc6hMode m[NT_BC6H_NUM_MODES] = NT_BC6H_MODES_INIT;
+    ModeOf5 t{};
+    for (int i = 0; i < 32; ++i) t.v[i] = -1;
+    for (int i = 2; i < NT_BC6H_NUM_MODES; ++i) t.v[m[i].mode_value & 31] = (int8_t)i;
+    return t;
+}
+__device__ const ModeOf5 c_mode_of5 = make_mode_of5();
+
 __device__ __forceinline__ int mode_index(const Block128 &b)
 {
     const int m2 = b.w[0] & 3;
-    if (m2 < 2) return m2;
-    const int m5 = b.w[0] & 31;
-#pragma unroll 1
-    for (int i = 2; i < NT_BC6H_NUM_MODES; ++i)
-        if (c_modes[i].mode_value == m5) return i;
-    return -1;
+    return m2 < 2 ? m2 : c_mode_of5.v[b.w[0] & 31];
 }
 
-__device__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48])
+// Interpolation weight of index i: round(64 i / 7) for 3-bit and round(64 i / 15) for 4-bit
+// indices, the BC6H weight tables (equal to NT_BC6H_WEIGHTS3_INIT / NT_BC6H_WEIGHTS4_INIT
+// for every index; tests/test_codec_cpu.py checks the tables against the same formula).
+__device__ __forceinline__ int bc6h_weight(int idx, bool three_bit)
+{
+    return three_bit ? (128 * idx + 7) / 14 : (128 * idx + 15) / 30;
+}
+
+__device__ __forceinline__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48])
 {
     const int mi = mode_index(b);
     if (mi < 0) {
@@ -107,10 +124,10 @@ __device__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48]
         return;
     }
     const NtBc6hMode M = c_modes[mi];
+    const uint64_t lo = (uint64_t)b.w[0] | ((uint64_t)b.w[1] << 32), hi = (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32);
     int e[4][3];
     int d = 0;
-    bc6h_unpack_header(mi, (uint64_t)b.w[0] | ((uint64_t)b.w[1] << 32), (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32),
-                       e, d);
+    bc6h_unpack_header(mi, lo, hi, e, d);
     const int ne = 2 * M.regions, epb = M.endpoint_bits;
 #pragma unroll
     for (int c = 0; c < 3; ++c) {
@@ -128,21 +145,31 @@ __device__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48]
         for (int i = 0; i < 4; ++i)
             if (i < ne) e[i][c] = unquantize(e[i][c], epb, is_signed);
     }
-    const int ib = M.regions == 2 ? 3 : 4;
-    const int anchor1 = M.regions == 2 ? c_anchors[d] : -1;
-    const uint16_t pmask = M.regions == 2 ? c_parts[d] : 0;
-    int pos = M.header_bits;
+    const bool two = M.regions == 2;
+    const int ib = two ? 3 : 4;
+    const int anchor1 = two ? c_anchors[d] : -1;
+    const uint32_t pmask = two ? c_parts[d] : 0u;
+    // the index bits follow the header (82 or 65 bits, so all within the high word)
+    uint64_t s = hi >> (M.header_bits - 64);
+    // a (64 - w) + b w = 64 a + (b - a) w, and an arithmetic shift floors, so
+    // (a (64 - w) + b w + 32) >> 6 == a + (((b - a) w + 32) >> 6) exactly
+    int dl[2][3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        dl[0][c] = e[1][c] - e[0][c];
+        dl[1][c] = e[3][c] - e[2][c];
+    }
 #pragma unroll
     for (int px = 0; px < 16; ++px) {
         const int nb = ib - ((px == 0 || px == anchor1) ? 1 : 0);
-        const int idx = b.bits(pos, nb);
-        pos += nb;
+        const int idx = (int)(s & ((1u << nb) - 1u));
+        s >>= nb;
+        const int w = bc6h_weight(idx, two);
         const int r = (pmask >> px) & 1;
-        const int w = ib == 3 ? c_w3[idx & 7] : c_w4[idx & 15];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-            const int a = r ? e[2][c] : e[0][c], bb = r ? e[3][c] : e[1][c];
-            out[px * 3 + c] = finish_unquantize((a * (64 - w) + bb * w + 32) >> 6, is_signed);
+            const int a = r ? e[2][c] : e[0][c], dd = r ? dl[1][c] : dl[0][c];
+            out[px * 3 + c] = finish_unquantize(a + ((dd * w + 32) >> 6), is_signed);
         }
     }
 }
@@ -515,13 +542,17 @@ __global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
                 if (ch >= p.channels) break;
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    uint16_t v[4];
+                    uint32_t v2[2];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        v[i] = __half_as_ushort(
-                            __float2half_rn(__half2float(__ushort_as_half(tex[(r * 4 + i) * 3 + c])) - p.bias));
+                    for (int i = 0; i < 2; ++i) {
+                        // half -> float - bias -> half, two texels per packed conversion
+                        const float2 f = __half22float2(__halves2half2(__ushort_as_half(tex[(r * 4 + 2 * i) * 3 + c]),
+                                                                       __ushort_as_half(tex[(r * 4 + 2 * i + 1) * 3 + c])));
+                        const __half2 o = __floats2half2_rn(f.x - p.bias, f.y - p.bias);
+                        v2[i] = *reinterpret_cast<const uint32_t *>(&o);
+                    }
                     *reinterpret_cast<uint2 *>(p.data + ch * p.cstride + (int64_t)(by * 4 + r) * p.rstride + bx * 4) =
-                        make_uint2(v[0] | ((uint32_t)v[1] << 16), v[2] | ((uint32_t)v[3] << 16));
+                        make_uint2(v2[0], v2[1]);
                 }
             }
             continue;

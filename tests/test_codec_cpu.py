@@ -12,6 +12,13 @@ def test_format_tables_are_consistent():
     assert [m[2] for m in F.MODES[:10]] == [10, 7, 11, 11, 11, 9, 8, 8, 8, 6]
 
 
+def test_weight_tables_follow_the_rounding_formula():
+    # the CUDA decoder computes the weights as round(64 i / (n - 1)) instead of loading them
+    from neural_textures_b200 import bc6h_format as F
+    assert F.WEIGHTS3 == [(128 * i + 7) // 14 for i in range(8)]
+    assert F.WEIGHTS4 == [(128 * i + 15) // 30 for i in range(16)]
+
+
 def test_generated_header_is_current():
     import os
     from neural_textures_b200 import bc6h_format as F

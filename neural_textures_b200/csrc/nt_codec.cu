@@ -27,8 +27,6 @@ __device__ const NtBc6hMode c_modes[NT_BC6H_NUM_MODES] = NT_BC6H_MODES_INIT;
 __device__ const uint8_t c_layout[NT_BC6H_NUM_MODES][82] = NT_BC6H_LAYOUT_INIT;
 __device__ const uint16_t c_parts[32] = NT_BC6H_PARTITIONS_INIT;
 __device__ const uint8_t c_anchors[32] = NT_BC6H_ANCHORS_INIT;
-__device__ const uint8_t c_w3[8] = NT_BC6H_WEIGHTS3_INIT;
-__device__ const uint8_t c_w4[16] = NT_BC6H_WEIGHTS4_INIT;
 
 struct Block128 {
     uint32_t w[4];
@@ -256,20 +254,34 @@ __device__ __forceinline__ int project_index(const int x[3], const int a[3], con
     }
     if (len2 == 0) return 0;
     const float t = __fdiv_rn(__fmul_rn(__ll2float_rn(dot), 64.0f), __ll2float_rn(len2));
+    // k0 = #{k >= 1 : t > mid_k} with mid_k = (w_{k-1} + w_k) / 2 (increasing in k): start from
+    // the nearest weight and step across the exact midpoints, which gives the same count as
+    // testing every midpoint
     const int ni = 1 << ib;
-    int k0 = 0;
+    const bool three = ib == 3;
+    const float tc = fminf(fmaxf(t, 0.f), 64.f);
+    int k0 = (int)(tc * (float)(ni - 1) * (1.f / 64.f) + 0.5f);
+    k0 = min(max(k0, 0), ni - 1);
+    auto mid = [&](int k) { return 0.5f * (float)(bc6h_weight(k - 1, three) + bc6h_weight(k, three)); };
 #pragma unroll 1
-    for (int k = 1; k < ni; ++k) {
-        const float mid = 0.5f * (float)(ib == 3 ? c_w3[k - 1] + c_w3[k] : c_w4[k - 1] + c_w4[k]);
-        if (t > mid) k0 = k;
-    }
+    while (k0 < ni - 1 && t > mid(k0 + 1)) ++k0;
+#pragma unroll 1
+    while (k0 > 0 && !(t > mid(k0))) --k0;
     return k0;
 }
 
-// Evaluate (and pack) one candidate; returns the squared error or -1 when the mode cannot
-// hold the endpoints.
+// One evaluated candidate: stored endpoints (after the delta transform), indices (4 bits
+// each), mode and partition.
+struct Cand {
+    int e[4][3];
+    uint64_t idx;
+    int mi, part;
+};
+
+// Evaluate one candidate; returns the squared error or -1 when the mode cannot hold the
+// endpoints.  Only the winner of the search is packed (pack_block).
 __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2][3], const int B[2][3],
-                            Block128 &out)
+                            Cand &out)
 {
     const NtBc6hMode M = c_modes[mi];
     const int regions = M.regions, epb = M.endpoint_bits, ib = regions == 2 ? 3 : 4;
@@ -311,7 +323,7 @@ __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2]
             for (int dk = -1; dk <= 1; ++dk) {
                 const int kk = k0 + dk;
                 if (kk < 0 || kk >= ni) continue;
-                const int w = ib == 3 ? c_w3[kk] : c_w4[kk];
+                const int w = bc6h_weight(kk, ib == 3);
                 int64_t dsum = 0;
 #pragma unroll
                 for (int c = 0; c < 3; ++c) {
@@ -369,6 +381,34 @@ __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2]
             }
         }
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) out.e[i][c] = e[i][c];
+    uint64_t pk = 0;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) pk |= (uint64_t)idx[px] << (4 * px);
+    out.idx = pk;
+    out.mi = mi;
+    out.part = part;
+    return err;
+}
+
+// Bitstream of a candidate: header fields through the mode's bit layout, then the indices
+// (anchor indices one bit shorter).
+__device__ void pack_block(const Cand &cd, Block128 &out)
+{
+    const int mi = cd.mi, part = cd.part;
+    const NtBc6hMode M = c_modes[mi];
+    const int regions = M.regions, ib = regions == 2 ? 3 : 4;
+    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
+    int e[4][3], idx[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) e[i][c] = cd.e[i][c];
+#pragma unroll
+    for (int px = 0; px < 16; ++px) idx[px] = (int)((cd.idx >> (4 * px)) & 15u);
     out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
 #pragma unroll 1
     for (int k = 0; k < M.header_bits; ++k) {
@@ -393,7 +433,6 @@ __device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2]
         for (int bb = 0; bb < nb; ++bb) out.set(pos + bb, (idx[px] >> bb) & 1);
         pos += nb;
     }
-    return err;
 }
 
 __device__ void encode_block(const uint16_t tex[48], Block128 &out)
@@ -404,7 +443,7 @@ __device__ void encode_block(const uint16_t tex[48], Block128 &out)
 #pragma unroll
         for (int c = 0; c < 3; ++c) x[px][c] = to_domain(tex[px * 3 + c]);
     int64_t best = INT64_MAX;
-    Block128 cand;
+    Cand cand, winner;
     int A[2][3], B[2][3];
     fit_endpoints(x, 0u, 0, A[0], B[0]);
 #pragma unroll
@@ -414,7 +453,7 @@ __device__ void encode_block(const uint16_t tex[48], Block128 &out)
         const int64_t e = try_mode(mi, 0, x, A, B, cand);
         if (e >= 0 && e < best) {
             best = e;
-            out = cand;
+            winner = cand;
         }
     }
     int bp = 0;
@@ -453,10 +492,11 @@ __device__ void encode_block(const uint16_t tex[48], Block128 &out)
         const int64_t e = try_mode(mi, bp, x, A, B, cand);
         if (e >= 0 && e < best) {
             best = e;
-            out = cand;
+            winner = cand;
         }
     }
     if (best == INT64_MAX) out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
+    else pack_block(winner, out);
 }
 
 struct CodecLaunch {

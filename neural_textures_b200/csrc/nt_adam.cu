@@ -25,7 +25,8 @@ __device__ __forceinline__ float adam_one(float w, float g, float &m, float &v, 
 }
 
 constexpr int kAdamThreads = 256;
-constexpr int kAdamPerThread = 8;
+constexpr int kAdamPerThread = 4;
+static_assert(kAdamThreads * kAdamPerThread == kAdamChunk, "chunk size shared with the host");
 
 // One chunk (kAdamThreads x kAdamPerThread consecutive entries of one segment).
 __device__ __forceinline__ void adam_chunk(const AdamLaunch &p, int b)
@@ -36,39 +37,30 @@ __device__ __forceinline__ void adam_chunk(const AdamLaunch &p, int b)
     const AdamSegment &s = p.seg[si];
     const int64_t i0 = ((int64_t)(b - s.first_block) * kAdamThreads + threadIdx.x) * kAdamPerThread;
     if (i0 >= s.n) return;
-    const bool vec = i0 + kAdamPerThread <= s.n && ((reinterpret_cast<uintptr_t>(s.w) & 15) == 0) &&
+    const bool vec = i0 + kAdamPerThread <= s.n && ((reinterpret_cast<uintptr_t>(s.w) & 7) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.g) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.m) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.v) & 15) == 0);
     if (vec) {
-        // all five streams are requested before any value is used (one memory round trip)
+        // all four streams are requested before any value is used (one memory round trip)
         const float4 g0 = *reinterpret_cast<const float4 *>(s.g + i0);
-        const float4 g1 = *reinterpret_cast<const float4 *>(s.g + i0 + 4);
-        uint4 wraw = *reinterpret_cast<const uint4 *>(s.w + i0);
+        uint2 wraw = *reinterpret_cast<const uint2 *>(s.w + i0);
         const float4 m0 = *reinterpret_cast<const float4 *>(s.m + i0);
-        const float4 m1 = *reinterpret_cast<const float4 *>(s.m + i0 + 4);
         const float4 v0 = *reinterpret_cast<const float4 *>(s.v + i0);
-        const float4 v1 = *reinterpret_cast<const float4 *>(s.v + i0 + 4);
-        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        bool any = false;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) any |= gv[e] != 0.f;
-        if (!any) return;  // nothing to update, nothing to zero
-        float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-        float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        const float gv[4] = {g0.x, g0.y, g0.z, g0.w};
+        if (gv[0] == 0.f && gv[1] == 0.f && gv[2] == 0.f && gv[3] == 0.f) return;  // nothing to update or zero
+        float mv[4] = {m0.x, m0.y, m0.z, m0.w};
+        float vv[4] = {v0.x, v0.y, v0.z, v0.w};
         __half *wh = reinterpret_cast<__half *>(&wraw);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
+        for (int e = 0; e < 4; ++e) {
             if (gv[e] == 0.f) continue;
             wh[e] = __float2half_rn(adam_one(__half2float(wh[e]), gv[e], mv[e], vv[e], s));
         }
-        *reinterpret_cast<uint4 *>(s.w + i0) = wraw;
+        *reinterpret_cast<uint2 *>(s.w + i0) = wraw;
         *reinterpret_cast<float4 *>(s.m + i0) = make_float4(mv[0], mv[1], mv[2], mv[3]);
-        *reinterpret_cast<float4 *>(s.m + i0 + 4) = make_float4(mv[4], mv[5], mv[6], mv[7]);
         *reinterpret_cast<float4 *>(s.v + i0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
-        *reinterpret_cast<float4 *>(s.v + i0 + 4) = make_float4(vv[4], vv[5], vv[6], vv[7]);
         *reinterpret_cast<float4 *>(s.g + i0) = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4 *>(s.g + i0 + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
     } else {
         const int64_t end = i0 + kAdamPerThread < s.n ? i0 + kAdamPerThread : s.n;
         for (int64_t i = i0; i < end; ++i) {

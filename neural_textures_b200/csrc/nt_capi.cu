@@ -143,7 +143,7 @@ static void finalize_adam(AdamLaunch &a)
     int blocks = 0;
     for (int i = 0; i < a.nseg; ++i) {
         a.seg[i].first_block = blocks;
-        blocks += (int)((a.seg[i].n + 256 * 8 - 1) / (256 * 8));
+        blocks += (int)((a.seg[i].n + kAdamChunk - 1) / kAdamChunk);
     }
     a.total_blocks = blocks;
 }

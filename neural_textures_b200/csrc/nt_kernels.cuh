@@ -52,6 +52,7 @@ struct DecodeLaunch {
 };
 
 constexpr int kMaxAdamSegments = 8;
+constexpr int kAdamChunk = 1024;  // parameters per Adam CTA
 
 struct AdamSegment {
     __half *w;

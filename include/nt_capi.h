@@ -97,6 +97,10 @@ typedef struct NtFeature {
 
 /* train.h:120-157.  Passed by pointer; the library copies what it needs at launch, so the
  * struct may be modified or freed as soon as the call returns. */
+/* Latent representations (NtKernelParams.latent_format). */
+#define NT_LATENT_GRID_F16 0
+#define NT_LATENT_BC6_BLOCKS 1
+
 typedef struct NtKernelParams {
     NtFeature features[NT_NUM_FEATURES];
     int32_t latent_channels;   /* C per grid: 8 or 12 */
@@ -154,6 +158,14 @@ typedef struct NtKernelParams {
      * outside them is skipped and sets bit 1 of the device status word. */
     int32_t lattice_row0, lattice_rows;
     int32_t row_origin[3], stored_rows[3];
+
+    /* Latent representation (train.h:29-64 keeps both in Feature): NT_LATENT_GRID_F16 (0)
+     * fp16 channel-interleaved grids, or NT_LATENT_BC6_BLOCKS (1) BC6 block features: per
+     * 4x4 block, ceil(C / 3) channel triples of 32 floats (endpoints e0..e3 xyz, 16 pixel
+     * indices, partition and mode as int32 bits, 2 unused), gradients and moments in the same
+     * layout, decoded with the reference's float BC6 decode (train.cu:161-261, :436-454).
+     * UNCONSTRAINED trains grids, BLOCK_FEATURES trains blocks, FINALIZE samples either. */
+    int32_t latent_format;
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */

@@ -23,6 +23,8 @@ STATUS_NAMES = {0: "NT_OK", 1: "NT_ERR_INVALID_ARG", 2: "NT_ERR_CUDA", 3: "NT_ER
 NT_TRAIN_UNCONSTRAINED = 0
 NT_TRAIN_BLOCK_FEATURES = 1
 NT_TRAIN_FINALIZE = 2
+NT_LATENT_GRID_F16 = 0
+NT_LATENT_BC6_BLOCKS = 1
 NT_DTYPE_F16 = 0
 NT_DTYPE_F32 = 1
 
@@ -73,6 +75,7 @@ class NtKernelParams(C.Structure):
         ("lattice_rows", C.c_int32),
         ("row_origin", C.c_int32 * 3),
         ("stored_rows", C.c_int32 * 3),
+        ("latent_format", C.c_int32),
     ]
 
 

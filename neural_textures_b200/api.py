@@ -194,6 +194,19 @@ class NeuralTexture:
         self.channel_weights = [1.0] * self.cout
         self.seed = 0
         self.step = 0
+        self.latent_format = N.NT_LATENT_GRID_F16
+        self.blocks = None  # BC6 block-feature records per grid (fp32), when latent_format is 1
+
+    def use_blocks(self, records):
+        """Switch the latents to BC6 block features: `records` holds, per grid, the fp32
+        records (ceil(C / 3) triples of 32 floats per 4x4 block, nt_capi.h latent_format).
+        Gradients and Adam moments of the records are allocated here, zeroed."""
+        torch = self.torch
+        self.blocks = [torch.as_tensor(np.ascontiguousarray(r, np.float32)).to(self.device) for r in records]
+        self.ggrads = [torch.zeros_like(b) for b in self.blocks]
+        self.gm1 = [torch.zeros_like(b) for b in self.blocks]
+        self.gm2 = [torch.zeros_like(b) for b in self.blocks]
+        self.latent_format = N.NT_LATENT_BC6_BLOCKS
 
     # -- initialisation -------------------------------------------------------------------
     def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False,
@@ -233,7 +246,7 @@ class NeuralTexture:
         p = NtKernelParams()
         for i in range(2):
             f = p.features[i]
-            f.grid = self.grids[i].data_ptr()
+            f.grid = (self.blocks[i] if self.latent_format == N.NT_LATENT_BC6_BLOCKS else self.grids[i]).data_ptr()
             f.gradients = self.ggrads[i].data_ptr()
             f.moment1 = self.gm1[i].data_ptr()
             f.moment2 = self.gm2[i].data_ptr()
@@ -267,6 +280,7 @@ class NeuralTexture:
         p.sample_stride_y = self.image_h / self.lattice[1]
         p.num_samples = self.lattice[0] * self.lattice[1]
         p.step = self.step if step is None else step
+        p.latent_format = self.latent_format
         p.seed = self.seed
         if loss_accum:
             p.loss_accum = self.loss_accum.data_ptr()

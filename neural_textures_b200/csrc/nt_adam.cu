@@ -37,6 +37,38 @@ __device__ __forceinline__ void adam_chunk(const AdamLaunch &p, int b)
     const AdamSegment &s = p.seg[si];
     const int64_t i0 = ((int64_t)(b - s.first_block) * kAdamThreads + threadIdx.x) * kAdamPerThread;
     if (i0 >= s.n) return;
+    if (s.w32) {  // fp32 parameters (AdamUpdateFloatParameter, train.cu:545-564)
+        if (i0 + kAdamPerThread <= s.n && ((reinterpret_cast<uintptr_t>(s.w32) | reinterpret_cast<uintptr_t>(s.g) |
+                                             reinterpret_cast<uintptr_t>(s.m) | reinterpret_cast<uintptr_t>(s.v)) &
+                                            15) == 0) {
+            const float4 g4 = *reinterpret_cast<const float4 *>(s.g + i0);
+            float4 w4 = *reinterpret_cast<const float4 *>(s.w32 + i0);
+            float4 m4 = *reinterpret_cast<const float4 *>(s.m + i0);
+            float4 v4 = *reinterpret_cast<const float4 *>(s.v + i0);
+            if (g4.x == 0.f && g4.y == 0.f && g4.z == 0.f && g4.w == 0.f) return;
+            float *wv = &w4.x, *mv = &m4.x, *vv = &v4.x;
+            const float gv[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (gv[e] != 0.f) wv[e] = adam_one(wv[e], gv[e], mv[e], vv[e], s);
+            *reinterpret_cast<float4 *>(s.w32 + i0) = w4;
+            *reinterpret_cast<float4 *>(s.m + i0) = m4;
+            *reinterpret_cast<float4 *>(s.v + i0) = v4;
+            *reinterpret_cast<float4 *>(s.g + i0) = make_float4(0.f, 0.f, 0.f, 0.f);
+            return;
+        }
+        const int64_t end = i0 + kAdamPerThread < s.n ? i0 + kAdamPerThread : s.n;
+        for (int64_t i = i0; i < end; ++i) {
+            const float g = s.g[i];
+            if (g == 0.f) continue;
+            float m = s.m[i], v = s.v[i];
+            s.w32[i] = adam_one(s.w32[i], g, m, v, s);
+            s.m[i] = m;
+            s.v[i] = v;
+            s.g[i] = 0.f;
+        }
+        return;
+    }
     const bool vec = i0 + kAdamPerThread <= s.n && ((reinterpret_cast<uintptr_t>(s.w) & 7) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.g) & 15) == 0) &&
                      ((reinterpret_cast<uintptr_t>(s.m) & 15) == 0) &&

@@ -103,6 +103,11 @@ static nt_status validate_network(const NtKernelParams *p)
         NT_REQUIRE(ft.width <= 32767 && ft.height <= 32767, "features[%d] is wider than 32767 texels", f);
         NT_REQUIRE((int64_t)ft.width * ft.height * p->latent_channels < (int64_t)1 << 31,
                    "features[%d] is too large", f);
+        NT_REQUIRE(p->latent_format == NT_LATENT_GRID_F16 ||
+                       (p->latent_format == NT_LATENT_BC6_BLOCKS && ft.width % 4 == 0 && ft.height % 4 == 0),
+                   "latent_format %d: features[%d] must be %s", p->latent_format, f,
+                   p->latent_format == NT_LATENT_BC6_BLOCKS ? "a multiple of 4 texels in each direction"
+                                                             : "a known latent format");
     }
     return NT_OK;
 }
@@ -123,6 +128,7 @@ static AdamSegment make_segment(void *w, float *g, float *m, float *v, int64_t n
 {
     AdamSegment s;
     s.w = reinterpret_cast<__half *>(w);
+    s.w32 = nullptr;
     s.g = g;
     s.m = m;
     s.v = v;
@@ -173,8 +179,17 @@ static nt_status add_feature_segments(const NtKernelParams *p, AdamLaunch &a)
         const NtFeature &ft = p->features[f];
         NT_REQUIRE(ft.gradients && ft.moment1 && ft.moment2,
                    "features[%d] gradient / moment buffers are required", f);
-        a.seg[a.nseg++] = make_segment(ft.grid, ft.gradients, ft.moment1, ft.moment2,
-                                       (int64_t)ft.width * ft.height * p->latent_channels, p->feature_adam, p->step);
+        if (p->latent_format == NT_LATENT_BC6_BLOCKS) {
+            // fp32 block records; partition / mode slots keep a zero gradient and are skipped
+            const int64_t n = (int64_t)(ft.width / 4) * (ft.height / 4) * ((p->latent_channels + 2) / 3) * 32;
+            AdamSegment sg = make_segment(nullptr, ft.gradients, ft.moment1, ft.moment2, n, p->feature_adam, p->step);
+            sg.w32 = reinterpret_cast<float *>(ft.grid);
+            a.seg[a.nseg++] = sg;
+        } else {
+            a.seg[a.nseg++] = make_segment(ft.grid, ft.gradients, ft.moment1, ft.moment2,
+                                           (int64_t)ft.width * ft.height * p->latent_channels, p->feature_adam,
+                                           p->step);
+        }
     }
     return NT_OK;
 }
@@ -226,6 +241,7 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(lattice_rows)
     NT_FIELD(row_origin)
     NT_FIELD(stored_rows)
+    NT_FIELD(latent_format)
 #undef NT_FIELD
     return (size_t)-1;
 }
@@ -235,10 +251,8 @@ uint64_t nt_launch_count(void) { return g_launches.load(); }
 nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type, nt_stream_t stream)
 {
     NT_REQUIRE(p, "params is null");
-    if (type == NT_TRAIN_BLOCK_FEATURES)
-        return fail(NT_ERR_UNSUPPORTED, "BLOCK_FEATURES training (BC6 block latents) is not built");
-    NT_REQUIRE(type == NT_TRAIN_UNCONSTRAINED || type == NT_TRAIN_FINALIZE, "unknown training kernel type %d",
-               (int)type);
+    NT_REQUIRE(type == NT_TRAIN_UNCONSTRAINED || type == NT_TRAIN_BLOCK_FEATURES || type == NT_TRAIN_FINALIZE,
+               "unknown training kernel type %d", (int)type);
     nt_status st = validate_network(p);
     if (st != NT_OK) return st;
     NT_REQUIRE(p->target && aligned16(p->target), "target must be a non-null 16-byte aligned device pointer");
@@ -303,6 +317,16 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
         sharded = sharded || L.rows[s] != h;
     }
     NT_REQUIRE(!sharded || train_engine() == 1, "row sharding needs the tcgen05 training engine (NT_TRAIN_ENGINE=mma is set)");
+    // latent representation: UNCONSTRAINED trains fp16 grids, BLOCK_FEATURES trains BC6 block
+    // features (train.cu:902-913), FINALIZE samples either and trains the network only
+    NT_REQUIRE(type != NT_TRAIN_UNCONSTRAINED || p->latent_format == NT_LATENT_GRID_F16,
+               "UNCONSTRAINED training needs latent_format NT_LATENT_GRID_F16");
+    NT_REQUIRE(type != NT_TRAIN_BLOCK_FEATURES || p->latent_format == NT_LATENT_BC6_BLOCKS,
+               "BLOCK_FEATURES training needs latent_format NT_LATENT_BC6_BLOCKS");
+    L.blocks = p->latent_format == NT_LATENT_BC6_BLOCKS;
+    NT_REQUIRE(!L.blocks || (!sharded && train_engine() == 1),
+               "BC6 block features need the tcgen05 engine and an unsharded call");
+    if (type == NT_TRAIN_BLOCK_FEATURES) L.finalize = 0;
     L.tiles_x = (p->lattice_width + kTileSide - 1) / kTileSide;
     L.tiles_y = (p->lattice_height + kTileSide - 1) / kTileSide;
     return check_cuda(launch_train(L, p->latent_channels, (cudaStream_t)stream), "training kernel");
@@ -323,9 +347,10 @@ nt_status nt_invoke_optimize_network(const NtKernelParams *p, nt_stream_t stream
 nt_status nt_invoke_optimize_features(const NtKernelParams *p, NtTrainingKernelType type, nt_stream_t stream)
 {
     NT_REQUIRE(p, "params is null");
-    if (type == NT_TRAIN_BLOCK_FEATURES)
-        return fail(NT_ERR_UNSUPPORTED, "BLOCK_FEATURES optimisation (BC6 block latents) is not built");
     if (type == NT_TRAIN_FINALIZE) return NT_OK;  // main.cpp:1074: features are frozen
+    // OptimizeFeatures<UNCONSTRAINED> / <BLOCK_FEATURES> (train.cu:990-1026): the type names the representation
+    NT_REQUIRE(type == (p->latent_format == NT_LATENT_BC6_BLOCKS ? NT_TRAIN_BLOCK_FEATURES : NT_TRAIN_UNCONSTRAINED),
+               "optimiser type %d does not match latent_format %d", (int)type, p->latent_format);
     nt_status st = validate_network(p);
     if (st != NT_OK) return st;
     AdamLaunch a;
@@ -355,6 +380,8 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     if (st != NT_OK) return st;
     NT_REQUIRE(p->image_width >= 1 && p->image_height >= 1, "image size must be positive");
     NT_REQUIRE(p->inference_output, "inference_output is null");
+    NT_REQUIRE(p->latent_format == NT_LATENT_GRID_F16,
+               "inference samples fp16 latent grids (train.cu:935, SampleUnconstrainedFeaturesTrilinear)");
     NT_REQUIRE(p->inference_output_dtype == NT_DTYPE_F16 || p->inference_output_dtype == NT_DTYPE_F32,
                "inference_output_dtype must be NT_DTYPE_F16 or NT_DTYPE_F32");
     NT_REQUIRE(!(p->inference_output_dtype == NT_DTYPE_F16 && p->output_channels == 8) ||

@@ -37,6 +37,7 @@ struct TrainLaunch {
     // (0, 1: latent grids, 2: target) stores rows_s rows from full row org[s] (wrapping).
     int32_t lat_row0, lat_rows;
     int32_t org[3], rows[3];
+    int32_t blocks;  // 1: grid / ggrid hold BC6 block-feature records (float), not fp16 texels
 };
 
 struct DecodeLaunch {
@@ -56,6 +57,7 @@ constexpr int kAdamChunk = 1024;  // parameters per Adam CTA
 
 struct AdamSegment {
     __half *w;
+    float *w32;  // fp32 parameters instead of w (BC6 block-feature records)
     float *g, *m, *v;
     int64_t n;
     float lr, beta1, beta2, eps, bc1, bc2;

@@ -45,6 +45,7 @@
 
 #include "nt_kernels.cuh"
 #include "nt_mma.cuh"
+#include "nt_bc6f.cuh"
 #include "nt_tc_common.cuh"
 #include "nt_umma.cuh"
 
@@ -614,8 +615,9 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
 // ---- the kernel ---------------------------------------------------------------------------------
 
 // C: latent channels per grid; TC: target channels when they have a vector gather (4, 8,
-// 12 or 16), 0 for the generic per-channel gather.
-template <int C, int TC>
+// 12 or 16), 0 for the generic per-channel gather; BLK: the latents are BC6 block features
+// (nt_bc6f.cuh: float records sampled through the BC6 decode, gradients into the records).
+template <int C, int TC, bool BLK>
 __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaunch p)
 {
     using K = Cfg<C>;
@@ -670,7 +672,10 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     if (valid) shard_rows(p, gi, p.gh[gi], fp);
                     if (valid) {
                         float f[C];
-                        gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
+                        if constexpr (BLK)
+                            gather_bc6f<C>(reinterpret_cast<const float *>(p.grid[gi]), p.gw[gi], fp, f);
+                        else
+                            gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
 #pragma unroll
                         for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
                     }
@@ -728,7 +733,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
         // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
-        if (!half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
+        if (!BLK && !half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
         if (half) {
             uint32_t v[16];
             umma::ld16(Rl, v);
@@ -781,6 +786,33 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 umma::wait_ld();
 #pragma unroll
                 for (int e = 0; e < C; ++e) dxv[e] = __uint_as_float(half ? v[C + e] : v[e]);
+            }
+            if constexpr (BLK) {
+                // block features: every tap adds to its block record (train.cu:436-454)
+                if (valid) {
+                    const float *blocks = reinterpret_cast<const float *>(p.grid[half]);
+                    float *grads = p.ggrid[half];
+                    const short2 b = s.base[half][r];
+                    const int gw = p.gw[half], gh = p.gh[half];
+                    for (int j = 0; j < 4; ++j) {
+                        const int yy = wrap_coord(b.y - 1 + j, gh);
+                        for (int i = 0; i < 4; ++i) {
+                            const int xx = wrap_coord(b.x - 1 + i, gw);
+                            const float wgt = __fmul_rn(s.wts[half][r][4 + j], s.wts[half][r][i]);
+                            float fg[C];
+#pragma unroll
+                            for (int k = 0; k < C; ++k) fg[k] = __fmul_rn(__fmul_rn(wgt, dxv[k]), p.inv_num_samples);
+                            bc6f_backward_texel<C>(blocks, grads, gw, xx, yy, fg);
+                        }
+                    }
+                }
+                first = false;
+                umma::fence_before();
+                if (__syncthreads_or(failed)) {
+                    failed = true;
+                    break;
+                }
+                continue;
             }
             bool tc_scatter = false;
             if constexpr (C == 8) tc_scatter = s.win[0].tc && s.win[1].tc;
@@ -912,19 +944,19 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     }
 }
 
-template <int C, int TC>
+template <int C, int TC, bool BLK>
 static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 {
     const size_t smem = sizeof(Smem<C>);
     static_assert(sizeof(Smem<C>) <= 113 * 1024, "two CTAs per SM");
-    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC>), smem);
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK>), smem);
     if (e != cudaSuccess) return e;
     p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
     p.tiles_y = (p.lat_rows + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = 2 * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;
-    train_tc_kernel<C, TC><<<grid, kThreadsTC, smem, stream>>>(p);
+    train_tc_kernel<C, TC, BLK><<<grid, kThreadsTC, smem, stream>>>(p);
     count_launch();
     return cudaGetLastError();
 }
@@ -934,8 +966,14 @@ static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream)
 {
     const int cout = p.net.cout;
-    if (channels == 8) return cout == 8 ? tc::launch_t<8, 8>(p, stream) : tc::launch_t<8, 0>(p, stream);
-    if (channels == 12) return cout == 12 ? tc::launch_t<12, 12>(p, stream) : tc::launch_t<12, 0>(p, stream);
+    if (p.blocks) {  // BC6 block features: generic target gather, one variant per channel count
+        if (channels == 8) return tc::launch_t<8, 0, true>(p, stream);
+        if (channels == 12) return tc::launch_t<12, 0, true>(p, stream);
+        return cudaErrorInvalidValue;
+    }
+    if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, false>(p, stream) : tc::launch_t<8, 0, false>(p, stream);
+    if (channels == 12)
+        return cout == 12 ? tc::launch_t<12, 12, false>(p, stream) : tc::launch_t<12, 0, false>(p, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -227,6 +227,145 @@ void nto_posenc(float u, float v, float out[8])
 
 /* One layer y[o] = b[o] + sum_i x[i] * W[o * pad_in + i] (column-major, main.cpp:195,
  * mlp.h:18-40), fp32 accumulation (double here: the oracle is the exact sum). */
+/* ---- BC6 block features ------------------------------------------------------------- */
+
+static const int32_t bc6f_part_masks[32] = { /* train.cu:20-29, gBC6HPartitionSets */
+    0xCCCC, 0x8888, 0xEEEE, 0xECC8, 0xC880, 0xFEEC, 0xFEC8, 0xEC80, 0xC800, 0xFFEC, 0xFE80,
+    0xE800, 0xFFE8, 0xFF00, 0xFFF0, 0xF000, 0xF710, 0x008E, 0x7100, 0x08CE, 0x008C, 0x7310,
+    0x3100, 0x8CCE, 0x088C, 0x3110, 0x6666, 0x366C, 0x17E8, 0x0FF0, 0x718E, 0x399C};
+static const int32_t bc6f_mode_bits[10] = {10, 7, 11, 11, 11, 9, 8, 8, 8, 6}; /* train.cu:31-34 */
+
+/* train.cu:161-167 UnquantizeEndpoints */
+static float bc6f_unquantize(float e, int32_t b)
+{
+    const float scale = (31.f / 64.f) * 65536.f;
+    return ldexpf(scale * e + 32768.f, -b);
+}
+
+/* train.cu:169-182 DecompressBC6, per channel; also returns the intermediates the backward
+ * pass needs (train.cu:184-202). */
+static float bc6f_channel(float e0, float e1, int32_t b, float x, float *eb0, float *eb1, float *y_out)
+{
+    const int q = 3;
+    const float u0 = bc6f_unquantize(e0, b), u1 = bc6f_unquantize(e1, b);
+    const float y = u0 + ldexpf(u1 - u0, q) * x;
+    float hyf = floorf((y - 1.f) / 1024.f) - 1.f;
+    hyf = hyf > 0.f ? hyf : 0.f;
+    const int32_t hy = (int32_t)hyf;
+    if (eb0) *eb0 = u0;
+    if (eb1) *eb1 = u1;
+    if (y_out) *y_out = y;
+    return ldexpf(y / 1024.f - (float)hy, hy - 14);
+}
+
+void nto_bc6f_decode(const float e0[3], const float e1[3], int32_t bits, float x, float out[3])
+{
+    for (int c = 0; c < 3; ++c) out[c] = bc6f_channel(e0[c], e1[c], bits, x, NULL, NULL, NULL);
+}
+
+/* train.cu:204-212 block / pixel index, :240-261 SampleBC6FeatureTexel, per channel triple */
+static const float *bc6f_block(const float *blocks, int32_t w, int32_t T, int32_t x, int32_t y, int32_t t)
+{
+    const int64_t b = (int64_t)(y >> 2) * (w >> 2) + (x >> 2);
+    return blocks + (b * T + t) * NTO_BC6F_FLOATS;
+}
+
+static int32_t bc6f_int(const float *p, int k)
+{
+    int32_t v;
+    memcpy(&v, p + k, sizeof v);
+    return v;
+}
+
+void nto_bc6f_texel(const float *blocks, int32_t w, int32_t channels, int32_t x, int32_t y, float *out)
+{
+    const int32_t T = (channels + 2) / 3, pix = ((y & 3) << 2) + (x & 3);
+    for (int32_t t = 0; t < T; ++t) {
+        const float *p = bc6f_block(blocks, w, T, x, y, t);
+        const int32_t part = bc6f_int(p, 28) & 31, mode = bc6f_int(p, 29);
+        const int32_t r = (bc6f_part_masks[part] >> pix) & 1;
+        const int32_t bits = bc6f_mode_bits[mode < 0 || mode > 9 ? 0 : mode];
+        float v[3];
+        nto_bc6f_decode(p + 6 * r, p + 6 * r + 3, bits, p[12 + pix], v);
+        for (int c = 0; c < 3; ++c)
+            if (3 * t + c < channels) out[3 * t + c] = v[c];
+    }
+}
+
+/* Catmull-Rom sample of a block-feature grid (nto_sample_grid's footprint and order). */
+static void sample_blocks(const float *blocks, int32_t w, int32_t h, int32_t C, float u, float v, float *out,
+                          int32_t base_out[2], float wx_out[4], float wy_out[4])
+{
+    float fx, fy;
+    const int32_t bx = cr_base(u, w, &fx), by = cr_base(v, h, &fy);
+    float wx[4], wy[4];
+    nto_catmull_rom_weights(fx, wx);
+    nto_catmull_rom_weights(fy, wy);
+    float acc[16] = {0};
+    for (int j = 0; j < 4; ++j) {
+        const int32_t yy = nto_wrap(by - 1 + j, h);
+        float row[16] = {0};
+        for (int i = 0; i < 4; ++i) {
+            const int32_t xx = nto_wrap(bx - 1 + i, w);
+            float t[16];
+            nto_bc6f_texel(blocks, w, C, xx, yy, t);
+            for (int k = 0; k < C; ++k) row[k] += wx[i] * t[k];
+        }
+        for (int k = 0; k < C; ++k) acc[k] += wy[j] * row[k];
+    }
+    for (int k = 0; k < C; ++k) out[k] = acc[k];
+    if (base_out) { base_out[0] = bx; base_out[1] = by; }
+    if (wx_out) memcpy(wx_out, wx, sizeof wx);
+    if (wy_out) memcpy(wy_out, wy, sizeof wy);
+}
+
+/* train.cu:436-454: gradients of one texel of a block-feature grid for the feature gradient
+ * fg (C channels, tap weight and 1 / numSamples applied): endpoints of its region and its
+ * pixel index. */
+static void bc6f_backward_texel(const float *blocks, float *grads, int32_t w, int32_t C, int32_t x, int32_t y,
+                                const float *fg)
+{
+    const int32_t T = (C + 2) / 3, pix = ((y & 3) << 2) + (x & 3);
+    const int q = 3;
+    for (int32_t t = 0; t < T; ++t) {
+        const float *p = bc6f_block(blocks, w, T, x, y, t);
+        float *gp = grads + (bc6f_block(blocks, w, T, x, y, t) - blocks);
+        const int32_t part = bc6f_int(p, 28) & 31, mode = bc6f_int(p, 29);
+        const int32_t r = (bc6f_part_masks[part] >> pix) & 1;
+        const int32_t bits = bc6f_mode_bits[mode < 0 || mode > 9 ? 0 : mode];
+        const float xv = p[12 + pix];
+        const float alpha = ldexpf(xv, q);
+        const float deibar_dei = ldexpf(31.f / 64, 16 - bits);
+        float dl_dx = 0.f;
+        float d0[3], d1[3];
+        for (int c = 0; c < 3; ++c) {
+            const float g = 3 * t + c < C ? fg[3 * t + c] : 0.f;
+            float eb0, eb1, y;
+            bc6f_channel(p[6 * r + c], p[6 * r + 3 + c], bits, xv, &eb0, &eb1, &y);
+            float hyf = floorf((y - 1.f) / 1024.f) - 1.f;
+            hyf = hyf > 0.f ? hyf : 0.f;
+            const float dl_dy = ldexpf(g, (int32_t)hyf - 24);
+            dl_dx += dl_dy * ldexpf(eb1 - eb0, q);
+            d0[c] = (1.f - alpha) * deibar_dei * dl_dy;
+            d1[c] = alpha * deibar_dei * dl_dy;
+        }
+        for (int c = 0; c < 3; ++c) {
+#ifdef _OPENMP
+#pragma omp atomic
+#endif
+            gp[6 * r + c] += d0[c];
+#ifdef _OPENMP
+#pragma omp atomic
+#endif
+            gp[6 * r + 3 + c] += d1[c];
+        }
+#ifdef _OPENMP
+#pragma omp atomic
+#endif
+        gp[12 + pix] += dl_dx;
+    }
+}
+
 static void layer(const float *x, int n_in, int pad_in, const uint16_t *W, const uint16_t *b,
                   int n_out, float *y)
 {
@@ -248,8 +387,11 @@ void nto_forward_sample(const nto_model *m, float u, float v, nto_fwd *f)
     float feat[16];
     memset(f->x, 0, sizeof f->x);
     for (int g = 0; g < 2; ++g) {
-        nto_sample_grid(m->grid[g], m->gw[g], m->gh[g], C, u, v, feat, f->base[g], f->wx[g],
-                        f->wy[g]);
+        if (m->blocks[g])
+            sample_blocks(m->blocks[g], m->gw[g], m->gh[g], C, u, v, feat, f->base[g], f->wx[g], f->wy[g]);
+        else
+            nto_sample_grid(m->grid[g], m->gw[g], m->gh[g], C, u, v, feat, f->base[g], f->wx[g],
+                            f->wy[g]);
         for (int k = 0; k < C; ++k) f->x[g * C + k] = r16(feat[k]);
     }
     float pe[8];
@@ -384,6 +526,19 @@ static void scatter_latent(const nto_model *m, const nto_fwd *f, const float *dx
     const int C = m->channels;
     for (int g = 0; g < 2; ++g) {
         if (!ggrid[g]) continue;
+        if (m->blocks[g]) { /* train.cu:436-454 per tap of the Catmull-Rom footprint */
+            for (int j = 0; j < 4; ++j) {
+                const int32_t yy = nto_wrap(f->base[g][1] - 1 + j, m->gh[g]);
+                for (int i = 0; i < 4; ++i) {
+                    const int32_t xx = nto_wrap(f->base[g][0] - 1 + i, m->gw[g]);
+                    const float wgt = f->wy[g][j] * f->wx[g][i];
+                    float fg[16];
+                    for (int k = 0; k < C; ++k) fg[k] = wgt * dx[g * C + k] * scale;
+                    bc6f_backward_texel(m->blocks[g], ggrid[g], m->gw[g], C, xx, yy, fg);
+                }
+            }
+            continue;
+        }
         for (int j = 0; j < 4; ++j) {
             const int32_t yy = nto_wrap(f->base[g][1] - 1 + j, m->gh[g]);
             for (int i = 0; i < 4; ++i) {

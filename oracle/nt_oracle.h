@@ -53,11 +53,22 @@ void nto_sample_grid(const uint16_t *grid, int32_t w, int32_t h, int32_t c, floa
 void nto_posenc(float u, float v, float out[8]);
 
 /* ---- network -------------------------------------------------------------------------- */
+/* ---- BC6 block features (train.cu:161-182, :240-261, :436-454) -------------------------
+ * A grid of C channels in block form: per 4x4 block (row-major, width / 4 blocks per row)
+ * ceil(C / 3) channel triples of 32 floats: endpoints e0..e3 (xyz, 12 floats), 16 pixel
+ * indices, partition (int32 bits), mode (int32 bits, 0..9), 2 unused.  Texel (x, y) of triple
+ * t uses region r = partition bit ((y & 3) * 4 + (x & 3)), endpoints e[2r], e[2r + 1], pixel
+ * index [(y & 3) * 4 + (x & 3)] and the mode's endpoint precision. */
+#define NTO_BC6F_FLOATS 32
+void nto_bc6f_decode(const float e0[3], const float e1[3], int32_t bits, float x, float out[3]);
+void nto_bc6f_texel(const float *blocks, int32_t w, int32_t channels, int32_t x, int32_t y, float *out);
+
 typedef struct nto_model {
     int32_t channels;       /* C per grid */
     int32_t cout;           /* output channels, <= 16 */
     int32_t gw[2], gh[2];
     const uint16_t *grid[2];
+    const float *blocks[2]; /* block-feature form of grid g (NULL: the fp16 grid) */
     const uint16_t *W[3];   /* padded column-major fp16: [64][32], [64][64], [16][64] */
     const uint16_t *b[3];   /* fp16: 64, 64, cout */
 } nto_model;

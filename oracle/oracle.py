@@ -61,7 +61,7 @@ class Sampler(C.Structure):
 class Model(C.Structure):
     _fields_ = [("channels", C.c_int32), ("cout", C.c_int32),
                 ("gw", C.c_int32 * 2), ("gh", C.c_int32 * 2),
-                ("grid", u16p * 2), ("W", u16p * 3), ("b", u16p * 3)]
+                ("grid", u16p * 2), ("blocks", f32p * 2), ("W", u16p * 3), ("b", u16p * 3)]
 
 
 class TrainArgs(C.Structure):
@@ -163,14 +163,20 @@ class OracleModel:
     grids: list          # 2 x uint16 [h][w][C]
     W: list              # 3 x uint16 padded column-major
     b: list              # 3 x uint16
+    blocks: list | None = None       # 2 x float32 BC6 block features (then grids are unused)
+    block_sizes: list | None = None  # 2 x (w, h) texels of the block grids
 
     def ctype(self) -> Model:
         m = Model()
         m.channels = self.channels
         m.cout = self.cout
         for g in range(2):
-            m.gh[g], m.gw[g] = self.grids[g].shape[0], self.grids[g].shape[1]
-            m.grid[g] = _p(self.grids[g], u16p)
+            if self.blocks is not None:
+                m.gw[g], m.gh[g] = self.block_sizes[g]
+                m.blocks[g] = _p(self.blocks[g], f32p)
+            else:
+                m.gh[g], m.gw[g] = self.grids[g].shape[0], self.grids[g].shape[1]
+                m.grid[g] = _p(self.grids[g], u16p)
         for l in range(3):
             m.W[l] = _p(self.W[l], u16p)
             m.b[l] = _p(self.b[l], u16p)
@@ -225,7 +231,8 @@ def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel
     a.finalize = int(finalize)
     gW = [np.zeros(x.shape, np.float32) for x in model.W]
     gb = [np.zeros(64, np.float32), np.zeros(64, np.float32), np.zeros(model.cout, np.float32)]
-    gg = [np.zeros(g.shape, np.float32) for g in model.grids]
+    gg = ([np.zeros(bl.shape, np.float32) for bl in model.blocks] if model.blocks is not None
+          else [np.zeros(g.shape, np.float32) for g in model.grids])
     pW = (f32p * 3)(*[_p(x, f32p) for x in gW])
     pb = (f32p * 3)(*[_p(x, f32p) for x in gb])
     pg = (f32p * 2)(*[_p(x, f32p) for x in gg])
@@ -307,6 +314,7 @@ _u8p = C.POINTER(C.c_uint8)
 def _codec_lib():
     L = lib()
     if not getattr(L, "_codec_bound", False):
+        L.nto_bc6f_decode.argtypes = [f32p, f32p, C.c_int32, C.c_float, f32p]
         L.nto_bc6h_mode_index.restype = C.c_int
         L.nto_bc6h_mode_index.argtypes = [_u8p]
         L.nto_bc6h_decode_block.argtypes = [_u8p, C.c_int, u16p]
@@ -374,3 +382,25 @@ def smooth_latents(rng: np.random.Generator, shape, std=0.5, clip=4.0, corr=8) -
         n = acc
     n = n / n.std() * std
     return np.clip(n, -clip, clip).astype(np.float16).view(np.uint16)
+
+
+def bc6f_decode(e0, e1, bits: int, x: float) -> np.ndarray:
+    """BC6 float decode of one texel (train.cu:161-182): 3 channels."""
+    a = np.ascontiguousarray(e0, np.float32)
+    b = np.ascontiguousarray(e1, np.float32)
+    out = np.zeros(3, np.float32)
+    _codec_lib().nto_bc6f_decode(_p(a, f32p), _p(b, f32p), int(bits), float(x), _p(out, f32p))
+    return out
+
+
+def random_blocks(rng, w: int, h: int, channels: int) -> np.ndarray:
+    """Seeded BC6 block features for a w x h grid: endpoints U(-1, 1), pixel indices U(0, 1),
+    random partition (0..31) and mode (0..9); float32 [blocks * triples * 32]."""
+    T = (channels + 2) // 3
+    nb = (w // 4) * (h // 4) * T
+    p = np.zeros((nb, 32), np.float32)
+    p[:, :12] = rng.uniform(-1, 1, (nb, 12))
+    p[:, 12:28] = rng.uniform(0, 1, (nb, 16))
+    p[:, 28].view(np.int32)[:] = rng.integers(0, 32, nb)
+    p[:, 29].view(np.int32)[:] = rng.integers(0, 10, nb)
+    return p.reshape(-1)

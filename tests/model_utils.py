@@ -39,3 +39,24 @@ def max_rel(a, b, floor=1.0):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), floor)))
+
+
+MODE_BITS = (10, 7, 11, 11, 11, 9, 8, 8, 8, 6)  # endpoint precision per mode (train.cu:31-34)
+
+
+def realistic_blocks(rng, w, h, C):
+    """Seeded BC6 block-feature records whose texels decode to about 0.5 .. 3 (the float decode
+    of train.cu:161-182 maps an endpoint e to ebar = (31744 e + 32768) 2^-bits in the 16-bit
+    half-float domain and interpolates with alpha = 8 x, so endpoints are drawn per mode for
+    ebar in [14500, 16500] and pixel indices x in [0, 1/8])."""
+    T = (C + 2) // 3
+    nb = (w // 4) * (h // 4) * T
+    p = np.zeros((nb, 32), np.float32)
+    mode = rng.integers(0, 10, nb)
+    bits = np.array(MODE_BITS)[mode].astype(np.float64)
+    y = rng.uniform(14500.0, 16500.0, (nb, 12))
+    p[:, :12] = ((y * np.exp2(bits)[:, None] - 32768.0) / 31744.0).astype(np.float32)
+    p[:, 12:28] = rng.uniform(0.0, 0.125, (nb, 16))
+    p[:, 28].view(np.int32)[:] = rng.integers(0, 32, nb)
+    p[:, 29].view(np.int32)[:] = mode
+    return p.reshape(-1)

@@ -83,11 +83,19 @@ def test_training_rejects_invalid_arguments(native, mutate, needle):
     assert needle in _native.last_error()
 
 
-def test_block_features_is_reported_unsupported(native):
+def test_latent_format_must_match_the_training_type(native):
     from neural_textures_b200 import _native
     p = _valid_looking_params()
-    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 6
-    assert native.nt_invoke_optimize_features(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 6
+    # fp16 grids cannot be trained as BC6 block features, and the reverse
+    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 1
+    assert "BLOCK_FEATURES" in _native.last_error()
+    assert native.nt_invoke_optimize_features(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 1
+    p.latent_format = _native.NT_LATENT_BC6_BLOCKS
+    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_UNCONSTRAINED, None) == 1
+    assert native.nt_invoke_inference(C.byref(p), None) == 1
+    p.features[0].width = 30  # block features need whole 4x4 blocks
+    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 1
+    assert "multiple of 4" in _native.last_error()
 
 
 def test_null_params_rejected(native):

@@ -289,6 +289,52 @@ def run_config4b(torch, dist, dev, stream, rank, world, steps, warmup):
     return out
 
 
+def run_blocks(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank):
+    """BLOCK_FEATURES fine-tuning on the config-1 material (train.cu:316-458, :728-762): the
+    fp16 latents are encoded as BC6H blocks and turned into float BC6 block records
+    (to_blocks), then each step = training pass through the float BC6 decode with the
+    gradient scatter into the records + fused Adam over the network and the fp32 records.
+    L2 flushed before every timed step, as for config 1."""
+    tex = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                           output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
+    tex.init(seed=rank)
+    tex.to_blocks(4.0)
+    sptr = stream.cuda_stream
+    B = CFG1["lattice"][0] * CFG1["lattice"][1]
+
+    def step_once(step, ev=None):
+        p = tex.params(step=step)
+        if ev:
+            ev[0].record(stream)
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 1, sptr))
+        if ev:
+            ev[1].record(stream)
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), sptr))
+        if ev:
+            ev[2].record(stream)
+
+    for w in range(warmup):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(w + 1)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for k in range(steps):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(warmup + k + 1, events[k])
+    torch.cuda.synchronize(dev)
+    t_train = sum(e[0].elapsed_time(e[1]) for e in events) / steps
+    t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / steps
+    P = sum(b.numel() for b in tex.blocks)
+    out = {"workload": "config1_block_features_1024sq_8ch", "value": B / ((t_train + t_adam) * 1e-3),
+           "unit": "samples/s", "ms_per_step": t_train + t_adam, "steps": steps, "warmup": warmup,
+           "kernels_ms": {"train_kernel_blocks": t_train, "adam_kernel": t_adam},
+           "records": f"{P} fp32 ({P // 32} records of 32 floats)",
+           "adam_hbm_gbs": 32 * P / (t_adam * 1e-3) / 1e9,
+           "adam_algorithmic": "32 B/param (w g m v read, w m v g written, fp32)",
+           "l2": "flushed (256 MB write) before every timed step"}
+    del tex
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -300,6 +346,7 @@ def main():
     ap.add_argument("--codec-iters", type=int, default=5, help="timed BC6H encode / decode passes (0: skip)")
     ap.add_argument("--decode-iters", type=int, default=200)
     ap.add_argument("--sharded-steps", type=int, default=20, help="timed config-4b sharded steps (0: skip)")
+    ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -417,10 +464,13 @@ def main():
     codec = None
     if args.codec_iters > 0:
         codec = run_codec_bench(torch, dev, stream, L, args.codec_iters, rank, world, dist)
+    blocks = None
+    if args.block_steps > 0:
+        blocks = run_blocks(torch, dev, stream, L, nt, _native, scratch, args.block_steps, 5, rank)
     cfg4b = None
     if args.sharded_steps > 0:
         cfg4b = run_config4b(torch, dist, dev, stream, rank, world, args.sharded_steps, 10)
-    clk = clocks.stop()  # sampled across the timed training, e2e, decode, codec and config-4b regions
+    clk = clocks.stop()  # sampled across the timed training, e2e, decode, codec, block-feature and config-4b regions
     texels = CFG0["image"][0] * CFG0["image"][1]
 
     if world > 1:
@@ -470,6 +520,9 @@ def main():
         codec["decode_traffic"] = tr.get("bc6h_decode_kernel", {}).get("bytes_per_launch")
         codec["encode_traffic"] = tr.get("bc6h_encode_kernel", {}).get("bytes_per_launch")
         line["codec"] = codec
+    if blocks:
+        blocks["adam_hbm_frac"] = blocks["adam_hbm_gbs"] / pk["hbm"]
+        line["block_features"] = blocks
     if cfg4b:
         line["config4b"] = cfg4b
     if not args.no_cpu_baseline:

@@ -100,6 +100,8 @@ typedef struct NtFeature {
 /* Latent representations (NtKernelParams.latent_format). */
 #define NT_LATENT_GRID_F16 0
 #define NT_LATENT_BC6_BLOCKS 1
+/* Floats per channel triple of a 4x4 block in NT_LATENT_BC6_BLOCKS records. */
+#define NT_BC6F_RECORD_FLOATS 32
 
 typedef struct NtKernelParams {
     NtFeature features[NT_NUM_FEATURES];
@@ -201,7 +203,9 @@ NT_API nt_status nt_invoke_optimize_all(const NtKernelParams *params, nt_stream_
 NT_API nt_status nt_invoke_inference(const NtKernelParams *params, nt_stream_t stream);
 
 /* One training step as the reference driver runs it (main.cpp:1071-1077):
- * training pass, then fused Adam over network and latents.  The caller increments step. */
+ * training pass, then fused Adam over network and latents.  The training type follows
+ * latent_format (UNCONSTRAINED for fp16 grids, BLOCK_FEATURES for BC6 block records).
+ * The caller increments step. */
 NT_API nt_status nt_train_step(const NtKernelParams *params, nt_stream_t stream);
 
 /* ---- tests/forward_pass_test.h:6 ------------------------------------------------------ */
@@ -250,6 +254,25 @@ NT_API nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int3
  * writes [blocks_h*4][blocks_w*4][4] floats.  Synchronous; allocates and frees the array. */
 NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h,
                                          int32_t is_signed, float *rgba);
+
+/* ---- block records <-> BC6H blocks (no reference counterpart: the reference's
+ * BLOCK_FEATURES path, train.cu:316-458, starts from and ends in float records) ----------- */
+
+/* Floats of the NT_LATENT_BC6_BLOCKS records of a width x height x channels grid
+ * ([height/4][width/4][ceil(channels/3)][NT_BC6F_RECORD_FLOATS]); 0 unless width and height
+ * are positive multiples of 4. */
+NT_API size_t nt_bc6f_records_floats(int32_t width, int32_t height, int32_t channels);
+/* Records from BC6H UF16 blocks in nt_bc6h_encode's layout: e = (31 u 2^b / 64 - 32768) / 31744
+ * for unquantized endpoints u, x = weight / 512, partition and mode kept for modes 1-10;
+ * one-region blocks give equal regions.  Each record's float decode is within one fp16 ulp
+ * of the block's integer decode (the texel values are value + the encoder's bias). */
+NT_API nt_status nt_bc6f_from_bc6h(const void *blocks, int32_t width, int32_t height, int32_t channels,
+                                   float *records, nt_stream_t stream);
+/* BC6H UF16 blocks from records: the record's partition, the best-fitting mode (its own
+ * first), nearest palette indices.  A record made by nt_bc6f_from_bc6h returns a block that
+ * decodes to the same texels. */
+NT_API nt_status nt_bc6f_to_bc6h(const float *records, int32_t width, int32_t height, int32_t channels,
+                                 void *blocks, nt_stream_t stream);
 
 /* ---- tensor-core self-test (no reference counterpart) ---------------------------------- */
 

@@ -16,6 +16,12 @@ from .api import (  # noqa: F401
     RunForwardPassTest,
     TrainingKernelType,
     TrainStep,
+    bc6f_from_bc6h,
+    bc6f_records_floats,
+    bc6f_to_bc6h,
+    bc6h_blocks_bytes,
+    bc6h_decode,
+    bc6h_encode,
     he_normal_weights,
     invoke_inference,
     invoke_optimize_all,

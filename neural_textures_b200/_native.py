@@ -25,6 +25,7 @@ NT_TRAIN_BLOCK_FEATURES = 1
 NT_TRAIN_FINALIZE = 2
 NT_LATENT_GRID_F16 = 0
 NT_LATENT_BC6_BLOCKS = 1
+NT_BC6F_RECORD_FLOATS = 32
 NT_DTYPE_F16 = 0
 NT_DTYPE_F32 = 1
 
@@ -109,6 +110,9 @@ SIGNATURES = {
     "nt_bc6h_decode": (C.c_int, [C.c_void_p, _S, C.c_float, C.c_void_p]),
     "nt_bc6h_decode_raw": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_void_p]),
     "nt_bc6h_decode_hardware": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
+    "nt_bc6f_records_floats": (C.c_size_t, [C.c_int32, C.c_int32, C.c_int32]),
+    "nt_bc6f_from_bc6h": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
+    "nt_bc6f_to_bc6h": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     "nt_umma_selftest": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
     "nt_read_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),

@@ -128,6 +128,32 @@ def bc6h_decode(blocks, out, layout: str = "planar", bias: float = 4.0, stream=N
     return out
 
 
+def bc6f_records_floats(width: int, height: int, channels: int) -> int:
+    return int(load().nt_bc6f_records_floats(width, height, channels))
+
+
+def bc6f_from_bc6h(blocks, width: int, height: int, channels: int, records=None, stream=None):
+    """BC6H blocks (bc6h_encode's layout) -> float BC6 block records (fp32 device tensor,
+    [height/4][width/4][ceil(channels/3)][32]), the BLOCK_FEATURES latent layout."""
+    import torch
+    n = bc6f_records_floats(width, height, channels)
+    if n == 0:
+        raise ValueError(f"block records need width and height multiples of 4, got {width} x {height}")
+    if records is None:
+        records = torch.empty(n, dtype=torch.float32, device=blocks.device)
+    check(load().nt_bc6f_from_bc6h(blocks.data_ptr(), width, height, channels, records.data_ptr(), _stream(stream)))
+    return records
+
+
+def bc6f_to_bc6h(records, width: int, height: int, channels: int, blocks=None, stream=None):
+    """Float BC6 block records -> BC6H UF16 blocks (uint8 device tensor, bc6h_encode's layout)."""
+    import torch
+    if blocks is None:
+        blocks = torch.empty(bc6h_blocks_bytes(width, height, channels), dtype=torch.uint8, device=records.device)
+    check(load().nt_bc6f_to_bc6h(records.data_ptr(), width, height, channels, blocks.data_ptr(), _stream(stream)))
+    return blocks
+
+
 # ---------------------------------------------------------------------------------------
 # parameter initialisation (host, seeded)
 
@@ -202,11 +228,56 @@ class NeuralTexture:
         records (ceil(C / 3) triples of 32 floats per 4x4 block, nt_capi.h latent_format).
         Gradients and Adam moments of the records are allocated here, zeroed."""
         torch = self.torch
-        self.blocks = [torch.as_tensor(np.ascontiguousarray(r, np.float32)).to(self.device) for r in records]
+        as_dev = lambda r: (r.to(self.device, torch.float32).contiguous() if isinstance(r, torch.Tensor) else
+                            torch.as_tensor(np.ascontiguousarray(r, np.float32)).to(self.device))
+        self.blocks = [as_dev(r) for r in records]
         self.ggrads = [torch.zeros_like(b) for b in self.blocks]
         self.gm1 = [torch.zeros_like(b) for b in self.blocks]
         self.gm2 = [torch.zeros_like(b) for b in self.blocks]
         self.latent_format = N.NT_LATENT_BC6_BLOCKS
+
+    def _shift_latent_inputs(self, delta: float):
+        """Layer-1 bias += delta * (sum of W1's latent columns): compensates latent inputs that
+        move by -delta (layer-1 inputs 0 .. 2C - 1 are the two grids' channels)."""
+        torch = self.torch
+        W1 = self.W[0].view(PAD_OUT[0], PAD_IN[0]).float()
+        b1 = self.b[0].float() + delta * W1[:, :2 * self.C].sum(dim=1)
+        self.b[0].copy_(b1.to(torch.float16))
+
+    def to_blocks(self, bias: float = 4.0, stream=None):
+        """Switch from fp16 grids to BC6 block features for compression-aware fine-tuning
+        (the reference's UNCONSTRAINED -> BLOCK_FEATURES schedule, main.cpp:1046-1061): each grid
+        is encoded as BC6H UF16 blocks of (value + bias) and the blocks become block records
+        (nt_bc6f_from_bc6h).  The records decode to value + bias, so the layer-1 bias absorbs
+        -bias x W1's latent columns and the network output stays that of the encoded grids."""
+        blocks = [bc6h_encode(g, "interleaved", bias, stream=stream) for g in self.grids]
+        recs = [bc6f_from_bc6h(b, w, h, self.C, stream=stream) for b, (w, h) in zip(blocks, self.grid_sizes)]
+        self._shift_latent_inputs(-bias)
+        self.use_blocks(recs)
+        self.block_bias = bias
+
+    def export_bc6h(self, stream=None):
+        """BC6H blocks of the block records (nt_bc6f_to_bc6h), one uint8 tensor per grid; they
+        hold value + self.block_bias, as bc6h_encode(..., bias=self.block_bias) would."""
+        if self.latent_format != N.NT_LATENT_BC6_BLOCKS:
+            raise RuntimeError("export_bc6h needs block features (call to_blocks first)")
+        return [bc6f_to_bc6h(r, w, h, self.C, stream=stream) for r, (w, h) in zip(self.blocks, self.grid_sizes)]
+
+    def from_bc6h(self, blocks, bias: float | None = None, stream=None):
+        """Back to fp16 grids: decode BC6H blocks (value + bias) into the grids, undo the
+        layer-1 shift of to_blocks and train / decode grids from here on."""
+        torch = self.torch
+        bias = getattr(self, "block_bias", 4.0) if bias is None else bias
+        for g, bl in zip(self.grids, blocks):
+            bc6h_decode(bl, g, "interleaved", bias, stream=stream)
+        if self.latent_format == N.NT_LATENT_BC6_BLOCKS:
+            self._shift_latent_inputs(bias)
+        f32 = torch.float32
+        self.ggrads = [torch.zeros(g.shape, dtype=f32, device=self.device) for g in self.grids]
+        self.gm1 = [torch.zeros_like(g) for g in self.ggrads]
+        self.gm2 = [torch.zeros_like(g) for g in self.ggrads]
+        self.blocks = None
+        self.latent_format = N.NT_LATENT_GRID_F16
 
     # -- initialisation -------------------------------------------------------------------
     def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False,

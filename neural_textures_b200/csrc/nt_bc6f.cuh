@@ -15,7 +15,7 @@
 
 namespace nt {
 
-constexpr int kBc6fFloats = 32;
+constexpr int kBc6fFloats = NT_BC6F_RECORD_FLOATS;
 
 __device__ const uint16_t c_bc6f_parts[32] = {  // train.cu:20-29
     0xCCCC, 0x8888, 0xEEEE, 0xECC8, 0xC880, 0xFEEC, 0xFEC8, 0xEC80, 0xC800, 0xFFEC, 0xFE80,

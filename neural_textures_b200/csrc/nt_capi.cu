@@ -50,6 +50,8 @@ cudaError_t set_smem_limit(const void *kernel, size_t bytes)
 
 cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, bool encode, cudaStream_t st);
 cudaError_t launch_bc6h_raw(const void *blocks, int64_t n, int is_signed, void *out, cudaStream_t st);
+cudaError_t launch_bc6f_convert(const void *blocks, float *records, int32_t w, int32_t h, int32_t channels,
+                                bool to_records, cudaStream_t st);
 cudaError_t hardware_decode(const void *blocks, int bw, int bh, int is_signed, float *rgba);
 cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t seed, int32_t pbr, cudaStream_t st);
 cudaError_t launch_init_latents(void *grid, int64_t count, uint32_t seed, cudaStream_t st);
@@ -181,7 +183,7 @@ static nt_status add_feature_segments(const NtKernelParams *p, AdamLaunch &a)
                    "features[%d] gradient / moment buffers are required", f);
         if (p->latent_format == NT_LATENT_BC6_BLOCKS) {
             // fp32 block records; partition / mode slots keep a zero gradient and are skipped
-            const int64_t n = (int64_t)(ft.width / 4) * (ft.height / 4) * ((p->latent_channels + 2) / 3) * 32;
+            const int64_t n = (int64_t)(ft.width / 4) * (ft.height / 4) * ((p->latent_channels + 2) / 3) * NT_BC6F_RECORD_FLOATS;
             AdamSegment sg = make_segment(nullptr, ft.gradients, ft.moment1, ft.moment2, n, p->feature_adam, p->step);
             sg.w32 = reinterpret_cast<float *>(ft.grid);
             a.seg[a.nseg++] = sg;
@@ -409,7 +411,10 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
 
 nt_status nt_train_step(const NtKernelParams *p, nt_stream_t stream)
 {
-    nt_status st = nt_invoke_training(p, NT_TRAIN_UNCONSTRAINED, stream);
+    NT_REQUIRE(p, "params is null");
+    const NtTrainingKernelType type =
+        p->latent_format == NT_LATENT_BC6_BLOCKS ? NT_TRAIN_BLOCK_FEATURES : NT_TRAIN_UNCONSTRAINED;
+    nt_status st = nt_invoke_training(p, type, stream);
     if (st != NT_OK) return st;
     return nt_invoke_optimize_all(p, stream);
 }
@@ -452,6 +457,41 @@ nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int32_t is_
     NT_REQUIRE(num_blocks >= 0, "num_blocks must be non-negative");
     if (num_blocks == 0) return NT_OK;
     return check_cuda(launch_bc6h_raw(blocks, num_blocks, is_signed, texels, (cudaStream_t)stream), "BC6H raw decode");
+}
+
+size_t nt_bc6f_records_floats(int32_t width, int32_t height, int32_t channels)
+{
+    if (width < 4 || height < 4 || width % 4 || height % 4 || channels < 1) return 0;
+    return (size_t)(width / 4) * (size_t)(height / 4) * (size_t)((channels + 2) / 3) * NT_BC6F_RECORD_FLOATS;
+}
+
+static nt_status validate_records(const void *blocks, const float *records, int32_t w, int32_t h, int32_t channels)
+{
+    NT_REQUIRE(blocks && aligned16(blocks), "blocks must be a 16-byte aligned device pointer");
+    NT_REQUIRE(records && aligned16(records), "records must be a 16-byte aligned device pointer");
+    NT_REQUIRE(w >= 4 && h >= 4 && w % 4 == 0 && h % 4 == 0,
+               "block records need a width and height that are positive multiples of 4 (got %d x %d)", w, h);
+    NT_REQUIRE(channels >= 1, "channels must be positive");
+    return NT_OK;
+}
+
+nt_status nt_bc6f_from_bc6h(const void *blocks, int32_t width, int32_t height, int32_t channels, float *records,
+                            nt_stream_t stream)
+{
+    nt_status st = validate_records(blocks, records, width, height, channels);
+    if (st != NT_OK) return st;
+    return check_cuda(launch_bc6f_convert(blocks, records, width, height, channels, true, (cudaStream_t)stream),
+                      "BC6H blocks to block records");
+}
+
+nt_status nt_bc6f_to_bc6h(const float *records, int32_t width, int32_t height, int32_t channels, void *blocks,
+                          nt_stream_t stream)
+{
+    nt_status st = validate_records(blocks, records, width, height, channels);
+    if (st != NT_OK) return st;
+    return check_cuda(launch_bc6f_convert(blocks, const_cast<float *>(records), width, height, channels, false,
+                                          (cudaStream_t)stream),
+                      "block records to BC6H blocks");
 }
 
 nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h, int32_t is_signed,

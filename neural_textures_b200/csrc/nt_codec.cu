@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include "neural_textures/bc6h_format.h"
+#include "nt_bc6f.cuh"
 #include "nt_bc6h_unpack.cuh"
 #include "nt_capi.h"
 #include "nt_kernels.cuh"
@@ -658,6 +659,278 @@ cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, 
         bc6h_encode_kernel<<<grid, 128, 0, st>>>(L);
     else
         bc6h_decode_kernel<<<grid, 128, 0, st>>>(L);
+    count_launch();
+    return cudaGetLastError();
+}
+
+// ---- float BC6 block records <-> BC6H blocks ---------------------------------------------
+//
+// Records are the reference's float BC6 block parameters (train.cu:161-212, the
+// BLOCK_FEATURES latents): per channel triple of a 4x4 block 32 floats, endpoints
+// [region][endpoint][xyz] at 0..11, pixel indices at 12..27, partition and mode as int32
+// bits at 28 and 29.  The reference's float decode ebar = (31744 e + 32768) 2^-b,
+// y = ebar0 + 8 (ebar1 - ebar0) x stands for a half-float bit pattern, which the format
+// reaches as (v * 31) >> 6 from unquantized endpoints u and weights w / 64; ebar = 31 u / 64
+// and x = w / 512 map one onto the other (the reference itself has no such bridge).
+//
+// from BC6H: e = (31 u 2^b / 64 - 32768) / 31744 (one double rounding, then float),
+//   x = w / 512; two-region blocks keep partition and mode (the reference's ten precisions
+//   are BC6H modes 1-10, train.cu:31-34); one-region blocks give both regions the same
+//   endpoints, partition 0, record mode 0; reserved modes give records that decode to zero.
+// to BC6H: endpoint targets U = round(64 ebar / 31) in [0, 65535], texel targets
+//   T = round(64 U0 + (U1 - U0) 512 x) in [0, 64 * 65535]; candidates: the record's mode,
+//   the other two-region modes, then the one-region modes when both regions' targets agree;
+//   endpoints quantized to the nearest unquantized value, per texel the palette index with
+//   the smallest sum_c (T_c - 64 v_c)^2 (ties: lower index), anchor fix-up by swapping a
+//   region's endpoints and flipping its indices (w(n-1-i) = 64 - w(i) keeps every decoded
+//   value), transformed deltas taken modulo 2^bits must fit; smallest error wins (ties: the
+//   earlier candidate).  Integer error and exact double targets: bit-identical to the CPU
+//   restatement in the oracle.
+
+__device__ __forceinline__ float bc6f_endpoint_param(int u, int b)
+{
+    const double v = __dmul_rn((double)(31 * u), ldexp(1.0, b - 6));
+    return __double2float_rn(__ddiv_rn(__dadd_rn(v, -32768.0), 31744.0));
+}
+
+// grid: (ceil(block columns / 128), block rows, channel triples); one thread per record
+__global__ void __launch_bounds__(128) bc6f_from_bc6h_kernel(const uint4 *__restrict__ blocks, float *__restrict__ records,
+                                                             int bw, int bh, int nt)
+{
+    const int bx = blockIdx.x * blockDim.x + threadIdx.x, by = blockIdx.y, t = blockIdx.z;
+    if (bx >= bw) return;
+    const uint4 raw = blocks[((int64_t)t * bh + by) * bw + bx];
+    Block128 blk;
+    blk.w[0] = raw.x;
+    blk.w[1] = raw.y;
+    blk.w[2] = raw.z;
+    blk.w[3] = raw.w;
+    float rec[kBc6fFloats];
+#pragma unroll
+    for (int k = 0; k < kBc6fFloats; ++k) rec[k] = 0.f;
+    int part = 0, mode = 0;
+    const int mi = mode_index(blk);
+    if (mi < 0) {
+#pragma unroll
+        for (int k = 0; k < 12; ++k) rec[k] = bc6f_endpoint_param(0, 10);
+    } else {
+        const NtBc6hMode M = c_modes[mi];
+        const uint64_t lo = (uint64_t)blk.w[0] | ((uint64_t)blk.w[1] << 32),
+                       hi = (uint64_t)blk.w[2] | ((uint64_t)blk.w[3] << 32);
+        int e[4][3];
+        int d = 0;
+        bc6h_unpack_header(mi, lo, hi, e, d);
+        const int ne = 2 * M.regions, epb = M.endpoint_bits;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+#pragma unroll
+            for (int i = 1; i < 4; ++i)
+                if (i < ne && M.transformed) e[i][c] = (e[0][c] + sign_extend(e[i][c], M.delta_bits[c])) & ((1 << epb) - 1);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                if (i < ne) e[i][c] = unquantize(e[i][c], epb, false);
+        }
+        const bool two = M.regions == 2;
+        const int b = two ? epb : 10;
+        if (two) {
+            part = d;
+            mode = mi;
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int c = 0; c < 3; ++c) rec[6 * r + 3 * i + c] = bc6f_endpoint_param(two ? e[2 * r + i][c] : e[i][c], b);
+        const int ib = two ? 3 : 4;
+        const int anchor1 = two ? c_anchors[d] : -1;
+        uint64_t sbits = hi >> (M.header_bits - 64);
+#pragma unroll
+        for (int px = 0; px < 16; ++px) {
+            const int nb = ib - ((px == 0 || px == anchor1) ? 1 : 0);
+            const int idx = (int)(sbits & ((1u << nb) - 1u));
+            sbits >>= nb;
+            rec[12 + px] = __fdiv_rn((float)bc6h_weight(idx, two), 512.f);
+        }
+    }
+    rec[28] = __int_as_float(part);
+    rec[29] = __int_as_float(mode);
+    float4 *out = reinterpret_cast<float4 *>(records + (((int64_t)by * bw + bx) * nt + t) * kBc6fFloats);
+#pragma unroll
+    for (int k = 0; k < kBc6fFloats / 4; ++k) out[k] = make_float4(rec[4 * k], rec[4 * k + 1], rec[4 * k + 2], rec[4 * k + 3]);
+}
+
+// One candidate mode for the record targets; returns the error or -1 when the deltas do not fit.
+__device__ int64_t bc6f_try_mode(int mi, int part, const int (&U)[2][2][3], const int32_t (&T)[16][3], Cand &out)
+{
+    const NtBc6hMode M = c_modes[mi];
+    const int regions = M.regions, epb = M.endpoint_bits, ib = regions == 2 ? 3 : 4;
+    const int ni = 1 << ib;
+    const uint32_t mask = regions == 2 ? c_parts[part] : 0u;
+    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
+    int q[2][2][3], u[2][2][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                q[r][i][c] = quantize_unsigned(U[r][i][c], epb);
+                u[r][i][c] = unquantize(q[r][i][c], epb, false);
+            }
+    int idx[16];
+    int64_t err = 0;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        const int r = (mask >> px) & 1;
+        int64_t best = INT64_MAX;
+        int bi = 0;
+#pragma unroll 1
+        for (int k = 0; k < ni; ++k) {
+            const int w = bc6h_weight(k, ib == 3);
+            int64_t dsum = 0;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int a = r ? u[1][0][c] : u[0][0][c], bb = r ? u[1][1][c] : u[0][1][c];
+                const int v = (a * (64 - w) + bb * w + 32) >> 6;
+                const int64_t dd = (int64_t)(T[px][c] - 64 * v);
+                dsum += dd * dd;
+            }
+            if (dsum < best) {
+                best = dsum;
+                bi = k;
+            }
+        }
+        idx[px] = bi;
+        err += best;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        if (r >= regions) break;
+        const int ap = r == 0 ? 0 : anchor1;
+        int aidx = 0;
+#pragma unroll
+        for (int px = 0; px < 16; ++px)
+            if (px == ap) aidx = idx[px];
+        if (aidx < ni / 2) continue;
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int t = q[r][0][c];
+            q[r][0][c] = q[r][1][c];
+            q[r][1][c] = t;
+        }
+#pragma unroll
+        for (int px = 0; px < 16; ++px)
+            if ((int)((mask >> px) & 1) == r) idx[px] = ni - 1 - idx[px];
+    }
+    int e[4][3];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) e[2 * r + i][c] = r < regions ? q[r][i][c] : 0;
+    if (M.transformed) {
+        // the decoder adds deltas modulo 2^epb, so the difference is taken modulo 2^epb
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+            if (i >= 2 * regions) break;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int dlt = sign_extend(e[i][c] - e[0][c], epb);
+                const int db = M.delta_bits[c];
+                if (dlt < -(1 << (db - 1)) || dlt > (1 << (db - 1)) - 1) return -1;
+                e[i][c] = dlt;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) out.e[i][c] = e[i][c];
+    uint64_t pk = 0;
+#pragma unroll
+    for (int px = 0; px < 16; ++px) pk |= (uint64_t)idx[px] << (4 * px);
+    out.idx = pk;
+    out.mi = mi;
+    out.part = part;
+    return err;
+}
+
+__device__ __forceinline__ double clamp_target(double v, double hi) { return fmin(fmax(v, 0.0), hi); }  // NaN -> 0
+
+// grid: (ceil(block columns / 128), block rows, channel triples); one thread per record
+__global__ void __launch_bounds__(128) bc6f_to_bc6h_kernel(const float *__restrict__ records, uint4 *__restrict__ blocks,
+                                                           int bw, int bh, int nt)
+{
+    const int bx = blockIdx.x * blockDim.x + threadIdx.x, by = blockIdx.y, t = blockIdx.z;
+    if (bx >= bw) return;
+    const float4 *in = reinterpret_cast<const float4 *>(records + (((int64_t)by * bw + bx) * nt + t) * kBc6fFloats);
+    float rec[kBc6fFloats];
+#pragma unroll
+    for (int k = 0; k < kBc6fFloats / 4; ++k) {
+        const float4 v = __ldg(in + k);
+        rec[4 * k] = v.x;
+        rec[4 * k + 1] = v.y;
+        rec[4 * k + 2] = v.z;
+        rec[4 * k + 3] = v.w;
+    }
+    const int part = __float_as_int(rec[28]) & 31;
+    const int own = (unsigned)__float_as_int(rec[29]) > 9u ? 0 : __float_as_int(rec[29]);
+    const int b = bc6f_mode_bits(own);
+    int U[2][2][3];
+#pragma unroll
+    for (int k = 0; k < 12; ++k) {
+        const double v = __ddiv_rn(__dmul_rn((double)bc6f_unquantize(rec[k], b), 64.0), 31.0);
+        U[k / 6][(k / 3) & 1][k % 3] = (int)floor(__dadd_rn(clamp_target(v, 65535.0), 0.5));
+    }
+    int32_t T[16][3];  // <= 64 * 65535
+    const uint32_t pmask = c_parts[part];
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        const int r = (pmask >> px) & 1;
+        const double a = __dmul_rn(512.0, (double)rec[12 + px]);
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int u0 = r ? U[1][0][c] : U[0][0][c], u1 = r ? U[1][1][c] : U[0][1][c];
+            const double v = __dadd_rn(__dmul_rn(64.0, (double)u0), __dmul_rn((double)(u1 - u0), a));
+            T[px][c] = (int32_t)floor(__dadd_rn(clamp_target(v, 64.0 * 65535.0), 0.5));
+        }
+    }
+    bool same = true;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int c = 0; c < 3; ++c) same = same && U[0][i][c] == U[1][i][c];
+    int64_t best = INT64_MAX;
+    Cand cand, winner;
+#pragma unroll 1
+    for (int k = 0; k < 14; ++k) {
+        const int mi = k == 0 ? own : (k <= 9 ? (k - 1 < own ? k - 1 : k) : k);
+        if (mi >= 10 && !same) break;
+        const int64_t e = bc6f_try_mode(mi, mi < 10 ? part : 0, U, T, cand);
+        if (e >= 0 && e < best) {
+            best = e;
+            winner = cand;
+        }
+    }
+    Block128 out;
+    if (best == INT64_MAX) out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;  // unreachable: mode 10 always fits
+    else pack_block(winner, out);
+    blocks[((int64_t)t * bh + by) * bw + bx] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
+}
+
+cudaError_t launch_bc6f_convert(const void *blocks, float *records, int32_t w, int32_t h, int32_t channels,
+                                bool to_records, cudaStream_t st)
+{
+    const int bw = w / 4, bh = h / 4, nt = (channels + 2) / 3;
+    if (bh > 65535 || nt > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((bw + 127) / 128, bh, nt);
+    uint4 *bl = reinterpret_cast<uint4 *>(const_cast<void *>(blocks));
+    if (to_records)
+        bc6f_from_bc6h_kernel<<<grid, 128, 0, st>>>(bl, records, bw, bh, nt);
+    else
+        bc6f_to_bc6h_kernel<<<grid, 128, 0, st>>>(records, bl, bw, bh, nt);
     count_launch();
     return cudaGetLastError();
 }

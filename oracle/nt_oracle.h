@@ -137,6 +137,13 @@ void nto_bc6h_encode_surface(const uint16_t *data, int32_t w, int32_t h, int32_t
 void nto_bc6h_decode_surface(const uint8_t *blocks, int32_t w, int32_t h, int32_t channels,
                              int64_t cstride, int64_t rstride, int64_t tstride, float bias,
                              uint16_t *data, int32_t threads);
+/* Float BC6 block records (32 floats per triple, NTO_BC6F_FLOATS) <-> BC6H UF16 blocks;
+ * surfaces need w and h multiples of 4: records [h/4][w/4][ceil(channels/3)][32], blocks as
+ * above. */
+void nto_bc6f_from_bc6h_block(const uint8_t block[16], float rec[32]);
+void nto_bc6f_to_bc6h_block(const float rec[32], uint8_t out[16]);
+void nto_bc6f_from_bc6h_surface(const uint8_t *blocks, int32_t w, int32_t h, int32_t channels, float *records);
+void nto_bc6f_to_bc6h_surface(const float *records, int32_t w, int32_t h, int32_t channels, uint8_t *blocks);
 
 /* ---- tests/forward_pass_test.cu:45-150 known-answer test ---------------------------- */
 void nto_fwdtest_generate(uint16_t inputs[32 * 12], uint16_t w0[256], uint16_t w1[256],

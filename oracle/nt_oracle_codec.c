@@ -26,6 +26,7 @@
  *      transformed deltas fit, pick the nearest palette entry per texel; the candidate with
  *      the smallest integer squared error wins (ties: first in the order above).
  */
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -449,4 +450,250 @@ void nto_bc6h_decode_surface(const uint8_t *blocks, int32_t w, int32_t h, int32_
         }
     }
     (void)threads;
+}
+
+/* ---- float BC6 block records <-> BC6H blocks ----------------------------------------------
+ *
+ * Bridge between the reference's float BC6 block records (train.cu:161-212: per channel
+ * triple of a 4x4 block 32 floats, endpoints [region][endpoint][xyz] at 0..11, pixel
+ * indices at 12..27, partition and mode as int32 bits at 28 and 29) and the integer BC6H
+ * bitstream above.  The reference decodes ebar = (31744 e + 32768) 2^-b and
+ * y = ebar0 + 8 (ebar1 - ebar0) x, y standing for a half-float bit pattern; the format reaches
+ * the half bits (v * 31) >> 6 from unquantized endpoints u and weights w / 64.  Taking
+ * ebar = 31 u / 64 and x = w / 512 maps one onto the other (the reference has no such bridge;
+ * its block-feature path starts from and ends in float records).
+ *
+ * from BC6H: e = (31 u 2^b / 64 - 32768) / 31744 (double, one rounding, then float),
+ *   x = w / 512; two-region modes keep their partition and mode (the reference's ten mode
+ *   precisions are those of BC6H modes 1-10, train.cu:31-34); one-region modes (11-14) give
+ *   both regions the same endpoints, partition 0 and record mode 0 (10 bits); reserved modes
+ *   give records that decode to zero (e = -32768 / 31744, x = 0).
+ * to BC6H: endpoint targets U = round(64 ebar / 31) in [0, 65535]; texel targets
+ *   T = round(64 U0 + (U1 - U0) 512 x) in [0, 64 * 65535] (units of 1/64); candidates: the
+ *   record's mode, the other two-region modes in order, then the one-region modes 11-14 when
+ *   both regions' targets are equal; per candidate the endpoints are quantized to the mode
+ *   precision (nearest unquantized value), each texel takes the palette index with the
+ *   smallest sum_c (T_c - 64 v_c)^2 (ties: lower index), a region whose anchor index has its
+ *   top bit set swaps its endpoints and flips its indices (w(n-1-i) = 64 - w(i): the decoded
+ *   values do not change), transformed deltas must fit; the smallest error wins (ties: the
+ *   earlier candidate).  A record made from a block therefore returns a block that decodes to
+ *   the same texels.
+ */
+#define BC6F_FLOATS 32
+
+static float bc6f_ebar(float e, int b) /* train.cu:161-167 */
+{
+    const float scale = (31.f / 64.f) * 65536.f;
+    return ldexpf(scale * e + 32768.f, -b);
+}
+
+static float bc6f_endpoint_param(int u, int b)
+{
+    return (float)(((double)(31 * u) * ldexp(1.0, b - 6) - 32768.0) / 31744.0);
+}
+
+static const int BC6F_MODE_BITS[10] = {10, 7, 11, 11, 11, 9, 8, 8, 8, 6}; /* train.cu:31-34 */
+
+static int bc6f_mode_of(const float rec[BC6F_FLOATS])
+{
+    int32_t m;
+    memcpy(&m, &rec[29], 4);
+    return (uint32_t)m > 9u ? 0 : m;
+}
+
+void nto_bc6f_from_bc6h_block(const uint8_t block[16], float rec[BC6F_FLOATS])
+{
+    memset(rec, 0, BC6F_FLOATS * sizeof(float));
+    int32_t part = 0, mode = 0;
+    const int mi = nto_bc6h_mode_index(block);
+    if (mi < 0) {
+        for (int k = 0; k < 12; ++k) rec[k] = bc6f_endpoint_param(0, 10);
+    } else {
+        const NtBc6hMode *M = &MODES[mi];
+        int e[4][3] = {{0}};
+        int d = 0;
+        for (int k = 0; k < M->header_bits; ++k) {
+            const int f = LAYOUT[mi][k] >> 4, bit = LAYOUT[mi][k] & 15;
+            const int v = get_bit(block, k);
+            if (f < 12)
+                e[f / 3][f % 3] |= v << bit;
+            else if (f == NT_BC6H_FIELD_D)
+                d |= v << bit;
+        }
+        const int ne = 2 * M->regions, epb = M->endpoint_bits;
+        for (int c = 0; c < 3; ++c) {
+            if (M->transformed)
+                for (int i = 1; i < ne; ++i) e[i][c] = (e[0][c] + sign_extend(e[i][c], M->delta_bits[c])) & ((1 << epb) - 1);
+            for (int i = 0; i < ne; ++i) e[i][c] = unquantize(e[i][c], epb, 0);
+        }
+        const int two = M->regions == 2;
+        const int b = two ? epb : 10;
+        if (two) {
+            part = d;
+            mode = mi;
+        }
+        for (int r = 0; r < 2; ++r)
+            for (int i = 0; i < 2; ++i)
+                for (int c = 0; c < 3; ++c) rec[6 * r + 3 * i + c] = bc6f_endpoint_param(e[two ? 2 * r + i : i][c], b);
+        const int ib = two ? 3 : 4;
+        int pos = M->header_bits;
+        for (int px = 0; px < 16; ++px) {
+            const int nb = ib - (px == 0 || (two && px == ANCHORS[d]));
+            const int idx = get_bits(block, pos, nb);
+            pos += nb;
+            rec[12 + px] = (float)(ib == 3 ? W3[idx] : W4[idx]) / 512.f;
+        }
+    }
+    memcpy(&rec[28], &part, 4);
+    memcpy(&rec[29], &mode, 4);
+}
+
+/* Candidate mi for the record targets; returns the error or -1 when the deltas do not fit. */
+static int64_t bc6f_try_mode(int mi, int part, const int U[2][2][3], const int64_t T[16][3], uint8_t out[16])
+{
+    const NtBc6hMode *M = &MODES[mi];
+    const int regions = M->regions, epb = M->endpoint_bits, ib = regions == 2 ? 3 : 4;
+    const int ni = 1 << ib;
+    const uint16_t mask = regions == 2 ? PARTS[part] : 0;
+    int q[2][2][3], u[2][2][3];
+    for (int r = 0; r < 2; ++r)
+        for (int i = 0; i < 2; ++i)
+            for (int c = 0; c < 3; ++c) {
+                q[r][i][c] = quantize_unsigned(U[r][i][c], epb);
+                u[r][i][c] = unquantize(q[r][i][c], epb, 0);
+            }
+    int idx[16];
+    int64_t err = 0;
+    for (int px = 0; px < 16; ++px) {
+        const int r = (mask >> px) & 1;
+        int64_t best = INT64_MAX;
+        int bi = 0;
+        for (int k = 0; k < ni; ++k) {
+            const int w = ib == 3 ? W3[k] : W4[k];
+            int64_t dsum = 0;
+            for (int c = 0; c < 3; ++c) {
+                const int v = (u[r][0][c] * (64 - w) + u[r][1][c] * w + 32) >> 6;
+                const int64_t dd = T[px][c] - 64 * (int64_t)v;
+                dsum += dd * dd;
+            }
+            if (dsum < best) {
+                best = dsum;
+                bi = k;
+            }
+        }
+        idx[px] = bi;
+        err += best;
+    }
+    for (int r = 0; r < regions; ++r) {
+        const int ap = r == 0 ? 0 : ANCHORS[part];
+        if (idx[ap] < ni / 2) continue;
+        for (int c = 0; c < 3; ++c) {
+            const int t = q[r][0][c];
+            q[r][0][c] = q[r][1][c];
+            q[r][1][c] = t;
+        }
+        for (int px = 0; px < 16; ++px)
+            if ((int)((mask >> px) & 1) == r) idx[px] = ni - 1 - idx[px];
+    }
+    int e[4][3];
+    for (int r = 0; r < 2; ++r)
+        for (int i = 0; i < 2; ++i)
+            for (int c = 0; c < 3; ++c) e[2 * r + i][c] = r < regions ? q[r][i][c] : 0;
+    if (M->transformed) {
+        /* the decoder adds deltas modulo 2^epb, so the difference is taken modulo 2^epb */
+        for (int i = 1; i < 2 * regions; ++i)
+            for (int c = 0; c < 3; ++c) {
+                const int dlt = sign_extend(e[i][c] - e[0][c], epb);
+                const int db = M->delta_bits[c];
+                if (dlt < -(1 << (db - 1)) || dlt > (1 << (db - 1)) - 1) return -1;
+                e[i][c] = dlt;
+            }
+    }
+    memset(out, 0, 16);
+    for (int k = 0; k < M->header_bits; ++k) {
+        const int f = LAYOUT[mi][k] >> 4, bit = LAYOUT[mi][k] & 15;
+        int v;
+        if (f < 12)
+            v = ((unsigned)e[f / 3][f % 3] >> bit) & 1;
+        else if (f == NT_BC6H_FIELD_D)
+            v = (part >> bit) & 1;
+        else
+            v = (M->mode_value >> bit) & 1;
+        set_bit(out, k, v);
+    }
+    int pos = M->header_bits;
+    for (int px = 0; px < 16; ++px) {
+        const int nb = ib - (px == 0 || (regions == 2 && px == ANCHORS[part]));
+        for (int b = 0; b < nb; ++b) set_bit(out, pos + b, (idx[px] >> b) & 1);
+        pos += nb;
+    }
+    return err;
+}
+
+static double bc6f_clamp(double v, double hi)
+{
+    return fmin(fmax(v, 0.0), hi); /* NaN -> 0 */
+}
+
+void nto_bc6f_to_bc6h_block(const float rec[BC6F_FLOATS], uint8_t out[16])
+{
+    int32_t part;
+    memcpy(&part, &rec[28], 4);
+    part &= 31;
+    const int own = bc6f_mode_of(rec), b = BC6F_MODE_BITS[own];
+    int U[2][2][3];
+    for (int r = 0; r < 2; ++r)
+        for (int i = 0; i < 2; ++i)
+            for (int c = 0; c < 3; ++c) {
+                const double t = (double)bc6f_ebar(rec[6 * r + 3 * i + c], b) * 64.0 / 31.0;
+                U[r][i][c] = (int)floor(bc6f_clamp(t, 65535.0) + 0.5);
+            }
+    int64_t T[16][3];
+    for (int px = 0; px < 16; ++px) {
+        const int r = (PARTS[part] >> px) & 1;
+        const double a = 512.0 * (double)rec[12 + px];
+        for (int c = 0; c < 3; ++c) {
+            const double t = 64.0 * U[r][0][c] + (double)(U[r][1][c] - U[r][0][c]) * a;
+            T[px][c] = (int64_t)floor(bc6f_clamp(t, 64.0 * 65535.0) + 0.5);
+        }
+    }
+    int64_t best = INT64_MAX;
+    uint8_t cand[16];
+    for (int k = 0; k < 14; ++k) {
+        int mi;
+        if (k == 0)
+            mi = own;
+        else if (k <= 9)
+            mi = k - 1 < own ? k - 1 : k;
+        else
+            mi = k;
+        if (mi >= 10 && memcmp(U[0], U[1], sizeof U[0]) != 0) break;
+        const int64_t e = bc6f_try_mode(mi, mi < 10 ? part : 0, U, T, cand);
+        if (e >= 0 && e < best) {
+            best = e;
+            memcpy(out, cand, 16);
+        }
+    }
+    if (best == INT64_MAX) memset(out, 0, 16); /* unreachable: mode 10 (6 bits) always fits */
+}
+
+/* records [block row][block column][triple][32] <-> blocks [triple][block row][block column] */
+void nto_bc6f_from_bc6h_surface(const uint8_t *blocks, int32_t w, int32_t h, int32_t channels, float *records)
+{
+    const int bw = w / 4, bh = h / 4, nt = (channels + 2) / 3;
+    for (int t = 0; t < nt; ++t)
+        for (int by = 0; by < bh; ++by)
+            for (int bx = 0; bx < bw; ++bx)
+                nto_bc6f_from_bc6h_block(blocks + (((int64_t)t * bh + by) * bw + bx) * 16,
+                                         records + (((int64_t)by * bw + bx) * nt + t) * BC6F_FLOATS);
+}
+
+void nto_bc6f_to_bc6h_surface(const float *records, int32_t w, int32_t h, int32_t channels, uint8_t *blocks)
+{
+    const int bw = w / 4, bh = h / 4, nt = (channels + 2) / 3;
+    for (int t = 0; t < nt; ++t)
+        for (int by = 0; by < bh; ++by)
+            for (int bx = 0; bx < bw; ++bx)
+                nto_bc6f_to_bc6h_block(records + (((int64_t)by * bw + bx) * nt + t) * BC6F_FLOATS,
+                                       blocks + (((int64_t)t * bh + by) * bw + bx) * 16);
 }

@@ -323,6 +323,10 @@ def _codec_lib():
                                               C.c_int64, C.c_float, _u8p, C.c_int32]
         L.nto_bc6h_decode_surface.argtypes = [_u8p, C.c_int32, C.c_int32, C.c_int32, C.c_int64, C.c_int64,
                                               C.c_int64, C.c_float, u16p, C.c_int32]
+        L.nto_bc6f_from_bc6h_block.argtypes = [_u8p, f32p]
+        L.nto_bc6f_to_bc6h_block.argtypes = [f32p, _u8p]
+        L.nto_bc6f_from_bc6h_surface.argtypes = [_u8p, C.c_int32, C.c_int32, C.c_int32, f32p]
+        L.nto_bc6f_to_bc6h_surface.argtypes = [f32p, C.c_int32, C.c_int32, C.c_int32, _u8p]
         L._codec_bound = True
     return L
 
@@ -390,6 +394,22 @@ def bc6f_decode(e0, e1, bits: int, x: float) -> np.ndarray:
     b = np.ascontiguousarray(e1, np.float32)
     out = np.zeros(3, np.float32)
     _codec_lib().nto_bc6f_decode(_p(a, f32p), _p(b, f32p), int(bits), float(x), _p(out, f32p))
+    return out
+
+
+def bc6f_from_bc6h(blocks: np.ndarray, w: int, h: int, channels: int) -> np.ndarray:
+    """BC6H blocks [triple][h/4][w/4] x 16 B -> float BC6 records [h/4][w/4][triple][32]."""
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    out = np.zeros((h // 4) * (w // 4) * ((channels + 2) // 3) * 32, np.float32)
+    _codec_lib().nto_bc6f_from_bc6h_surface(blocks.ctypes.data_as(_u8p), w, h, channels, _p(out, f32p))
+    return out
+
+
+def bc6f_to_bc6h(records: np.ndarray, w: int, h: int, channels: int) -> np.ndarray:
+    """Float BC6 records -> BC6H blocks (layouts as bc6f_from_bc6h)."""
+    records = np.ascontiguousarray(records, np.float32)
+    out = np.zeros((h // 4) * (w // 4) * ((channels + 2) // 3) * 16, np.uint8)
+    _codec_lib().nto_bc6f_to_bc6h_surface(_p(records, f32p), w, h, channels, out.ctypes.data_as(_u8p))
     return out
 
 

@@ -122,3 +122,97 @@ def test_block_adam_bit_exact(cuda, oracle):
         assert np.array_equal(tex.gm2[g].cpu().numpy().view(np.uint32), m2.view(np.uint32))
         assert np.all(tex.ggrads[g].cpu().numpy() == 0)
         assert np.array_equal(got.reshape(-1, 32)[:, 28:30].view(np.int32), recs[g].reshape(-1, 32)[:, 28:30].view(np.int32))
+
+
+# ---- block records <-> BC6H blocks (nt_bc6f_from_bc6h / nt_bc6f_to_bc6h) -----------------
+
+def _edge_records(rng, n):
+    """Records outside the trained range: NaN / inf endpoints and indices, negative and large
+    pixel indices, far endpoints, out-of-range partition and mode fields."""
+    rec = np.zeros((n, 32), np.float32)
+    rec[:, :12] = rng.uniform(-3000.0, 3000.0, (n, 12))
+    rec[:, 12:28] = rng.uniform(-0.5, 0.7, (n, 16))
+    rec[0, 3] = np.nan
+    rec[1, 14] = np.inf
+    rec[2, 0] = -np.inf
+    rec[3, 20] = np.nan
+    rec[:, 28].view(np.int32)[:] = rng.integers(-100, 100, n)
+    rec[:, 29].view(np.int32)[:] = rng.integers(-3, 14, n)
+    return rec.reshape(-1)
+
+
+def test_bridge_matches_oracle(cuda, oracle):
+    import torch
+    import neural_textures_b200 as nt
+    rng = np.random.default_rng(41)
+    dev = torch.device("cuda", 0)
+    # bitstreams: random raw blocks (every mode) and blocks our encoder writes
+    W, H, C = 64, 32, 12
+    raw = rng.integers(0, 256, nt.bc6h_blocks_bytes(W, H, C), dtype=np.uint8)
+    lat = oracle.smooth_latents(rng, (C, H, W))
+    enc = oracle.bc6h_encode_surface(lat, "planar", 4.0)
+    for blocks in (raw, enc):
+        got = nt.bc6f_from_bc6h(torch.from_numpy(blocks).to(dev), W, H, C).cpu().numpy()
+        want = oracle.bc6f_from_bc6h(blocks, W, H, C)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        back = nt.bc6f_to_bc6h(torch.from_numpy(want).to(dev), W, H, C).cpu().numpy()
+        assert np.array_equal(back, oracle.bc6f_to_bc6h(want, W, H, C))
+    # trained-like and out-of-range records
+    n = (W // 4) * (H // 4) * (C // 3)
+    for rec in (realistic_blocks(rng, W, H, C), _edge_records(rng, n)):
+        got = nt.bc6f_to_bc6h(torch.from_numpy(rec).to(dev), W, H, C).cpu().numpy()
+        assert np.array_equal(got, oracle.bc6f_to_bc6h(rec, W, H, C))
+
+
+def _smooth_texture(oracle, seed):
+    import torch
+    image, grids, Cc, cout, lattice = CASES[0]
+    tex = make_texture(image, grids, Cc, cout, lattice=lattice, seed=seed)
+    rng = np.random.default_rng(seed)
+    for g, (w, h) in zip(tex.grids, grids):
+        lat = oracle.smooth_latents(rng, (Cc, h, w)).transpose(1, 2, 0).copy()
+        g.copy_(torch.from_numpy(lat).view(torch.float16).to(g.device))
+    tex.step = 3
+    return tex
+
+
+def _finalize_loss(tex):
+    import neural_textures_b200 as nt
+    return _gpu(tex, nt.TrainingKernelType.FINALIZE)[0]
+
+
+def test_to_blocks_keeps_the_encoded_network_output(cuda, oracle):
+    """After to_blocks the block features reproduce the loss of the BC6H-decoded grids (the
+    records decode within one fp16 ulp of the blocks; layer 1 absorbs the codec bias)."""
+    import neural_textures_b200 as nt
+    tex = _smooth_texture(oracle, 51)
+    bias = 4.0
+    for g in tex.grids:  # grids as the codec returns them
+        nt.bc6h_decode(nt.bc6h_encode(g, "interleaved", bias), g, "interleaved", bias)
+    want = _finalize_loss(tex)
+    tex.to_blocks(bias)
+    got = _finalize_loss(tex)
+    assert _status() == 0
+    assert abs(got - want) <= 1e-2 * want, (got, want)
+
+
+def test_export_and_return_to_grids(cuda, oracle):
+    """Records made from encoded grids export to the very same bitstream; from_bc6h brings
+    the decoded grids and the original layer-1 bias back."""
+    import torch
+    import neural_textures_b200 as nt
+    tex = _smooth_texture(oracle, 61)
+    bias = 4.0
+    enc = [nt.bc6h_encode(g, "interleaved", bias) for g in tex.grids]
+    b1 = tex.b[0].clone()
+    tex.to_blocks(bias)
+    exported = tex.export_bc6h()
+    for a, b in zip(exported, enc):
+        assert torch.equal(a, b)
+    tex.from_bc6h(exported)
+    assert tex.latent_format == nt._native.NT_LATENT_GRID_F16
+    assert (tex.b[0].float() - b1.float()).abs().max().item() <= 1e-2  # two fp16 roundings of a shift of a few units
+    for g, e in zip(tex.grids, enc):
+        ref = torch.empty_like(g)
+        nt.bc6h_decode(e, ref, "interleaved", bias)
+        assert torch.equal(g, ref)

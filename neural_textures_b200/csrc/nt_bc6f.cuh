@@ -30,11 +30,19 @@ __device__ __forceinline__ int bc6f_mode_bits(int mode)  // train.cu:31-34
     return (int)((packed >> (4 * m)) & 15u);
 }
 
+// x * 2^n.  While 2^n is a normal float (every scale a record's decode produces) this is one
+// correctly rounded product of the exact value x 2^n, i.e. ldexpf(x, n); other n take ldexpf.
+__device__ __forceinline__ float scale2(float x, int n)
+{
+    if ((unsigned)(n + 126) <= 253u) return __fmul_rn(x, __int_as_float((n + 127) << 23));
+    return ldexpf(x, n);
+}
+
 // train.cu:161-167
 __device__ __forceinline__ float bc6f_unquantize(float e, int b)
 {
     const float scale = (31.f / 64.f) * 65536.f;
-    return ldexpf(__fadd_rn(__fmul_rn(scale, e), 32768.f), -b);
+    return scale2(__fadd_rn(__fmul_rn(scale, e), 32768.f), -b);
 }
 
 // train.cu:169-182 per channel, with the intermediates of train.cu:184-202
@@ -48,10 +56,11 @@ __device__ __forceinline__ Bc6fChannel bc6f_channel(float e0, float e1, int b, f
     Bc6fChannel r;
     r.eb0 = bc6f_unquantize(e0, b);
     r.eb1 = bc6f_unquantize(e1, b);
-    r.y = __fadd_rn(r.eb0, __fmul_rn(ldexpf(__fsub_rn(r.eb1, r.eb0), 3), x));
-    const float hyf = fmaxf(__fsub_rn(floorf(__fdiv_rn(__fsub_rn(r.y, 1.f), 1024.f)), 1.f), 0.f);
+    // v / 1024 == v * 2^-10 exactly (both round the same real number)
+    r.y = __fadd_rn(r.eb0, __fmul_rn(__fmul_rn(__fsub_rn(r.eb1, r.eb0), 8.f), x));
+    const float hyf = fmaxf(__fsub_rn(floorf(__fmul_rn(__fsub_rn(r.y, 1.f), 0x1p-10f)), 1.f), 0.f);
     r.hy = (int)hyf;
-    r.w = ldexpf(__fsub_rn(__fdiv_rn(r.y, 1024.f), (float)r.hy), r.hy - 14);
+    r.w = scale2(__fsub_rn(__fmul_rn(r.y, 0x1p-10f), (float)r.hy), r.hy - 14);
     return r;
 }
 
@@ -124,16 +133,15 @@ __device__ __forceinline__ void bc6f_backward_texel(const float *__restrict__ bl
         const int r = (c_bc6f_parts[part] >> pix) & 1;
         const int bits = bc6f_mode_bits(mode);
         const float xv = __ldg(p + 12 + pix);
-        const float alpha = ldexpf(xv, 3);
-        const float deibar_dei = ldexpf(31.f / 64, 16 - bits);
+        const float alpha = __fmul_rn(xv, 8.f);
+        const float deibar_dei = scale2(31.f / 64, 16 - bits);
         float dl_dx = 0.f;
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
             if (3 * t + c >= C) break;
             const Bc6fChannel ch = bc6f_channel(__ldg(p + 6 * r + c), __ldg(p + 6 * r + 3 + c), bits, xv);
-            const float hyf = fmaxf(__fsub_rn(floorf(__fdiv_rn(__fsub_rn(ch.y, 1.f), 1024.f)), 1.f), 0.f);
-            const float dl_dy = ldexpf(fg[3 * t + c], (int)hyf - 24);
-            dl_dx = __fadd_rn(dl_dx, __fmul_rn(dl_dy, ldexpf(__fsub_rn(ch.eb1, ch.eb0), 3)));
+            const float dl_dy = scale2(fg[3 * t + c], ch.hy - 24);
+            dl_dx = __fadd_rn(dl_dx, __fmul_rn(dl_dy, __fmul_rn(__fsub_rn(ch.eb1, ch.eb0), 8.f)));
             atomicAdd(gp + 6 * r + c, __fmul_rn(__fmul_rn(__fsub_rn(1.f, alpha), deibar_dei), dl_dy));
             atomicAdd(gp + 6 * r + 3 + c, __fmul_rn(__fmul_rn(alpha, deibar_dei), dl_dy));
         }

@@ -35,7 +35,9 @@
 //
 // Latent gradients: dX rows go to shared memory and a column sweep over the tile's
 // footprint window accumulates them per texel before one float4 reduction per 4 channels
-// (per-tap vector atomics when a window does not fit).
+// (per-tap vector atomics when a window does not fit).  Block features (BLK) take the same
+// per-texel sums through the BC6 backward into the block records, once per window texel
+// instead of once per tap.
 //
 // Every wait is bounded.  A timeout sets bit 0 of the device status word (read back by
 // nt_read_device_status); the CTA agrees on it at its next barrier, stops issuing work,
@@ -231,7 +233,10 @@ __device__ __forceinline__ void window_cands(Smem<C> &s, int gi, int lane)
 
 // ---- latent-gradient column sweep (see nt_train.cu for the derivation) -------------------
 
-template <int C>
+// Latent gradient sum of one texel (x 1 / num_samples) into the grid gradients, or, for block
+// features, through the BC6 backward into the texel's block records (train.cu:436-454; the
+// backward is linear in the feature gradient, so summing a texel's taps first is exact).
+template <int C, bool BLK>
 __device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, int ty, const float (&row)[C])
 {
     bool any = false;
@@ -242,13 +247,20 @@ __device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, 
     const float sc = p.inv_num_samples;
     const int sy = stored_row(p, gi, ty, gh);
     if (sy < 0) return;
+    if constexpr (BLK) {
+        float fg[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) fg[c] = row[c] * sc;
+        bc6f_backward_texel<C>(reinterpret_cast<const float *>(p.grid[gi]), p.ggrid[gi], gw, wrap_coord(tx, gw), sy, fg);
+        return;
+    }
     float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)sy * gw + wrap_coord(tx, gw)) * C);
 #pragma unroll
     for (int q = 0; q < C / 4; ++q)
         atomicAdd(dst + q, make_float4(row[4 * q] * sc, row[4 * q + 1] * sc, row[4 * q + 2] * sc, row[4 * q + 3] * sc));
 }
 
-template <int C, int L>
+template <int C, int L, bool BLK>
 __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p, int r)
 {
     constexpr int kRows = 2, kChunks = kTileH / kRows, DXS = Cfg<C>::DXS;
@@ -278,7 +290,7 @@ __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p,
             const int fy = rmin - 1;
             if (fy_cur == INT_MIN) fy_cur = fy;
             while (fy > fy_cur) {
-                flush_row<C>(p, gi, tx, fy_cur, R[0]);
+                flush_row<C, BLK>(p, gi, tx, fy_cur, R[0]);
 #pragma unroll
                 for (int m = 0; m < 4; ++m)
 #pragma unroll
@@ -317,12 +329,13 @@ __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p,
         }
         if (fy_cur == INT_MIN) continue;
 #pragma unroll
-        for (int m = 0; m < 5; ++m) flush_row<C>(p, gi, tx, fy_cur + m, R[m]);
+        for (int m = 0; m < 5; ++m) flush_row<C, BLK>(p, gi, tx, fy_cur + m, R[m]);
     }
 }
 
-// Per-sample, per-tap vector atomics (windows the sweep does not handle).
-template <int C>
+// Per-sample, per-tap vector atomics (windows the sweep does not handle); block features
+// take the BC6 backward per tap.
+template <int C, bool BLK>
 __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLaunch &p, int gi, int r)
 {
     const float *dxr = reinterpret_cast<const float *>(s.t.m.H2) + r * Cfg<C>::DXS + gi * C;
@@ -334,6 +347,14 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
         if (yy < 0) continue;
         for (int i = 0; i < 4; ++i) {
             const int xx = wrap_coord(b.x - 1 + i, gw);
+            if constexpr (BLK) {
+                const float wgt = __fmul_rn(s.wts[gi][r][4 + j], s.wts[gi][r][i]);
+                float fg[C];
+#pragma unroll
+                for (int k = 0; k < C; ++k) fg[k] = __fmul_rn(__fmul_rn(wgt, dxr[k]), scale);
+                bc6f_backward_texel<C>(reinterpret_cast<const float *>(p.grid[gi]), p.ggrid[gi], gw, xx, yy, fg);
+                continue;
+            }
             const float wgt = s.wts[gi][r][i] * s.wts[gi][r][4 + j] * scale;
             float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)yy * gw + xx) * C);
 #pragma unroll
@@ -444,6 +465,35 @@ __device__ __forceinline__ void scatter_stage_out(Smem<C> &s, uint32_t tmem, int
 #pragma unroll
             for (int j = 0; j < 16; ++j) o[8 * j] = __uint_as_float(v[j]);
         }
+    }
+}
+
+// Staged window sums of block features -> the BC6 backward of every window texel.
+template <int C>
+__device__ __forceinline__ void scatter_reduce_blocks(const Smem<C> &s, const TrainLaunch &p, int tid)
+{
+    constexpr int n0 = sc_h(0) * sc_w(0), n1 = sc_h(1) * sc_w(1);  // (row, column) slots
+    static_assert((n0 + n1) % kThreadsTC == 0, "whole slots per thread");
+#pragma unroll 1
+    for (int it = 0; it < (n0 + n1) / kThreadsTC; ++it) {
+        const int k = tid + it * kThreadsTC;
+        const int g = k < n0 ? 0 : 1;
+        const int kk = g ? k - n0 : k;
+        const int x = g ? kk & (sc_w(1) - 1) : kk & (sc_w(0) - 1);
+        const int y = g ? kk >> 4 : kk >> 5;
+        const Window &W = s.win[g];
+        if (x >= W.w || y >= W.h) continue;
+        const float *src = g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * 8 : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * 8;
+        float row[C];
+#pragma unroll
+        for (int q = 0; q < C / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4 *>(src + 4 * q);
+            row[4 * q] = v.x;
+            row[4 * q + 1] = v.y;
+            row[4 * q + 2] = v.z;
+            row[4 * q + 3] = v.w;
+        }
+        flush_row<C, true>(p, g, W.x0 + x, W.y0 + y, row);
     }
 }
 
@@ -733,7 +783,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
         // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
-        if (!BLK && !half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
+        if (!half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
         if (half) {
             uint32_t v[16];
             umma::ld16(Rl, v);
@@ -787,33 +837,6 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 #pragma unroll
                 for (int e = 0; e < C; ++e) dxv[e] = __uint_as_float(half ? v[C + e] : v[e]);
             }
-            if constexpr (BLK) {
-                // block features: every tap adds to its block record (train.cu:436-454)
-                if (valid) {
-                    const float *blocks = reinterpret_cast<const float *>(p.grid[half]);
-                    float *grads = p.ggrid[half];
-                    const short2 b = s.base[half][r];
-                    const int gw = p.gw[half], gh = p.gh[half];
-                    for (int j = 0; j < 4; ++j) {
-                        const int yy = wrap_coord(b.y - 1 + j, gh);
-                        for (int i = 0; i < 4; ++i) {
-                            const int xx = wrap_coord(b.x - 1 + i, gw);
-                            const float wgt = __fmul_rn(s.wts[half][r][4 + j], s.wts[half][r][i]);
-                            float fg[C];
-#pragma unroll
-                            for (int k = 0; k < C; ++k) fg[k] = __fmul_rn(__fmul_rn(wgt, dxv[k]), p.inv_num_samples);
-                            bc6f_backward_texel<C>(blocks, grads, gw, xx, yy, fg);
-                        }
-                    }
-                }
-                first = false;
-                umma::fence_before();
-                if (__syncthreads_or(failed)) {
-                    failed = true;
-                    break;
-                }
-                continue;
-            }
             bool tc_scatter = false;
             if constexpr (C == 8) tc_scatter = s.win[0].tc && s.win[1].tc;
             if (tc_scatter) {
@@ -827,7 +850,10 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     failed = true;
                     break;
                 }
-                scatter_reduce<C>(s, p, tid);
+                if constexpr (BLK)
+                    scatter_reduce_blocks<C>(s, p, tid);
+                else
+                    scatter_reduce<C>(s, p, tid);
                 first = false;
                 umma::fence_before();
                 if (__syncthreads_or(failed)) {
@@ -848,11 +874,11 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             const bool both = s.win[0].ok && s.win[1].ok;
             const int span = max(s.win[0].span, s.win[1].span);
             if (both && span <= 5) {
-                sweep_tc<C, 5>(s, p, tid);
+                sweep_tc<C, 5, BLK>(s, p, tid);
             } else if (both && span <= 10) {
-                sweep_tc<C, 10>(s, p, tid);
+                sweep_tc<C, 10, BLK>(s, p, tid);
             } else if (valid) {
-                scatter_taps_tc<C>(s, p, half, r);
+                scatter_taps_tc<C, BLK>(s, p, half, r);
             }
         }
         first = false;
@@ -966,9 +992,10 @@ static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream)
 {
     const int cout = p.net.cout;
-    if (p.blocks) {  // BC6 block features: generic target gather, one variant per channel count
-        if (channels == 8) return tc::launch_t<8, 0, true>(p, stream);
-        if (channels == 12) return tc::launch_t<12, 0, true>(p, stream);
+    if (p.blocks) {  // BC6 block features
+        if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, true>(p, stream) : tc::launch_t<8, 0, true>(p, stream);
+        if (channels == 12)
+            return cout == 12 ? tc::launch_t<12, 12, true>(p, stream) : tc::launch_t<12, 0, true>(p, stream);
         return cudaErrorInvalidValue;
     }
     if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, false>(p, stream) : tc::launch_t<8, 0, false>(p, stream);

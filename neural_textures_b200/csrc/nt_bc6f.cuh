@@ -70,24 +70,32 @@ __device__ __forceinline__ int64_t bc6f_record(int w, int T, int x, int y, int t
     return (((int64_t)(y >> 2) * (w >> 2) + (x >> 2)) * T + t) * kBc6fFloats;
 }
 
-// The C channels of texel (x, y) (train.cu:240-261 per triple).
+// Channels 3t .. 3t + 2 of texel (x, y) (train.cu:240-261): triple t of a grid with T triples.
+__device__ __forceinline__ void bc6f_texel_triple(const float *__restrict__ blocks, int w, int T, int x, int y, int t,
+                                                  float (&out)[3])
+{
+    const int pix = ((y & 3) << 2) + (x & 3);
+    const float *p = blocks + bc6f_record(w, T, x, y, t);
+    const int part = __float_as_int(__ldg(p + 28)) & 31, mode = __float_as_int(__ldg(p + 29));
+    const int r = (c_bc6f_parts[part] >> pix) & 1;
+    const int bits = bc6f_mode_bits(mode);
+    const float xv = __ldg(p + 12 + pix);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) out[c] = bc6f_channel(__ldg(p + 6 * r + c), __ldg(p + 6 * r + 3 + c), bits, xv).w;
+}
+
+// The C channels of texel (x, y).
 template <int C>
 __device__ __forceinline__ void bc6f_texel(const float *__restrict__ blocks, int w, int x, int y, float (&out)[C])
 {
     constexpr int T = (C + 2) / 3;
-    const int pix = ((y & 3) << 2) + (x & 3);
 #pragma unroll
     for (int t = 0; t < T; ++t) {
-        const float *p = blocks + bc6f_record(w, T, x, y, t);
-        const int part = __float_as_int(__ldg(p + 28)) & 31, mode = __float_as_int(__ldg(p + 29));
-        const int r = (c_bc6f_parts[part] >> pix) & 1;
-        const int bits = bc6f_mode_bits(mode);
-        const float xv = __ldg(p + 12 + pix);
+        float v[3];
+        bc6f_texel_triple(blocks, w, T, x, y, t, v);
 #pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            if (3 * t + c >= C) break;
-            out[3 * t + c] = bc6f_channel(__ldg(p + 6 * r + c), __ldg(p + 6 * r + 3 + c), bits, xv).w;
-        }
+        for (int c = 0; c < 3; ++c)
+            if (3 * t + c < C) out[3 * t + c] = v[c];
     }
 }
 

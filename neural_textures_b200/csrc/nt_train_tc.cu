@@ -662,6 +662,84 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
     return true;
 }
 
+// ---- block-feature gather through a decoded window ----------------------------------------
+//
+// The 128 samples of a tile read about 290 distinct texels of the two grids (config 1) but
+// 4,096 taps.  Each window texel is decoded from its block records once per tile into shared
+// memory (over the H1 / H2 / DY tiles, idle until F1 completes), and the samples gather from
+// there in gather_bc6f's order, so the features are bit-identical to the direct decode.
+
+template <int C>
+__device__ __forceinline__ float *blk_window(Smem<C> &s) { return reinterpret_cast<float *>(s.t.m.H1); }
+
+template <int C>
+__host__ __device__ constexpr int blk_window_floats()
+{
+    return (int)((sizeof(Smem<C>::t.m.H1) + sizeof(Smem<C>::t.m.H2) + sizeof(Smem<C>::t.m.DY)) / sizeof(float));
+}
+
+// Decode the windows of both grids (all threads); false when they do not fit.
+template <int C>
+__device__ __forceinline__ bool blk_decode_windows(Smem<C> &s, const TrainLaunch &p, int tid)
+{
+    constexpr int T = (C + 2) / 3;
+    const Window &W0 = s.win[0], &W1 = s.win[1];
+    const long long n0 = (long long)W0.w * W0.h, n1 = (long long)W1.w * W1.h;
+    if ((n0 + n1) * C > blk_window_floats<C>()) return false;
+    float *buf = blk_window<C>(s);
+    const int items0 = (int)n0 * T, items = items0 + (int)n1 * T;
+    for (int k = tid; k < items; k += kThreadsTC) {
+        const int g = k < items0 ? 0 : 1;
+        const int kk = g ? k - items0 : k;
+        const int n = g ? (int)n1 : (int)n0;
+        const int t = kk / n, idx = kk - t * n;  // consecutive threads: consecutive texels of a row
+        const Window &W = s.win[g];
+        const int ly = idx / W.w, lx = idx - ly * W.w;
+        const int gw = p.gw[g], gh = p.gh[g];
+        float v[3];
+        bc6f_texel_triple(reinterpret_cast<const float *>(p.grid[g]), gw, T, wrap_coord(W.x0 + lx, gw),
+                          wrap_coord(W.y0 + ly, gh), t, v);
+        float *dst = buf + (g ? (int)n0 * C : 0) + idx * C + 3 * t;
+#pragma unroll
+        for (int c = 0; c < 3; ++c)
+            if (3 * t + c < C) dst[c] = v[c];
+    }
+    return true;
+}
+
+// Catmull-Rom gather of sample r from a decoded window (gather_bc6f's fmaf order).
+template <int C>
+__device__ __forceinline__ void blk_gather_window(const Smem<C> &s, const float *win, int g, int r, float (&out)[C])
+{
+    const Window &W = s.win[g];
+    const short2 b = s.base[g][r];
+    const float4 wx4 = *reinterpret_cast<const float4 *>(&s.wts[g][r][0]);
+    const float4 wy4 = *reinterpret_cast<const float4 *>(&s.wts[g][r][4]);
+    const float wx[4] = {wx4.x, wx4.y, wx4.z, wx4.w}, wy[4] = {wy4.x, wy4.y, wy4.z, wy4.w};
+#pragma unroll
+    for (int k = 0; k < C; ++k) out[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float *rp = win + ((b.y - 1 + j - W.y0) * W.w + (b.x - 1 - W.x0)) * C;
+        float row[C];
+#pragma unroll
+        for (int k = 0; k < C; ++k) row[k] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int q = 0; q < C / 4; ++q) {
+                const float4 v = *reinterpret_cast<const float4 *>(rp + i * C + 4 * q);
+                row[4 * q] = fmaf(wx[i], v.x, row[4 * q]);
+                row[4 * q + 1] = fmaf(wx[i], v.y, row[4 * q + 1]);
+                row[4 * q + 2] = fmaf(wx[i], v.z, row[4 * q + 2]);
+                row[4 * q + 3] = fmaf(wx[i], v.w, row[4 * q + 3]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < C; ++k) out[k] = fmaf(wy[j], row[k], out[k]);
+    }
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------
 
 // C: latent channels per grid; TC: target channels when they have a vector gather (4, 8,
@@ -720,16 +798,13 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     Footprint fp;
                     footprint(u, v, p.gw[gi], p.gh[gi], fp);
                     if (valid) shard_rows(p, gi, p.gh[gi], fp);
-                    if (valid) {
+                    if (valid && !BLK) {  // block features gather after the window decode below
                         float f[C];
-                        if constexpr (BLK)
-                            gather_bc6f<C>(reinterpret_cast<const float *>(p.grid[gi]), p.gw[gi], fp, f);
-                        else
-                            gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
+                        gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
 #pragma unroll
                         for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
                     }
-                    if (!p.finalize) {
+                    if (BLK || !p.finalize) {
                         s.base[gi][r] = make_short2((short)fp.bx, (short)fp.by);
                         float4 *wr = reinterpret_cast<float4 *>(s.wts[gi][r]);
                         wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
@@ -737,10 +812,12 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                         extents_partial(s.part[gi], fp.bx, fp.by, valid, warp, lane);
                     }
                 }
+                if constexpr (!BLK) {
 #pragma unroll
-                for (int j = 0; j < K::LC; ++j)
-                    st16(s.t.m.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                         packed[4 * j + 3]);
+                    for (int j = 0; j < K::LC; ++j)
+                        st16(s.t.m.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1],
+                             packed[4 * j + 2], packed[4 * j + 3]);
+                }
             } else {
                 uint32_t packed[4] = {0u, 0u, 0u, 0u};
                 if (valid) {
@@ -763,6 +840,40 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
             }
         }
+        if constexpr (BLK) {
+            __syncthreads();  // footprints and extents
+            if (warp < 2) finalize_window_tc<C>(s, warp, lane);
+            __syncthreads();  // windows
+            const bool windowed = blk_decode_windows<C>(s, p, tid);
+            __syncthreads();  // decoded window texels
+            if (half == 0) {
+                uint32_t packed[K::LC * 4];
+#pragma unroll
+                for (int k = 0; k < K::LC * 4; ++k) packed[k] = 0u;
+                if (valid) {
+#pragma unroll
+                    for (int gi = 0; gi < 2; ++gi) {
+                        float f[C];
+                        if (windowed) {
+                            const float *win = blk_window<C>(s) + (gi ? s.win[0].w * s.win[0].h * C : 0);
+                            blk_gather_window<C>(s, win, gi, r, f);
+                        } else {
+                            float u = 0.f, v = 0.f;
+                            sample_uv(p.sampler, ix, iy, u, v);
+                            Footprint fp;
+                            footprint(u, v, p.gw[gi], p.gh[gi], fp);
+                            gather_bc6f<C>(reinterpret_cast<const float *>(p.grid[gi]), p.gw[gi], fp, f);
+                        }
+#pragma unroll
+                        for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < K::LC; ++j)
+                    st16(s.t.m.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                         packed[4 * j + 3]);
+            }
+        }
         if (!run_stage<C>(0, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // F1
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
@@ -783,7 +894,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
         // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
-        if (!half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);
+        if (!BLK && !half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);  // BLK: in the gather
         if (half) {
             uint32_t v[16];
             umma::ld16(Rl, v);

@@ -522,6 +522,11 @@ def main():
         line["codec"] = codec
     if blocks:
         blocks["adam_hbm_frac"] = blocks["adam_hbm_gbs"] / pk["hbm"]
+        blk_tf = train_flop / (blocks["kernels_ms"]["train_kernel_blocks"] * 1e-3) / 1e12
+        blocks["roofline"] = {"kernel": "nt::tc::train_tc_kernel<8, 8, true> (block features)", "bound": "tensor",
+                              "achieved": blk_tf, "peak": pk["tensor"], "unit": "TFLOP/s", "frac": blk_tf / pk["tensor"],
+                              "traffic": tr.get("train_kernel_blocks", {}).get("bytes_per_launch"),
+                              "algorithmic": f"{MLP_FLOP_TRAIN} FLOP/sample x {B} samples"}
         line["block_features"] = blocks
     if cfg4b:
         line["config4b"] = cfg4b

@@ -335,6 +335,52 @@ def run_blocks(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank)
     return out
 
 
+def run_mips(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank, lod=0.5):
+    """Config-1 material with mip chains (the reference's BCf-0.5k mode, main.cpp:72-77: 512^2
+    with 8 levels, 256^2 with 7; target chain of 8 levels) trained at a fractional mip
+    coordinate: every sample blends two levels of each grid and of the target
+    (train.cu:78-103, :264-314), the gradients go to both levels, Adam runs over the whole
+    chains.  L2 flushed before every timed step."""
+    tex = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                           output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"], num_mips=(8, 7),
+                           target_num_mips=8)
+    tex.init(seed=rank)
+    tex.lod = lod
+    sptr = stream.cuda_stream
+    B = CFG1["lattice"][0] * CFG1["lattice"][1]
+
+    def step_once(step, ev=None):
+        p = tex.params(step=step)
+        if ev:
+            ev[0].record(stream)
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 0, sptr))
+        if ev:
+            ev[1].record(stream)
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), sptr))
+        if ev:
+            ev[2].record(stream)
+
+    for w in range(warmup):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(w + 1)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for k in range(steps):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(warmup + k + 1, events[k])
+    torch.cuda.synchronize(dev)
+    t_train = sum(e[0].elapsed_time(e[1]) for e in events) / steps
+    t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / steps
+    P = sum(c.numel() for c in tex.grid_chains)
+    out = {"workload": "config1_mips_lod0.5_1024sq_8ch", "value": B / ((t_train + t_adam) * 1e-3), "unit": "samples/s",
+           "ms_per_step": t_train + t_adam, "steps": steps, "warmup": warmup, "lod": lod,
+           "chains": "512^2 x 8 levels + 256^2 x 7 levels, fp16 x 8; target 1024^2 x 8 levels",
+           "kernels_ms": {"train_kernel_mips": t_train, "adam_kernel": t_adam},
+           "adam_hbm_gbs": 28 * P / (t_adam * 1e-3) / 1e9, "latent_params": P,
+           "l2": "flushed (256 MB write) before every timed step"}
+    del tex
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -347,6 +393,7 @@ def main():
     ap.add_argument("--decode-iters", type=int, default=200)
     ap.add_argument("--sharded-steps", type=int, default=20, help="timed config-4b sharded steps (0: skip)")
     ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
+    ap.add_argument("--mip-steps", type=int, default=50, help="timed steps at a fractional mip coordinate (0: skip)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -467,10 +514,13 @@ def main():
     blocks = None
     if args.block_steps > 0:
         blocks = run_blocks(torch, dev, stream, L, nt, _native, scratch, args.block_steps, 5, rank)
+    mips = None
+    if args.mip_steps > 0:
+        mips = run_mips(torch, dev, stream, L, nt, _native, scratch, args.mip_steps, 5, rank)
     cfg4b = None
     if args.sharded_steps > 0:
         cfg4b = run_config4b(torch, dist, dev, stream, rank, world, args.sharded_steps, 10)
-    clk = clocks.stop()  # sampled across the timed training, e2e, decode, codec, block-feature and config-4b regions
+    clk = clocks.stop()  # sampled across every timed region above
     texels = CFG0["image"][0] * CFG0["image"][1]
 
     if world > 1:
@@ -528,6 +578,9 @@ def main():
                               "traffic": tr.get("train_kernel_blocks", {}).get("bytes_per_launch"),
                               "algorithmic": f"{MLP_FLOP_TRAIN} FLOP/sample x {B} samples"}
         line["block_features"] = blocks
+    if mips:
+        mips["adam_hbm_frac"] = mips["adam_hbm_gbs"] / pk["hbm"]
+        line["mips"] = mips
     if cfg4b:
         line["config4b"] = cfg4b
     if not args.no_cpu_baseline:

@@ -93,6 +93,7 @@ typedef struct NtFeature {
     float *moment2;
     int32_t width;
     int32_t height;
+    int32_t num_mips;   /* train.h:61; 0 or 1: one level (see NtKernelParams.lod) */
 } NtFeature;
 
 /* train.h:120-157.  Passed by pointer; the library copies what it needs at launch, so the
@@ -168,6 +169,22 @@ typedef struct NtKernelParams {
      * layout, decoded with the reference's float BC6 decode (train.cu:161-261, :436-454).
      * UNCONSTRAINED trains grids, BLOCK_FEATURES trains blocks, FINALIZE samples either. */
     int32_t latent_format;
+
+    /* Mip chains (train.h:61 numMips; level choice train.cu:78-103, blend :264-314).  A grid
+     * with features[f].num_mips = n > 1 stores its n levels one after another in grid,
+     * gradients and moments: level m has max(width >> m, 1) x max(height >> m, 1) texels
+     * (train.cu:214-218), or, for block features, max(w_m >> 2, 1) x max(h_m >> 2, 1) blocks
+     * of records (train.cu:220-231).  Every sample reads its latents and its target at mip
+     * coordinate lod (the reference's uvs.z, 0 in its driver): lod is clamped to [0, n - 1],
+     * m0 = floor(lod), m1 = min(m0 + 1, n - 1), and the value is (1 - t) level m0 + t level
+     * m1 with t = lod - m0 (t = 0: one level).  Gradients reach the levels read, with the same
+     * weights.  The target is a chain of target_num_mips levels of a target_width x
+     * target_height image (0: the image size).  A fractional lod needs the tcgen05 engines and
+     * fp16 grids; sharded calls need lod 0; inference_mse_accum compares with the target level
+     * of an integer lod, which must have the image's size. */
+    float lod;
+    int32_t target_num_mips;
+    int32_t target_width, target_height;
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */
@@ -254,6 +271,17 @@ NT_API nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int3
  * writes [blocks_h*4][blocks_w*4][4] floats.  Synchronous; allocates and frees the array. */
 NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h,
                                          int32_t is_signed, float *rgba);
+
+/* ---- mip chains (no reference counterpart: the reference loads its chains from EXR files,
+ * main.cpp:360-433) ------------------------------------------------------------------------ */
+
+/* Texels of an n-level chain of a width x height image (NtKernelParams.lod). */
+NT_API int64_t nt_mip_chain_texels(int32_t width, int32_t height, int32_t num_mips);
+/* Levels 1 .. num_mips - 1 of an fp16 [texel][channels] chain from its level 0: texel (x, y) of
+ * level m is ((a + b) + (c + d)) / 4 in fp32 over texels (2x, 2y), (2x + 1, 2y), (2x, 2y + 1),
+ * (2x + 1, 2y + 1) of level m - 1 (clamped to its size), rounded to fp16. */
+NT_API nt_status nt_build_mips(void *chain, int32_t width, int32_t height, int32_t channels, int32_t num_mips,
+                               nt_stream_t stream);
 
 /* ---- block records <-> BC6H blocks (no reference counterpart: the reference's
  * BLOCK_FEATURES path, train.cu:316-458, starts from and ends in float records) ----------- */

@@ -37,7 +37,7 @@ class NtAdamConstants(C.Structure):
 
 class NtFeature(C.Structure):
     _fields_ = [("grid", C.c_void_p), ("gradients", C.c_void_p), ("moment1", C.c_void_p),
-                ("moment2", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32)]
+                ("moment2", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32), ("num_mips", C.c_int32)]
 
 
 class NtKernelParams(C.Structure):
@@ -77,6 +77,10 @@ class NtKernelParams(C.Structure):
         ("row_origin", C.c_int32 * 3),
         ("stored_rows", C.c_int32 * 3),
         ("latent_format", C.c_int32),
+        ("lod", C.c_float),
+        ("target_num_mips", C.c_int32),
+        ("target_width", C.c_int32),
+        ("target_height", C.c_int32),
     ]
 
 
@@ -116,6 +120,8 @@ SIGNATURES = {
     "nt_umma_selftest": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
     "nt_read_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
+    "nt_mip_chain_texels": (C.c_int64, [C.c_int32, C.c_int32, C.c_int32]),
+    "nt_build_mips": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
 }
 
 _lib = None

@@ -128,6 +128,11 @@ def bc6h_decode(blocks, out, layout: str = "planar", bias: float = 4.0, stream=N
     return out
 
 
+def mip_chain_texels(width: int, height: int, num_mips: int) -> int:
+    """Texels of a num_mips-level chain (level m: max(w >> m, 1) x max(h >> m, 1))."""
+    return int(load().nt_mip_chain_texels(width, height, num_mips))
+
+
 def bc6f_records_floats(width: int, height: int, channels: int) -> int:
     return int(load().nt_bc6f_records_floats(width, height, channels))
 
@@ -189,19 +194,27 @@ class NeuralTexture:
     def __init__(self, image_w: int, image_h: int, grid_sizes=((512, 512), (256, 256)),
                  latent_channels: int = 8, output_channels: int = 8, device="cuda",
                  lattice=None, latent_lr: float = 1e-2, network_lr: float = 5e-3,
-                 beta1: float = 0.9, beta2: float = 0.99, eps: float = 1e-8):
+                 beta1: float = 0.9, beta2: float = 0.99, eps: float = 1e-8, num_mips=(1, 1),
+                 target_num_mips: int = 1):
         import torch
         self.torch = torch
         self.device = torch.device(device)
         self.image_w, self.image_h = image_w, image_h
         self.C, self.cout = latent_channels, output_channels
         self.grid_sizes = [tuple(g) for g in grid_sizes]
+        self.num_mips = [max(int(n), 1) for n in num_mips]
+        self.target_num_mips = max(int(target_num_mips), 1)
+        self.lod = 0.0  # mip coordinate of every sample (NtKernelParams.lod)
         f16, f32 = torch.float16, torch.float32
         z = lambda shape, dt: torch.zeros(shape, dtype=dt, device=self.device)
-        self.grids = [z((h, w, self.C), f16) for (w, h) in self.grid_sizes]
-        self.ggrads = [z(g.shape, f32) for g in self.grids]
-        self.gm1 = [z(g.shape, f32) for g in self.grids]
-        self.gm2 = [z(g.shape, f32) for g in self.grids]
+        # each grid is a mip chain (level 0 first); grids[g] views level 0 as [h][w][C]
+        self.grid_chains = [z(mip_chain_texels(w, h, n) * self.C, f16)
+                            for (w, h), n in zip(self.grid_sizes, self.num_mips)]
+        self.grids = [c[:w * h * self.C].view(h, w, self.C) for c, (w, h) in zip(self.grid_chains, self.grid_sizes)]
+        shaped = lambda c, g: c.view(g.shape) if c.numel() == g.numel() else c
+        self.ggrads = [shaped(z(c.numel(), f32), g) for c, g in zip(self.grid_chains, self.grids)]
+        self.gm1 = [shaped(z(c.numel(), f32), g) for c, g in zip(self.grid_chains, self.grids)]
+        self.gm2 = [shaped(z(c.numel(), f32), g) for c, g in zip(self.grid_chains, self.grids)]
         self.W = [z(PAD_OUT[l] * PAD_IN[l], f16) for l in range(3)]
         self.b = [z(64, f16), z(64, f16), z(self.cout, f16)]
         self.gW = [z(w.shape, f32) for w in self.W]
@@ -210,7 +223,8 @@ class NeuralTexture:
         self.gb = [z(b.shape, f32) for b in self.b]
         self.mb = [z(b.shape, f32) for b in self.b]
         self.vb = [z(b.shape, f32) for b in self.b]
-        self.target = z((image_h, image_w, self.cout), f16)
+        self.target_chain = z(mip_chain_texels(image_w, image_h, self.target_num_mips) * self.cout, f16)
+        self.target = self.target_chain[:image_w * image_h * self.cout].view(image_h, image_w, self.cout)
         self.loss_accum = z(1, f32)
         if lattice is None:
             lattice = (image_w, image_h)
@@ -250,6 +264,8 @@ class NeuralTexture:
         is encoded as BC6H UF16 blocks of (value + bias) and the blocks become block records
         (nt_bc6f_from_bc6h).  The records decode to value + bias, so the layer-1 bias absorbs
         -bias x W1's latent columns and the network output stays that of the encoded grids."""
+        if max(self.num_mips) > 1:
+            raise ValueError("to_blocks converts single-level grids (num_mips 1)")
         blocks = [bc6h_encode(g, "interleaved", bias, stream=stream) for g in self.grids]
         recs = [bc6f_from_bc6h(b, w, h, self.C, stream=stream) for b, (w, h) in zip(blocks, self.grid_sizes)]
         self._shift_latent_inputs(-bias)
@@ -284,7 +300,7 @@ class NeuralTexture:
              stream=None):
         torch = self.torch
         L = load()
-        for i, g in enumerate(self.grids):
+        for i, g in enumerate(self.grid_chains):  # per-index hash: level 0 does not depend on the chain
             check(L.nt_init_latents(g.data_ptr(), g.numel(), seed * 7919 + i + 1, _stream(stream)))
         Ws = he_normal_weights(seed, self.cout)
         Ws[0] = zero_padded_inputs(Ws[0], 2 * self.C + 8)
@@ -294,9 +310,35 @@ class NeuralTexture:
         ts = seed if target_seed is None else target_seed
         check(L.nt_generate_target(self.target.data_ptr(), self.image_w, self.image_h, self.cout,
                                    ts, int(pbr_normals), _stream(stream)))
+        self.build_target_mips(stream)
         for t in self.ggrads + self.gm1 + self.gm2 + self.gW + self.mW + self.vW + self.gb + self.mb + self.vb:
             t.zero_()
         self.step = 0
+
+    # -- mip chains -----------------------------------------------------------------------------
+    def mip_level(self, g: int, m: int, chain=None):
+        """[h_m][w_m][C] view of level m of grid g's chain (or of a same-layout chain: gradients,
+        moments)."""
+        w, h = self.grid_sizes[g]
+        c = (self.grid_chains[g] if chain is None else chain).reshape(-1)
+        off = mip_chain_texels(w, h, m) if m > 0 else 0
+        lw, lh = max(w >> m, 1), max(h >> m, 1)
+        return c[off * self.C:(off + lw * lh) * self.C].view(lh, lw, self.C)
+
+    def target_level(self, m: int):
+        off = mip_chain_texels(self.image_w, self.image_h, m) if m > 0 else 0
+        lw, lh = max(self.image_w >> m, 1), max(self.image_h >> m, 1)
+        return self.target_chain[off * self.cout:(off + lw * lh) * self.cout].view(lh, lw, self.cout)
+
+    def build_target_mips(self, stream=None):
+        """Levels 1 .. target_num_mips - 1 of the target from level 0 (nt_build_mips)."""
+        check(load().nt_build_mips(self.target_chain.data_ptr(), self.image_w, self.image_h, self.cout,
+                                   self.target_num_mips, _stream(stream)))
+
+    def build_latent_mips(self, stream=None):
+        """Latent levels 1 .. n - 1 from level 0 (box filter), e.g. after training level 0."""
+        for c, (w, h), n in zip(self.grid_chains, self.grid_sizes, self.num_mips):
+            check(load().nt_build_mips(c.data_ptr(), w, h, self.C, n, _stream(stream)))
 
     def load_host(self, grids, W, b, target=None):
         """Upload host fp16 arrays (grids [h][w][C], padded W, b, optional target)."""
@@ -322,6 +364,7 @@ class NeuralTexture:
             f.moment1 = self.gm1[i].data_ptr()
             f.moment2 = self.gm2[i].data_ptr()
             f.width, f.height = self.grid_sizes[i]
+            f.num_mips = self.num_mips[i]
         p.latent_channels, p.output_channels = self.C, self.cout
         for l in range(3):
             p.network_weights[l] = self.W[l].data_ptr()
@@ -352,6 +395,8 @@ class NeuralTexture:
         p.num_samples = self.lattice[0] * self.lattice[1]
         p.step = self.step if step is None else step
         p.latent_format = self.latent_format
+        p.lod = self.lod
+        p.target_num_mips = self.target_num_mips
         p.seed = self.seed
         if loss_accum:
             p.loss_accum = self.loss_accum.data_ptr()

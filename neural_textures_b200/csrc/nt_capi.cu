@@ -2,6 +2,7 @@
 // descriptors, per-step Adam constants and error reporting.  No exception crosses the ABI;
 // every entry point returns an nt_status and records a message for
 // nt_get_last_error_string().
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -56,6 +57,7 @@ cudaError_t hardware_decode(const void *blocks, int bw, int bh, int is_signed, f
 cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t seed, int32_t pbr, cudaStream_t st);
 cudaError_t launch_init_latents(void *grid, int64_t count, uint32_t seed, cudaStream_t st);
 cudaError_t launch_flush(void *scratch, size_t bytes, cudaStream_t st);
+cudaError_t launch_build_mips(__half *chain, int32_t w, int32_t h, int32_t c, int32_t num_mips, cudaStream_t st);
 
 }  // namespace nt
 
@@ -105,6 +107,8 @@ static nt_status validate_network(const NtKernelParams *p)
         NT_REQUIRE(ft.width <= 32767 && ft.height <= 32767, "features[%d] is wider than 32767 texels", f);
         NT_REQUIRE((int64_t)ft.width * ft.height * p->latent_channels < (int64_t)1 << 31,
                    "features[%d] is too large", f);
+        NT_REQUIRE(ft.num_mips >= 0 && ft.num_mips <= 16, "features[%d].num_mips must be in [0, 16] (got %d)", f,
+                   ft.num_mips);
         NT_REQUIRE(p->latent_format == NT_LATENT_GRID_F16 ||
                        (p->latent_format == NT_LATENT_BC6_BLOCKS && ft.width % 4 == 0 && ft.height % 4 == 0),
                    "latent_format %d: features[%d] must be %s", p->latent_format, f,
@@ -112,6 +116,88 @@ static nt_status validate_network(const NtKernelParams *p)
                                                              : "a known latent format");
     }
     return NT_OK;
+}
+
+// ---- mip chains (train.h:61, train.cu:78-103, :214-231, :264-314) --------------------------
+
+static int mip_dim(int size, int m)
+{
+    const int d = m < 31 ? size >> m : 0;
+    return d > 0 ? d : 1;
+}
+
+// Units of level m: texels, or 4x4 blocks of records (train.cu:220-231).
+static int64_t mip_units(int w, int h, int m, bool blocks)
+{
+    const int lw = mip_dim(w, m), lh = mip_dim(h, m);
+    if (!blocks) return (int64_t)lw * lh;
+    return (int64_t)std::max(lw >> 2, 1) * std::max(lh >> 2, 1);
+}
+
+static int64_t mip_offset(int w, int h, int m, bool blocks)
+{
+    int64_t off = 0;
+    for (int k = 0; k < m; ++k) off += mip_units(w, h, k, blocks);
+    return off;
+}
+
+struct MipSel {
+    int m0, m1;
+    float t;  // weight of level m1; 0: level m0 alone
+};
+
+// train.cu:83-87: lod clamped to the chain, levels floor(lod) and the next one.
+static MipSel mip_select(int num_mips, float lod)
+{
+    const int last = num_mips > 1 ? num_mips - 1 : 0;
+    float c = lod > 0.f ? lod : 0.f;  // NaN -> 0
+    if (c > (float)last) c = (float)last;
+    MipSel s;
+    s.m0 = std::min((int)floorf(c), last);
+    s.m1 = std::min(s.m0 + 1, last);
+    s.t = s.m1 > s.m0 ? c - (float)s.m0 : 0.f;
+    return s;
+}
+
+static int feature_mips(const NtFeature &ft) { return ft.num_mips > 1 ? ft.num_mips : 1; }
+
+// Elements (fp16 texel channels, or record floats) per unit of a latent chain.
+static int64_t unit_elems(const NtKernelParams *p)
+{
+    return p->latent_format == NT_LATENT_BC6_BLOCKS ? (int64_t)((p->latent_channels + 2) / 3) * NT_BC6F_RECORD_FLOATS
+                                                     : p->latent_channels;
+}
+
+// Level pointers and sizes of grid f at p->lod (training and decode share them).
+struct LevelView {
+    const void *grid, *grid_b;
+    float *grad, *grad_b;
+    int w, h, w_b, h_b;
+    float t;
+    int m0;
+};
+
+static LevelView feature_levels(const NtKernelParams *p, int f)
+{
+    const NtFeature &ft = p->features[f];
+    const bool blocks = p->latent_format == NT_LATENT_BC6_BLOCKS;
+    const size_t esz = blocks ? sizeof(float) : sizeof(__half);
+    const int64_t per = unit_elems(p);
+    const MipSel ms = mip_select(feature_mips(ft), p->lod);
+    LevelView v;
+    const int64_t oa = mip_offset(ft.width, ft.height, ms.m0, blocks) * per;
+    const int64_t ob = mip_offset(ft.width, ft.height, ms.m1, blocks) * per;
+    v.grid = static_cast<const char *>(ft.grid) + oa * esz;
+    v.grid_b = static_cast<const char *>(ft.grid) + ob * esz;
+    v.grad = ft.gradients ? ft.gradients + oa : nullptr;
+    v.grad_b = ft.gradients ? ft.gradients + ob : nullptr;
+    v.w = mip_dim(ft.width, ms.m0);
+    v.h = mip_dim(ft.height, ms.m0);
+    v.w_b = mip_dim(ft.width, ms.m1);
+    v.h_b = mip_dim(ft.height, ms.m1);
+    v.t = ms.t;
+    v.m0 = ms.m0;
+    return v;
 }
 
 static NetView net_view(const NtKernelParams *p)
@@ -181,16 +267,16 @@ static nt_status add_feature_segments(const NtKernelParams *p, AdamLaunch &a)
         const NtFeature &ft = p->features[f];
         NT_REQUIRE(ft.gradients && ft.moment1 && ft.moment2,
                    "features[%d] gradient / moment buffers are required", f);
-        if (p->latent_format == NT_LATENT_BC6_BLOCKS) {
+        // every level of the chain (train.cu:990-1026 runs Adam over all mips)
+        const bool blocks = p->latent_format == NT_LATENT_BC6_BLOCKS;
+        const int64_t n = mip_offset(ft.width, ft.height, feature_mips(ft), blocks) * unit_elems(p);
+        if (blocks) {
             // fp32 block records; partition / mode slots keep a zero gradient and are skipped
-            const int64_t n = (int64_t)(ft.width / 4) * (ft.height / 4) * ((p->latent_channels + 2) / 3) * NT_BC6F_RECORD_FLOATS;
             AdamSegment sg = make_segment(nullptr, ft.gradients, ft.moment1, ft.moment2, n, p->feature_adam, p->step);
             sg.w32 = reinterpret_cast<float *>(ft.grid);
             a.seg[a.nseg++] = sg;
         } else {
-            a.seg[a.nseg++] = make_segment(ft.grid, ft.gradients, ft.moment1, ft.moment2,
-                                           (int64_t)ft.width * ft.height * p->latent_channels, p->feature_adam,
-                                           p->step);
+            a.seg[a.nseg++] = make_segment(ft.grid, ft.gradients, ft.moment1, ft.moment2, n, p->feature_adam, p->step);
         }
     }
     return NT_OK;
@@ -244,6 +330,10 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(row_origin)
     NT_FIELD(stored_rows)
     NT_FIELD(latent_format)
+    NT_FIELD(lod)
+    NT_FIELD(target_num_mips)
+    NT_FIELD(target_width)
+    NT_FIELD(target_height)
 #undef NT_FIELD
     return (size_t)-1;
 }
@@ -275,18 +365,48 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
 
     TrainLaunch L;
     memset(&L, 0, sizeof L);
+    bool fractional = false;
     for (int f = 0; f < 2; ++f) {
-        L.grid[f] = reinterpret_cast<const __half *>(p->features[f].grid);
-        L.ggrid[f] = p->features[f].gradients;
-        L.gw[f] = p->features[f].width;
-        L.gh[f] = p->features[f].height;
+        const LevelView v = feature_levels(p, f);
+        L.grid[f] = reinterpret_cast<const __half *>(v.grid);
+        L.ggrid[f] = v.grad;
+        L.gw[f] = v.w;
+        L.gh[f] = v.h;
+        NT_REQUIRE(p->latent_format != NT_LATENT_BC6_BLOCKS || (v.w % 4 == 0 && v.h % 4 == 0 && v.t == 0.f),
+                   "block features sample one mip level whose size is a multiple of 4 (features[%d], lod %g)", f,
+                   (double)p->lod);
+        if (v.t > 0.f) {
+            L.grid_b[f] = reinterpret_cast<const __half *>(v.grid_b);
+            L.ggrid_b[f] = v.grad_b;
+            L.gw_b[f] = v.w_b;
+            L.gh_b[f] = v.h_b;
+            L.mip_t[f] = v.t;
+            fractional = true;
+        }
     }
     L.net = net_view(p);
     for (int l = 0; l < 3; ++l) {
         L.gW[l] = p->network_weight_gradients[l];
         L.gb[l] = p->network_bias_gradients[l];
     }
-    L.target = reinterpret_cast<const __half *>(p->target);
+    {  // target chain at the same lod
+        NT_REQUIRE(p->target_num_mips >= 0 && p->target_num_mips <= 16 && p->target_width >= 0 && p->target_height >= 0,
+                   "target_num_mips must be in [0, 16] and the target size non-negative");
+        const int tw = p->target_width ? p->target_width : p->image_width;
+        const int th = p->target_height ? p->target_height : p->image_height;
+        const MipSel ts = mip_select(p->target_num_mips, p->lod);
+        const __half *t0 = reinterpret_cast<const __half *>(p->target);
+        L.target = t0 + mip_offset(tw, th, ts.m0, false) * p->output_channels;
+        L.tw = mip_dim(tw, ts.m0);
+        L.th = mip_dim(th, ts.m0);
+        if (ts.t > 0.f) {
+            L.target_b = t0 + mip_offset(tw, th, ts.m1, false) * p->output_channels;
+            L.tw_b = mip_dim(tw, ts.m1);
+            L.th_b = mip_dim(th, ts.m1);
+            L.target_t = ts.t;
+            fractional = true;
+        }
+    }
     for (int c = 0; c < 16; ++c) L.cw[c] = c < p->output_channels ? p->channel_loss_weights[c] : 0.f;
     L.sampler.image_w = p->image_width;
     L.sampler.image_h = p->image_height;
@@ -310,7 +430,7 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
     L.lat_rows = p->lattice_rows ? p->lattice_rows : p->lattice_height - p->lattice_row0;
     bool sharded = p->lattice_row0 != 0 || L.lat_rows != p->lattice_height;
     for (int s = 0; s < 3; ++s) {
-        const int h = s < 2 ? p->features[s].height : p->image_height;
+        const int h = s < 2 ? L.gh[s] : L.th;
         NT_REQUIRE(p->stored_rows[s] >= 0 && p->stored_rows[s] <= h && p->row_origin[s] >= 0 && p->row_origin[s] < h,
                    "source %d: stored rows %d from row %d do not fit its %d rows", s, p->stored_rows[s],
                    p->row_origin[s], h);
@@ -319,6 +439,9 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
         sharded = sharded || L.rows[s] != h;
     }
     NT_REQUIRE(!sharded || train_engine() == 1, "row sharding needs the tcgen05 training engine (NT_TRAIN_ENGINE=mma is set)");
+    NT_REQUIRE(!sharded || (p->lod == 0.f && L.th == p->image_height),
+               "row sharding needs lod 0 and a target of the image's height");
+    NT_REQUIRE(!fractional || train_engine() == 1, "a fractional lod needs the tcgen05 training engine");
     // latent representation: UNCONSTRAINED trains fp16 grids, BLOCK_FEATURES trains BC6 block
     // features (train.cu:902-913), FINALIZE samples either and trains the network only
     NT_REQUIRE(type != NT_TRAIN_UNCONSTRAINED || p->latent_format == NT_LATENT_GRID_F16,
@@ -392,15 +515,33 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     NT_REQUIRE(!p->inference_mse_accum || p->target, "inference_mse_accum requires a target");
     DecodeLaunch L;
     memset(&L, 0, sizeof L);
+    bool fractional = false;
     for (int f = 0; f < 2; ++f) {
-        L.grid[f] = reinterpret_cast<const __half *>(p->features[f].grid);
-        L.gw[f] = p->features[f].width;
-        L.gh[f] = p->features[f].height;
+        const LevelView v = feature_levels(p, f);
+        L.grid[f] = reinterpret_cast<const __half *>(v.grid);
+        L.gw[f] = v.w;
+        L.gh[f] = v.h;
+        if (v.t > 0.f) {
+            L.grid_b[f] = reinterpret_cast<const __half *>(v.grid_b);
+            L.gw_b[f] = v.w_b;
+            L.gh_b[f] = v.h_b;
+            L.mip_t[f] = v.t;
+            fractional = true;
+        }
     }
+    NT_REQUIRE(!fractional || decode_engine() == 1, "a fractional lod needs the tcgen05 decode engine");
     L.net = net_view(p);
     L.out = p->inference_output;
     L.out_f32 = p->inference_output_dtype == NT_DTYPE_F32;
     L.target = reinterpret_cast<const __half *>(p->target);
+    if (p->inference_mse_accum) {  // the target level of this lod, texel for texel
+        const int tw = p->target_width ? p->target_width : p->image_width;
+        const int th = p->target_height ? p->target_height : p->image_height;
+        const MipSel ts = mip_select(p->target_num_mips, p->lod);
+        NT_REQUIRE(ts.t == 0.f && mip_dim(tw, ts.m0) == p->image_width && mip_dim(th, ts.m0) == p->image_height,
+                   "inference_mse_accum needs an integer lod whose target level has the image's size");
+        L.target += mip_offset(tw, th, ts.m0, false) * p->output_channels;
+    }
     L.mse_accum = p->inference_mse_accum;
     L.image_w = p->image_width;
     L.image_h = p->image_height;
@@ -518,6 +659,24 @@ nt_status nt_init_latents(void *grid, int64_t count, uint32_t seed, nt_stream_t 
     NT_REQUIRE(count >= 0, "count must be non-negative");
     if (count == 0) return NT_OK;
     return check_cuda(launch_init_latents(grid, count, seed, (cudaStream_t)stream), "latent init");
+}
+
+int64_t nt_mip_chain_texels(int32_t width, int32_t height, int32_t num_mips)
+{
+    if (width < 1 || height < 1 || num_mips < 0 || num_mips > 16) return 0;
+    return mip_offset(width, height, num_mips > 1 ? num_mips : 1, false);
+}
+
+nt_status nt_build_mips(void *chain, int32_t width, int32_t height, int32_t channels, int32_t num_mips,
+                        nt_stream_t stream)
+{
+    NT_REQUIRE(chain && (reinterpret_cast<uintptr_t>(chain) & 1u) == 0, "chain must be a 2-byte aligned device pointer");
+    NT_REQUIRE(width >= 1 && height >= 1 && channels >= 1, "chain size must be positive");
+    NT_REQUIRE(num_mips >= 0 && num_mips <= 16, "num_mips must be in [0, 16]");
+    if (num_mips <= 1) return NT_OK;
+    return check_cuda(launch_build_mips(reinterpret_cast<__half *>(chain), width, height, channels, num_mips,
+                                        (cudaStream_t)stream),
+                      "mip chain build");
 }
 
 nt_status nt_flush_l2(void *scratch, size_t bytes, nt_stream_t stream)

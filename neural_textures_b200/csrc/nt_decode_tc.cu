@@ -178,7 +178,8 @@ __device__ __forceinline__ bool dec_stage(int stage, const DecSmem<C> &s, uint32
     return true;
 }
 
-template <int C>
+// MIP: a fractional mip coordinate; grid g also reads a second level with weight mip_t[g].
+template <int C, bool MIP>
 __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const DecodeLaunch p)
 {
     using K = Cfg<C>;
@@ -249,6 +250,18 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
                         Footprint fp;
                         footprint(u, v, p.gw[g], p.gh[g], fp);
                         gather_cr<C>(p.grid[g], p.gw[g], fp, f);
+                    }
+                    if constexpr (MIP) {
+                        const float t = p.mip_t[g];
+                        if (t > 0.f) {  // second mip level: (1 - t) level m0 + t level m1
+                            Footprint fb;
+                            footprint(u, v, p.gw_b[g], p.gh_b[g], fb);
+                            float fl[C];
+                            gather_cr<C>(p.grid_b[g], p.gw_b[g], fb, fl);
+                            const float omt = __fsub_rn(1.f, t);
+#pragma unroll
+                            for (int k = 0; k < C; ++k) f[k] = __fadd_rn(__fmul_rn(omt, f[k]), __fmul_rn(t, fl[k]));
+                        }
                     }
                 }
 #pragma unroll
@@ -344,18 +357,18 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
     }
 }
 
-template <int C>
+template <int C, bool MIP>
 static cudaError_t launch_dec_t(DecodeLaunch p, cudaStream_t stream)
 {
     const size_t smem = sizeof(DecSmem<C>);
-    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(decode_tc_kernel<C>), smem);
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(decode_tc_kernel<C, MIP>), smem);
     if (e != cudaSuccess) return e;
     p.tiles_x = (p.image_w + kTileW - 1) / kTileW;
     p.tiles_y = (p.image_h + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = kDecCtas * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;
-    decode_tc_kernel<C><<<grid, kDecThreads, smem, stream>>>(p);
+    decode_tc_kernel<C, MIP><<<grid, kDecThreads, smem, stream>>>(p);
     count_launch();
     return cudaGetLastError();
 }
@@ -364,8 +377,9 @@ static cudaError_t launch_dec_t(DecodeLaunch p, cudaStream_t stream)
 
 cudaError_t launch_decode_tc(const DecodeLaunch &p, int channels, cudaStream_t stream)
 {
-    if (channels == 8) return tc::launch_dec_t<8>(p, stream);
-    if (channels == 12) return tc::launch_dec_t<12>(p, stream);
+    const bool mip = p.mip_t[0] > 0.f || p.mip_t[1] > 0.f;
+    if (channels == 8) return mip ? tc::launch_dec_t<8, true>(p, stream) : tc::launch_dec_t<8, false>(p, stream);
+    if (channels == 12) return mip ? tc::launch_dec_t<12, true>(p, stream) : tc::launch_dec_t<12, false>(p, stream);
     return cudaErrorInvalidValue;
 }
 

@@ -38,6 +38,17 @@ struct TrainLaunch {
     int32_t lat_row0, lat_rows;
     int32_t org[3], rows[3];
     int32_t blocks;  // 1: grid / ggrid hold BC6 block-feature records (float), not fp16 texels
+    // Mip chains.  grid / ggrid / gw / gh above are the level m0 that every sample reads; with
+    // mip_t[g] > 0 grid g also reads level m1 (grid_b ...): feature (1 - t) a + t b.  The target
+    // level m0 is tw x th texels; target_t > 0 adds level m1.
+    const __half *grid_b[2];
+    float *ggrid_b[2];
+    int32_t gw_b[2], gh_b[2];
+    float mip_t[2];
+    int32_t tw, th;
+    const __half *target_b;
+    int32_t tw_b, th_b;
+    float target_t;
 };
 
 struct DecodeLaunch {
@@ -50,6 +61,10 @@ struct DecodeLaunch {
     float *mse_accum;      // optional
     int32_t image_w, image_h;
     int32_t tiles_x, tiles_y;
+    // second mip level of grid g when mip_t[g] > 0 (TrainLaunch)
+    const __half *grid_b[2];
+    int32_t gw_b[2], gh_b[2];
+    float mip_t[2];
 };
 
 constexpr int kMaxAdamSegments = 8;

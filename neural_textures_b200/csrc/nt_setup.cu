@@ -5,6 +5,7 @@
 // target generator follows the integer parameter derivation of the CPU oracle exactly
 // (same hash, integer frequencies, integer phase reduction); only the final sine /
 // exponential differ in rounding, below fp16 resolution in almost every texel.
+#include <algorithm>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -106,6 +107,45 @@ __global__ void flush_kernel(uint4 *p, int64_t n16, uint32_t val)
 {
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x)
         p[i] = make_uint4(val, val, val, val);
+}
+
+// One level of a mip chain from the level below: 2x2 box average in fp32 ((a + b) + (c + d)) / 4,
+// source texels clamped to the level below (odd sizes drop the last row / column), rounded to
+// fp16.  One thread per (texel, channel).
+__global__ void build_mip_kernel(const __half *__restrict__ src, int sw, int sh, __half *__restrict__ dst, int dw,
+                                 int dh, int c)
+{
+    const int64_t n = (int64_t)dw * dh * c;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int k = (int)(i % c);
+        const int64_t texel = i / c;
+        const int x = (int)(texel % dw), y = (int)(texel / dw);
+        const int x0 = min(2 * x, sw - 1), x1 = min(2 * x + 1, sw - 1);
+        const int y0 = min(2 * y, sh - 1), y1 = min(2 * y + 1, sh - 1);
+        const float a = __half2float(src[((int64_t)y0 * sw + x0) * c + k]);
+        const float b = __half2float(src[((int64_t)y0 * sw + x1) * c + k]);
+        const float d = __half2float(src[((int64_t)y1 * sw + x0) * c + k]);
+        const float e = __half2float(src[((int64_t)y1 * sw + x1) * c + k]);
+        dst[i] = __float2half_rn(__fmul_rn(__fadd_rn(__fadd_rn(a, b), __fadd_rn(d, e)), 0.25f));
+    }
+}
+
+cudaError_t launch_build_mips(__half *chain, int32_t w, int32_t h, int32_t c, int32_t num_mips, cudaStream_t st)
+{
+    int64_t off = 0;
+    for (int m = 1; m < num_mips; ++m) {
+        const int sw = max(w >> (m - 1), 1), sh = max(h >> (m - 1), 1);
+        const int dw = max(w >> m, 1), dh = max(h >> m, 1);
+        __half *src = chain + off * c;
+        off += (int64_t)sw * sh;
+        const int64_t n = (int64_t)dw * dh * c;
+        const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4 * sm_count());
+        build_mip_kernel<<<blocks, 256, 0, st>>>(src, sw, sh, chain + off * c, dw, dh, c);
+        count_launch();
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t seed, int32_t pbr,

@@ -480,8 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1) train_kernel(const TrainLaunch p)
 #pragma unroll
                 for (int k = 0; k < 4; ++k) packed[C + k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
                 Footprint fp;
-                footprint(u, v, p.sampler.image_w, p.sampler.image_h, fp);
-                gather_target(p.target, p.sampler.image_w, p.net.cout, fp, tgt);
+                footprint(u, v, p.tw, p.th, fp);
+                gather_target(p.target, p.tw, p.net.cout, fp, tgt);
             }
             uint4 *xr = reinterpret_cast<uint4 *>(s.X + tid * kStrideK32);
 #pragma unroll

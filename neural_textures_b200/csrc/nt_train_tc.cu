@@ -744,8 +744,11 @@ __device__ __forceinline__ void blk_gather_window(const Smem<C> &s, const float 
 
 // C: latent channels per grid; TC: target channels when they have a vector gather (4, 8,
 // 12 or 16), 0 for the generic per-channel gather; BLK: the latents are BC6 block features
-// (nt_bc6f.cuh: float records sampled through the BC6 decode, gradients into the records).
-template <int C, int TC, bool BLK>
+// (nt_bc6f.cuh: float records sampled through the BC6 decode, gradients into the records);
+// MIP: a fractional mip coordinate, so a grid or the target also reads a second level
+// (weight mip_t / target_t): features and target blend the two, the first level's gradient
+// takes the usual scatter at weight 1 - t and the second level per-tap atomics at weight t.
+template <int C, int TC, bool BLK, bool MIP>
 __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaunch p)
 {
     using K = Cfg<C>;
@@ -801,6 +804,18 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     if (valid && !BLK) {  // block features gather after the window decode below
                         float f[C];
                         gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
+                        if constexpr (MIP) {
+                            const float t = p.mip_t[gi];
+                            if (t > 0.f) {  // (1 - t) level m0 + t level m1 (train.cu:303-304)
+                                Footprint fb;
+                                footprint(u, v, p.gw_b[gi], p.gh_b[gi], fb);
+                                float fl[C];
+                                gather_cr<C>(p.grid_b[gi], p.gw_b[gi], fb, fl);
+                                const float omt = __fsub_rn(1.f, t);
+#pragma unroll
+                                for (int k = 0; k < C; ++k) f[k] = __fadd_rn(__fmul_rn(omt, f[k]), __fmul_rn(t, fl[k]));
+                            }
+                        }
 #pragma unroll
                         for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
                     }
@@ -826,12 +841,29 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 #pragma unroll
                     for (int k = 0; k < 4; ++k) packed[k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
                     Footprint fp;
-                    footprint(u, v, p.sampler.image_w, p.sampler.image_h, fp);
-                    shard_rows(p, 2, p.sampler.image_h, fp);
+                    footprint(u, v, p.tw, p.th, fp);
+                    shard_rows(p, 2, p.th, fp);
                     if constexpr (TC > 0)
-                        gather_cr<TC>(p.target, p.sampler.image_w, fp, tgt);
+                        gather_cr<TC>(p.target, p.tw, fp, tgt);
                     else
-                        gather_cr_any(p.target, p.sampler.image_w, cout, fp, tgt);
+                        gather_cr_any(p.target, p.tw, cout, fp, tgt);
+                    if constexpr (MIP) {
+                        const float t = p.target_t;
+                        if (t > 0.f) {  // train.cu:102: sample0 (1 - t) + sample1 t
+                            float tb[16];
+                            footprint(u, v, p.tw_b, p.th_b, fp);
+                            if constexpr (TC > 0) {
+#pragma unroll
+                                for (int k = TC; k < 16; ++k) tb[k] = 0.f;
+                                gather_cr<TC>(p.target_b, p.tw_b, fp, tb);
+                            } else {
+                                gather_cr_any(p.target_b, p.tw_b, cout, fp, tb);
+                            }
+                            const float omt = __fsub_rn(1.f, t);
+#pragma unroll
+                            for (int k = 0; k < 16; ++k) tgt[k] = __fadd_rn(__fmul_rn(omt, tgt[k]), __fmul_rn(t, tb[k]));
+                        }
+                    }
                 }
                 static_assert(K::XC == K::LC + 2 || K::XC == K::LC + 3, "X row: latents, posenc, 1, [0]");
                 st16(s.t.m.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
@@ -947,6 +979,34 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 umma::wait_ld();
 #pragma unroll
                 for (int e = 0; e < C; ++e) dxv[e] = __uint_as_float(half ? v[C + e] : v[e]);
+            }
+            if constexpr (MIP) {
+                const float t = p.mip_t[half];
+                if (t > 0.f) {
+                    if (valid) {  // level m1 of grid `half`: per-tap atomics at weight t
+                        float u = 0.f, v = 0.f;
+                        sample_uv(p.sampler, ix, iy, u, v);
+                        Footprint fb;
+                        footprint(u, v, p.gw_b[half], p.gh_b[half], fb);
+                        float db[C];
+#pragma unroll
+                        for (int k = 0; k < C; ++k) db[k] = __fmul_rn(dxv[k], t);
+                        for (int j = 0; j < 4; ++j) {
+                            for (int i = 0; i < 4; ++i) {
+                                const float wgt = fb.wx[i] * fb.wy[j] * p.inv_num_samples;
+                                float4 *dst = reinterpret_cast<float4 *>(
+                                    p.ggrid_b[half] + ((size_t)fb.ys[j] * p.gw_b[half] + fb.xs[i]) * C);
+#pragma unroll
+                                for (int q = 0; q < C / 4; ++q)
+                                    atomicAdd(dst + q, make_float4(wgt * db[4 * q], wgt * db[4 * q + 1],
+                                                                   wgt * db[4 * q + 2], wgt * db[4 * q + 3]));
+                            }
+                        }
+                    }
+                    const float omt = __fsub_rn(1.f, t);  // level m0 takes the usual scatter
+#pragma unroll
+                    for (int k = 0; k < C; ++k) dxv[k] = __fmul_rn(dxv[k], omt);
+                }
             }
             bool tc_scatter = false;
             if constexpr (C == 8) tc_scatter = s.win[0].tc && s.win[1].tc;
@@ -1081,19 +1141,19 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     }
 }
 
-template <int C, int TC, bool BLK>
+template <int C, int TC, bool BLK, bool MIP = false>
 static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 {
     const size_t smem = sizeof(Smem<C>);
     static_assert(sizeof(Smem<C>) <= 113 * 1024, "two CTAs per SM");
-    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK>), smem);
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK, MIP>), smem);
     if (e != cudaSuccess) return e;
     p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
     p.tiles_y = (p.lat_rows + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = 2 * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;
-    train_tc_kernel<C, TC, BLK><<<grid, kThreadsTC, smem, stream>>>(p);
+    train_tc_kernel<C, TC, BLK, MIP><<<grid, kThreadsTC, smem, stream>>>(p);
     count_launch();
     return cudaGetLastError();
 }
@@ -1107,6 +1167,14 @@ cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t str
         if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, true>(p, stream) : tc::launch_t<8, 0, true>(p, stream);
         if (channels == 12)
             return cout == 12 ? tc::launch_t<12, 12, true>(p, stream) : tc::launch_t<12, 0, true>(p, stream);
+        return cudaErrorInvalidValue;
+    }
+    if (p.mip_t[0] > 0.f || p.mip_t[1] > 0.f || p.target_t > 0.f) {  // two mip levels
+        if (channels == 8)
+            return cout == 8 ? tc::launch_t<8, 8, false, true>(p, stream) : tc::launch_t<8, 0, false, true>(p, stream);
+        if (channels == 12)
+            return cout == 12 ? tc::launch_t<12, 12, false, true>(p, stream)
+                              : tc::launch_t<12, 0, false, true>(p, stream);
         return cudaErrorInvalidValue;
     }
     if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, false>(p, stream) : tc::launch_t<8, 0, false>(p, stream);

@@ -381,6 +381,12 @@ static void layer(const float *x, int n_in, int pad_in, const uint16_t *W, const
  * positional features, 32 -> 64 ReLU -> 64 ReLU -> cout.  Hidden activations are rounded
  * to fp16 (they are tensor-core operands); the output is rounded to fp16 like the
  * reference's half output vector (train.cu:878, mlp.h:65-99). */
+/* Two-level blend of a mip chain (train.cu:102, :303-304): (1 - t) a + t b. */
+static float mip_blend(float a, float b, float t)
+{
+    return (1.f - t) * a + t * b;
+}
+
 void nto_forward_sample(const nto_model *m, float u, float v, nto_fwd *f)
 {
     const int C = m->channels;
@@ -392,6 +398,12 @@ void nto_forward_sample(const nto_model *m, float u, float v, nto_fwd *f)
         else
             nto_sample_grid(m->grid[g], m->gw[g], m->gh[g], C, u, v, feat, f->base[g], f->wx[g],
                             f->wy[g]);
+        if (m->grid_b[g] && m->mip_t[g] > 0.f) {
+            float fb[16];
+            nto_sample_grid(m->grid_b[g], m->gw_b[g], m->gh_b[g], C, u, v, fb, f->base_b[g], f->wx_b[g],
+                            f->wy_b[g]);
+            for (int k = 0; k < C; ++k) feat[k] = mip_blend(feat[k], fb[k], m->mip_t[g]);
+        }
         for (int k = 0; k < C; ++k) f->x[g * C + k] = r16(feat[k]);
     }
     float pe[8];
@@ -520,12 +532,44 @@ static double backward_sample(const nto_model *m, const nto_fwd *f, const float 
 
 /* train.cu:460-509 (BackwardUnconstrainedFeaturePass) with the Catmull-Rom footprint:
  * grad[texel] += wy * wx * dL/dfeature for the 16 taps of each grid. */
+static void scatter_taps(float *grad, int32_t w, int32_t h, int C, const int32_t base[2], const float wx[4],
+                         const float wy[4], const float *dx, float scale)
+{
+    for (int j = 0; j < 4; ++j) {
+        const int32_t yy = nto_wrap(base[1] - 1 + j, h);
+        for (int i = 0; i < 4; ++i) {
+            const int32_t xx = nto_wrap(base[0] - 1 + i, w);
+            const float wgt = wy[j] * wx[i];
+            float *dst = grad + ((int64_t)yy * w + xx) * C;
+            for (int k = 0; k < C; ++k) {
+                const float val = wgt * dx[k] * scale;
+#ifdef _OPENMP
+#pragma omp atomic
+#endif
+                dst[k] += val;
+            }
+        }
+    }
+}
+
 static void scatter_latent(const nto_model *m, const nto_fwd *f, const float *dx, float scale,
-                           float *ggrid[2])
+                           float *ggrid[2], float *const ggrid_b[2])
 {
     const int C = m->channels;
     for (int g = 0; g < 2; ++g) {
         if (!ggrid[g]) continue;
+        if (!m->blocks[g] && m->grid_b[g] && m->mip_t[g] > 0.f) { /* two mip levels: (1 - t) and t */
+            const float t = m->mip_t[g];
+            float da[16], db[16];
+            for (int k = 0; k < C; ++k) {
+                da[k] = dx[g * C + k] * (1.f - t);
+                db[k] = dx[g * C + k] * t;
+            }
+            scatter_taps(ggrid[g], m->gw[g], m->gh[g], C, f->base[g], f->wx[g], f->wy[g], da, scale);
+            if (ggrid_b && ggrid_b[g])
+                scatter_taps(ggrid_b[g], m->gw_b[g], m->gh_b[g], C, f->base_b[g], f->wx_b[g], f->wy_b[g], db, scale);
+            continue;
+        }
         if (m->blocks[g]) { /* train.cu:436-454 per tap of the Catmull-Rom footprint */
             for (int j = 0; j < 4; ++j) {
                 const int32_t yy = nto_wrap(f->base[g][1] - 1 + j, m->gh[g]);
@@ -590,10 +634,17 @@ double nto_train_pass_range(const nto_model *m, const nto_train_args *a, int64_t
             nto_fwd f;
             nto_forward_sample(m, u, v, &f);
             float t[16] = {0};
-            sample_target(a->target, s->image_w, s->image_h, m->cout, u, v, t);
+            const int32_t tw = a->target_w > 0 ? a->target_w : s->image_w;
+            const int32_t th = a->target_h > 0 ? a->target_h : s->image_h;
+            sample_target(a->target, tw, th, m->cout, u, v, t);
+            if (a->target_b && a->target_t > 0.f) {
+                float tb[16] = {0};
+                sample_target(a->target_b, a->target_w_b, a->target_h_b, m->cout, u, v, tb);
+                for (int c = 0; c < m->cout; ++c) t[c] = mip_blend(t[c], tb[c], a->target_t);
+            }
             float dx[32];
             sse_total += backward_sample(m, &f, t, a->channel_weights, acc, dx);
-            scatter_latent(m, &f, dx, scale, gg);
+            scatter_latent(m, &f, dx, scale, gg, a->finalize ? NULL : a->ggrid_b);
         }
     }
     for (int l = 0; l < 3; ++l) {
@@ -619,6 +670,60 @@ double nto_train_pass(const nto_model *m, const nto_train_args *a, float *gW[3],
 {
     const int64_t total = (int64_t)a->sampler.lattice_w * a->sampler.lattice_h;
     return nto_train_pass_range(m, a, 0, total, gW, gb, ggrid, threads);
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Mip chains                                                                            */
+/* ------------------------------------------------------------------------------------ */
+
+int32_t nto_mip_dim(int32_t size, int32_t m) /* train.cu:214-218 */
+{
+    const int32_t d = size >> m;
+    return d > 0 ? d : 1;
+}
+
+int64_t nto_mip_offset(int32_t w, int32_t h, int32_t m)
+{
+    int64_t off = 0;
+    for (int32_t k = 0; k < m; ++k) off += (int64_t)nto_mip_dim(w, k) * nto_mip_dim(h, k);
+    return off;
+}
+
+/* train.cu:83-87 (SampleReferenceTextureTrilinear); the feature sampler of train.cu:266-282
+ * picks the same levels and weights for every lod in [0, n - 1]. */
+void nto_mip_select(int32_t num_mips, float lod, int32_t *m0, int32_t *m1, float *t)
+{
+    const int32_t last = num_mips > 1 ? num_mips - 1 : 0;
+    float c = lod > 0.f ? lod : 0.f; /* NaN -> 0 */
+    if (c > (float)last) c = (float)last;
+    int32_t a = (int32_t)floorf(c);
+    if (a > last) a = last;
+    const int32_t b = a + 1 < last ? a + 1 : last;
+    *m0 = a;
+    *m1 = b;
+    *t = b > a ? c - (float)a : 0.f;
+}
+
+void nto_build_mips(uint16_t *chain, int32_t w, int32_t h, int32_t c, int32_t num_mips)
+{
+    for (int32_t m = 1; m < num_mips; ++m) {
+        const int32_t sw = nto_mip_dim(w, m - 1), sh = nto_mip_dim(h, m - 1);
+        const int32_t dw = nto_mip_dim(w, m), dh = nto_mip_dim(h, m);
+        const uint16_t *src = chain + nto_mip_offset(w, h, m - 1) * c;
+        uint16_t *dst = chain + nto_mip_offset(w, h, m) * c;
+        for (int32_t y = 0; y < dh; ++y)
+            for (int32_t x = 0; x < dw; ++x) {
+                const int32_t x0 = 2 * x < sw ? 2 * x : sw - 1, x1 = 2 * x + 1 < sw ? 2 * x + 1 : sw - 1;
+                const int32_t y0 = 2 * y < sh ? 2 * y : sh - 1, y1 = 2 * y + 1 < sh ? 2 * y + 1 : sh - 1;
+                for (int32_t k = 0; k < c; ++k) {
+                    const float a = nto_h2f(src[((int64_t)y0 * sw + x0) * c + k]);
+                    const float b = nto_h2f(src[((int64_t)y0 * sw + x1) * c + k]);
+                    const float d = nto_h2f(src[((int64_t)y1 * sw + x0) * c + k]);
+                    const float e = nto_h2f(src[((int64_t)y1 * sw + x1) * c + k]);
+                    dst[((int64_t)y * dw + x) * c + k] = nto_f2h(((a + b) + (d + e)) * 0.25f);
+                }
+            }
+    }
 }
 
 /* ------------------------------------------------------------------------------------ */

@@ -71,6 +71,11 @@ typedef struct nto_model {
     const float *blocks[2]; /* block-feature form of grid g (NULL: the fp16 grid) */
     const uint16_t *W[3];   /* padded column-major fp16: [64][32], [64][64], [16][64] */
     const uint16_t *b[3];   /* fp16: 64, 64, cout */
+    /* Second mip level of grid g (nto_mip_select): features = (1 - t) level + t level_b;
+     * mip_t[g] = 0 or grid_b[g] = NULL: one level. */
+    const uint16_t *grid_b[2];
+    int32_t gw_b[2], gh_b[2];
+    float mip_t[2];
 } nto_model;
 
 typedef struct nto_fwd {
@@ -80,6 +85,8 @@ typedef struct nto_fwd {
     float y[16];     /* fp16-rounded outputs */
     int32_t base[2][2];
     float wx[2][4], wy[2][4];
+    int32_t base_b[2][2];   /* second mip level's footprint (mip_t > 0) */
+    float wx_b[2][4], wy_b[2][4];
 } nto_fwd;
 
 void nto_forward_sample(const nto_model *m, float u, float v, nto_fwd *f);
@@ -93,10 +100,16 @@ void nto_decode_range(const nto_model *m, int32_t w, int32_t h, int64_t first, i
                       void *out, int32_t out_f32, int32_t threads);
 
 typedef struct nto_train_args {
-    const uint16_t *target;    /* fp16 [image_h][image_w][cout] */
+    const uint16_t *target;    /* fp16 [target_h][target_w][cout] */
     const float *channel_weights; /* [cout] or NULL */
     nto_sampler sampler;
     int32_t finalize;          /* 1: no latent gradients */
+    /* mip chains (all zero: one level, target of the image's size) */
+    int32_t target_w, target_h;          /* 0: the sampler's image size */
+    const uint16_t *target_b;            /* second target level, weight target_t */
+    int32_t target_w_b, target_h_b;
+    float target_t;
+    float *ggrid_b[2];                   /* gradients of the grids' second levels */
 } nto_train_args;
 
 /* One training pass: accumulates network and latent gradients (fp32, already scaled by
@@ -107,6 +120,18 @@ double nto_train_pass(const nto_model *m, const nto_train_args *a, float *gW[3],
 double nto_train_pass_range(const nto_model *m, const nto_train_args *a, int64_t first,
                             int64_t count, float *gW[3], float *gb[3], float *ggrid[2],
                             int32_t threads);
+
+/* ---- mip chains ------------------------------------------------------------------------
+ * A chain of n levels stores level m (max(w >> m, 1) x max(h >> m, 1) texels, train.cu:214-218)
+ * after level m - 1.  nto_mip_select gives the levels a sample at mip coordinate lod reads
+ * (train.cu:78-103, :264-314): lod clamped to [0, n - 1] (NaN: 0), m0 = floor, m1 =
+ * min(m0 + 1, n - 1), t = lod - m0 when m1 > m0, else 0; the sample is (1 - t) s(m0) + t s(m1). */
+void nto_mip_select(int32_t num_mips, float lod, int32_t *m0, int32_t *m1, float *t);
+int32_t nto_mip_dim(int32_t size, int32_t m);
+int64_t nto_mip_offset(int32_t w, int32_t h, int32_t m); /* texels before level m */
+/* Levels 1 .. n - 1 of an fp16 chain from level 0: 2x2 box average in fp32 ((a + b) + (c + d))
+ * * 0.25, source texels clamped to the level below, rounded to fp16. */
+void nto_build_mips(uint16_t *chain, int32_t w, int32_t h, int32_t c, int32_t num_mips);
 
 /* ---- Adam (train.cu:521-564, :566-588) ---------------------------------------------- */
 void nto_adam_bias_correction(float beta1, float beta2, int32_t step, float *bc1, float *bc2);

@@ -61,12 +61,15 @@ class Sampler(C.Structure):
 class Model(C.Structure):
     _fields_ = [("channels", C.c_int32), ("cout", C.c_int32),
                 ("gw", C.c_int32 * 2), ("gh", C.c_int32 * 2),
-                ("grid", u16p * 2), ("blocks", f32p * 2), ("W", u16p * 3), ("b", u16p * 3)]
+                ("grid", u16p * 2), ("blocks", f32p * 2), ("W", u16p * 3), ("b", u16p * 3),
+                ("grid_b", u16p * 2), ("gw_b", C.c_int32 * 2), ("gh_b", C.c_int32 * 2), ("mip_t", C.c_float * 2)]
 
 
 class TrainArgs(C.Structure):
     _fields_ = [("target", u16p), ("channel_weights", f32p), ("sampler", Sampler),
-                ("finalize", C.c_int32)]
+                ("finalize", C.c_int32), ("target_w", C.c_int32), ("target_h", C.c_int32),
+                ("target_b", u16p), ("target_w_b", C.c_int32), ("target_h_b", C.c_int32),
+                ("target_t", C.c_float), ("ggrid_b", f32p * 2)]
 
 
 def lib():
@@ -95,6 +98,13 @@ def lib():
                                  u16p, C.POINTER(C.c_double), C.c_int32]
         L.nto_decode_range.argtypes = [C.POINTER(Model), C.c_int32, C.c_int32, C.c_int64,
                                        C.c_int64, C.c_void_p, C.c_int32, C.c_int32]
+        L.nto_mip_select.argtypes = [C.c_int32, C.c_float, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_float)]
+        L.nto_mip_dim.restype = C.c_int32
+        L.nto_mip_dim.argtypes = [C.c_int32, C.c_int32]
+        L.nto_mip_offset.restype = C.c_int64
+        L.nto_mip_offset.argtypes = [C.c_int32, C.c_int32, C.c_int32]
+        L.nto_build_mips.argtypes = [u16p, C.c_int32, C.c_int32, C.c_int32, C.c_int32]
         L.nto_train_pass.restype = C.c_double
         L.nto_train_pass.argtypes = [C.POINTER(Model), C.POINTER(TrainArgs), f32p * 3, f32p * 3,
                                      f32p * 2, C.c_int32]
@@ -165,6 +175,12 @@ class OracleModel:
     b: list              # 3 x uint16
     blocks: list | None = None       # 2 x float32 BC6 block features (then grids are unused)
     block_sizes: list | None = None  # 2 x (w, h) texels of the block grids
+    mips: list | None = None         # 2 x list of levels (uint16 [h_m][w_m][C]); level 0 = grids[g]
+    lod: float = 0.0                 # mip coordinate of every sample (with mips)
+
+    def levels(self, g):
+        """(m0, m1, t) of grid g at self.lod (nto_mip_select)."""
+        return mip_select(len(self.mips[g]) if self.mips else 1, self.lod)
 
     def ctype(self) -> Model:
         m = Model()
@@ -174,6 +190,15 @@ class OracleModel:
             if self.blocks is not None:
                 m.gw[g], m.gh[g] = self.block_sizes[g]
                 m.blocks[g] = _p(self.blocks[g], f32p)
+            elif self.mips is not None:
+                m0, m1, t = self.levels(g)
+                a, b = self.mips[g][m0], self.mips[g][m1]
+                m.gh[g], m.gw[g] = a.shape[0], a.shape[1]
+                m.grid[g] = _p(a, u16p)
+                if t > 0:
+                    m.gh_b[g], m.gw_b[g] = b.shape[0], b.shape[1]
+                    m.grid_b[g] = _p(b, u16p)
+                    m.mip_t[g] = t
             else:
                 m.gh[g], m.gw[g] = self.grids[g].shape[0], self.grids[g].shape[1]
                 m.grid[g] = _p(self.grids[g], u16p)
@@ -217,11 +242,46 @@ def decode_range(model: OracleModel, w: int, h: int, first: int, count: int, thr
     return out
 
 
+def mip_select(num_mips: int, lod: float):
+    m0, m1, t = C.c_int32(), C.c_int32(), C.c_float()
+    lib().nto_mip_select(num_mips, lod, C.byref(m0), C.byref(m1), C.byref(t))
+    return m0.value, m1.value, t.value
+
+
+def mip_chain_levels(w: int, h: int, n: int):
+    """[(w_m, h_m, texel offset)] of an n-level chain."""
+    L = lib()
+    return [(L.nto_mip_dim(w, m), L.nto_mip_dim(h, m), L.nto_mip_offset(w, h, m)) for m in range(n)]
+
+
+def build_mips(level0: np.ndarray, n: int) -> list:
+    """fp16 bit chain (list of [h_m][w_m][c] uint16 levels) built from level 0 (nto_build_mips)."""
+    h, w, c = level0.shape
+    lv = mip_chain_levels(w, h, n)
+    total = lv[-1][2] + lv[-1][0] * lv[-1][1]
+    chain = np.zeros(total * c, np.uint16)
+    chain[:w * h * c] = level0.reshape(-1)
+    lib().nto_build_mips(_p(chain, u16p), w, h, c, n)
+    return [chain[o * c:(o + lw * lh) * c].reshape(lh, lw, c) for (lw, lh, o) in lv]
+
+
 def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel_weights=None,
-               finalize: bool = False, threads: int = 1, first: int = 0, count: int | None = None):
-    """One training pass.  Returns (sse, gW[3], gb[3], ggrid[2]) with fresh fp32 grads."""
+               finalize: bool = False, threads: int = 1, first: int = 0, count: int | None = None,
+               target_mips: list | None = None):
+    """One training pass.  Returns (sse, gW[3], gb[3], ggrid[2]) with fresh fp32 grads; with
+    model.mips, ggrid[g] is the list of per-level gradients of grid g's chain.  target_mips
+    (list of levels, level 0 = target) is sampled at model.lod."""
     m = model.ctype()
     a = TrainArgs()
+    if target_mips is not None:
+        t0, t1, tt = mip_select(len(target_mips), model.lod)
+        target = target_mips[t0]
+        a.target_h, a.target_w = target.shape[0], target.shape[1]
+        if tt > 0:
+            tb = target_mips[t1]
+            a.target_b = _p(tb, u16p)
+            a.target_h_b, a.target_w_b = tb.shape[0], tb.shape[1]
+            a.target_t = tt
     a.target = _p(target, u16p)
     cw = None
     if channel_weights is not None:
@@ -231,11 +291,20 @@ def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel
     a.finalize = int(finalize)
     gW = [np.zeros(x.shape, np.float32) for x in model.W]
     gb = [np.zeros(64, np.float32), np.zeros(64, np.float32), np.zeros(model.cout, np.float32)]
-    gg = ([np.zeros(bl.shape, np.float32) for bl in model.blocks] if model.blocks is not None
-          else [np.zeros(g.shape, np.float32) for g in model.grids])
+    if model.mips is not None:
+        chains = [[np.zeros(lv.shape, np.float32) for lv in model.mips[g]] for g in range(2)]
+        sel = [model.levels(g) for g in range(2)]
+        pg = (f32p * 2)(*[_p(chains[g][sel[g][0]], f32p) for g in range(2)])
+        for g in range(2):
+            if sel[g][2] > 0:
+                a.ggrid_b[g] = _p(chains[g][sel[g][1]], f32p)
+        gg = chains
+    else:
+        gg = ([np.zeros(bl.shape, np.float32) for bl in model.blocks] if model.blocks is not None
+              else [np.zeros(g.shape, np.float32) for g in model.grids])
+        pg = (f32p * 2)(*[_p(x, f32p) for x in gg])
     pW = (f32p * 3)(*[_p(x, f32p) for x in gW])
     pb = (f32p * 3)(*[_p(x, f32p) for x in gb])
-    pg = (f32p * 2)(*[_p(x, f32p) for x in gg])
     if count is None:
         sse = lib().nto_train_pass(C.byref(m), C.byref(a), pW, pb, pg, threads)
     else:

@@ -73,6 +73,8 @@ def _valid_looking_params():
     (lambda p: setattr(p.features[0], "width", 0), "features[0]"),
     (lambda p: p.network_weights.__setitem__(2, None), "network_weights[2]"),
     (lambda p: setattr(p, "sample_stride_x", 0.0), "strides"),
+    (lambda p: setattr(p.features[0], "num_mips", 17), "num_mips"),
+    (lambda p: setattr(p, "target_num_mips", 17), "target_num_mips"),
 ])
 def test_training_rejects_invalid_arguments(native, mutate, needle):
     from neural_textures_b200 import _native
@@ -96,6 +98,24 @@ def test_latent_format_must_match_the_training_type(native):
     p.features[0].width = 30  # block features need whole 4x4 blocks
     assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 1
     assert "multiple of 4" in _native.last_error()
+
+
+def test_mip_coordinate_restrictions(native):
+    """Sharded calls sample level 0; block features sample one level whose size is a multiple
+    of 4 (both rejected on the host, before any CUDA call)."""
+    from neural_textures_b200 import _native
+    p = _valid_looking_params()
+    p.features[0].num_mips = p.features[1].num_mips = 3
+    p.lod = 1.0
+    p.lattice_rows = 32
+    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_UNCONSTRAINED, None) == 1
+    assert b"lod 0" in native.nt_get_last_error_string()
+    p = _valid_looking_params()
+    p.latent_format = _native.NT_LATENT_BC6_BLOCKS
+    p.features[0].num_mips = 3
+    p.lod = 0.5
+    assert native.nt_invoke_training(C.byref(p), _native.NT_TRAIN_BLOCK_FEATURES, None) == 1
+    assert b"one mip level" in native.nt_get_last_error_string()
 
 
 def test_null_params_rejected(native):

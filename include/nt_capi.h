@@ -60,17 +60,18 @@ typedef enum nt_status {
     NT_ERR_NCCL = 3,
     NT_ERR_TIMEOUT = 4,
     NT_ERR_BOUNDS = 5,
-    NT_ERR_UNSUPPORTED = 6
+    NT_ERR_UNSUPPORTED = 6,
+    NT_ERR_IO = 7               /* a checkpoint file could not be read or written, or is corrupt */
 } nt_status;
 
 /* train.h:22-27 */
 typedef enum NtTrainingKernelType {
     NT_TRAIN_UNCONSTRAINED = 0, /* latents are free fp16 grids */
-    NT_TRAIN_BLOCK_FEATURES = 1, /* BC6 block latents: not built (returns NT_ERR_UNSUPPORTED) */
+    NT_TRAIN_BLOCK_FEATURES = 1, /* BC6 block latents (latent_format NT_LATENT_BC6_BLOCKS) */
     NT_TRAIN_FINALIZE = 2        /* network gradients only, latents frozen */
 } NtTrainingKernelType;
 
-typedef enum NtDtype { NT_DTYPE_F16 = 0, NT_DTYPE_F32 = 1 } NtDtype;
+typedef enum NtDtype { NT_DTYPE_F16 = 0, NT_DTYPE_F32 = 1, NT_DTYPE_U8 = 2, NT_DTYPE_I32 = 3 } NtDtype;
 
 /* Opaque CUDA stream (cudaStream_t); NULL means the legacy default stream. */
 typedef void *nt_stream_t;
@@ -282,6 +283,35 @@ NT_API int64_t nt_mip_chain_texels(int32_t width, int32_t height, int32_t num_mi
  * (2x + 1, 2y + 1) of level m - 1 (clamped to its size), rounded to fp16. */
 NT_API nt_status nt_build_mips(void *chain, int32_t width, int32_t height, int32_t channels, int32_t num_mips,
                                nt_stream_t stream);
+
+/* ---- on-disk format (no reference counterpart: the reference's driver reads and writes EXR
+ * images, main.cpp:360-556, :855-904, and keeps no training state on disk) -----------------
+ *
+ * A checkpoint file is a set of named, typed sections in host memory order: an 64-byte header
+ * ("NTB2CKPT", version 1, section count, index offset and the index's FNV-1a 64 checksum),
+ * the payloads at 64-byte aligned offsets, then the index (per section: name, dtype, shape,
+ * offset, bytes and the payload's FNV-1a 64 checksum).  nt_checkpoint_write writes
+ * path + ".tmp" and renames it over path, so a reader never sees a partial file.  Reads verify
+ * the checksums and return NT_ERR_IO for a missing, truncated or corrupt file.  All buffers are
+ * host memory; neural_textures_b200.NeuralTexture.save / load map a material onto sections. */
+#define NT_CKPT_NAME_LEN 32
+#define NT_CKPT_MAX_SECTIONS 4096
+typedef struct NtCheckpointSection {
+    char name[NT_CKPT_NAME_LEN]; /* NUL-terminated, non-empty, unique within a file */
+    int32_t dtype;               /* NtDtype */
+    int32_t ndim;                /* 0 .. 4 */
+    int64_t shape[4];
+    int64_t bytes;               /* product of the shape x element size */
+    const void *data;            /* payload (nt_checkpoint_write); NULL in an index */
+} NtCheckpointSection;
+
+NT_API nt_status nt_checkpoint_write(const char *path, const NtCheckpointSection *sections, int32_t count);
+/* Fills up to capacity entries (data NULL) and *count with the file's section count; sections
+ * may be NULL with capacity 0 to query the count. */
+NT_API nt_status nt_checkpoint_index(const char *path, NtCheckpointSection *sections, int32_t capacity,
+                                     int32_t *count);
+/* Reads section `name` into dst, which must hold exactly its bytes. */
+NT_API nt_status nt_checkpoint_read(const char *path, const char *name, void *dst, int64_t bytes);
 
 /* ---- block records <-> BC6H blocks (no reference counterpart: the reference's
  * BLOCK_FEATURES path, train.cu:316-458, starts from and ends in float records) ----------- */

@@ -18,7 +18,7 @@ NT_MAX_OUTPUT = 16
 
 NT_OK = 0
 STATUS_NAMES = {0: "NT_OK", 1: "NT_ERR_INVALID_ARG", 2: "NT_ERR_CUDA", 3: "NT_ERR_NCCL",
-                4: "NT_ERR_TIMEOUT", 5: "NT_ERR_BOUNDS", 6: "NT_ERR_UNSUPPORTED"}
+                4: "NT_ERR_TIMEOUT", 5: "NT_ERR_BOUNDS", 6: "NT_ERR_UNSUPPORTED", 7: "NT_ERR_IO"}
 
 NT_TRAIN_UNCONSTRAINED = 0
 NT_TRAIN_BLOCK_FEATURES = 1
@@ -28,6 +28,9 @@ NT_LATENT_BC6_BLOCKS = 1
 NT_BC6F_RECORD_FLOATS = 32
 NT_DTYPE_F16 = 0
 NT_DTYPE_F32 = 1
+NT_DTYPE_U8 = 2
+NT_DTYPE_I32 = 3
+NT_CKPT_NAME_LEN = 32
 
 
 class NtAdamConstants(C.Structure):
@@ -38,6 +41,11 @@ class NtAdamConstants(C.Structure):
 class NtFeature(C.Structure):
     _fields_ = [("grid", C.c_void_p), ("gradients", C.c_void_p), ("moment1", C.c_void_p),
                 ("moment2", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32), ("num_mips", C.c_int32)]
+
+
+class NtCheckpointSection(C.Structure):
+    _fields_ = [("name", C.c_char * NT_CKPT_NAME_LEN), ("dtype", C.c_int32), ("ndim", C.c_int32),
+                ("shape", C.c_int64 * 4), ("bytes", C.c_int64), ("data", C.c_void_p)]
 
 
 class NtKernelParams(C.Structure):
@@ -121,6 +129,10 @@ SIGNATURES = {
     "nt_read_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "nt_mip_chain_texels": (C.c_int64, [C.c_int32, C.c_int32, C.c_int32]),
+    "nt_checkpoint_write": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32]),
+    "nt_checkpoint_index": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32,
+                                      C.POINTER(C.c_int32)]),
+    "nt_checkpoint_read": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_int64]),
     "nt_build_mips": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
 }
 

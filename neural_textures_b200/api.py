@@ -16,6 +16,7 @@ from __future__ import annotations
 import ctypes as C
 import enum
 import math
+import os
 
 import numpy as np
 
@@ -157,6 +158,60 @@ def bc6f_to_bc6h(records, width: int, height: int, channels: int, blocks=None, s
         blocks = torch.empty(bc6h_blocks_bytes(width, height, channels), dtype=torch.uint8, device=records.device)
     check(load().nt_bc6f_to_bc6h(records.data_ptr(), width, height, channels, blocks.data_ptr(), _stream(stream)))
     return blocks
+
+
+# ---------------------------------------------------------------------------------------
+# on-disk format (nt_checkpoint_write / _index / _read: named, typed, checksummed sections)
+
+_CKPT_DTYPES = {np.dtype(np.float16): N.NT_DTYPE_F16, np.dtype(np.float32): N.NT_DTYPE_F32,
+                np.dtype(np.uint8): N.NT_DTYPE_U8, np.dtype(np.int32): N.NT_DTYPE_I32}
+_CKPT_NUMPY = {v: k for k, v in _CKPT_DTYPES.items()}
+
+
+def checkpoint_write(path, sections: dict):
+    """Write host arrays (float16, float32, uint8 or int32; up to 4 dimensions) as named
+    sections; the file is replaced atomically."""
+    arrs = [(str(k), np.asarray(v, order="C")) for k, v in sections.items()]  # keeps 0-d arrays 0-d
+    tab = (N.NtCheckpointSection * max(len(arrs), 1))()
+    for i, (name, a) in enumerate(arrs):
+        if a.dtype not in _CKPT_DTYPES or a.ndim > 4:
+            raise ValueError(f"section {name!r}: dtype {a.dtype} with {a.ndim} dimensions is not storable")
+        e = tab[i]
+        e.name = name.encode()
+        e.dtype = _CKPT_DTYPES[a.dtype]
+        e.ndim = a.ndim
+        for d in range(a.ndim):
+            e.shape[d] = a.shape[d]
+        e.bytes = a.nbytes
+        e.data = a.ctypes.data
+    check(load().nt_checkpoint_write(os.fsencode(str(path)), tab, len(arrs)))
+
+
+def checkpoint_index(path) -> dict:
+    """{name: (numpy dtype, shape)} of a checkpoint file."""
+    L = load()
+    n = C.c_int32(0)
+    check(L.nt_checkpoint_index(os.fsencode(str(path)), None, 0, C.byref(n)))
+    tab = (N.NtCheckpointSection * max(n.value, 1))()
+    check(L.nt_checkpoint_index(os.fsencode(str(path)), tab, n.value, C.byref(n)))
+    return {tab[i].name.decode(): (_CKPT_NUMPY[tab[i].dtype], tuple(tab[i].shape[:tab[i].ndim]))
+            for i in range(n.value)}
+
+
+def checkpoint_read(path, name: str | None = None):
+    """One section as a numpy array, or all of them as a dict (checksums verified)."""
+    idx = checkpoint_index(path)
+    names = [name] if name is not None else list(idx)
+    out = {}
+    for nm in names:
+        if nm not in idx:
+            raise KeyError(f"{path} has no section {nm!r}")
+        dt, shape = idx[nm]
+        a = np.empty(shape, dt)
+        check(load().nt_checkpoint_read(os.fsencode(str(path)), nm.encode(), a.ctypes.data if a.nbytes else None,
+                                        a.nbytes))
+        out[nm] = a
+    return out[name] if name is not None else out
 
 
 # ---------------------------------------------------------------------------------------
@@ -339,6 +394,95 @@ class NeuralTexture:
         """Latent levels 1 .. n - 1 from level 0 (box filter), e.g. after training level 0."""
         for c, (w, h), n in zip(self.grid_chains, self.grid_sizes, self.num_mips):
             check(load().nt_build_mips(c.data_ptr(), w, h, self.C, n, _stream(stream)))
+
+    # -- checkpoints ------------------------------------------------------------------------------
+    def save(self, path, optimizer: bool = True, latents: str = "native", bias: float = 4.0,
+             target: bool = False):
+        """Write the material to a checkpoint file (nt_checkpoint_write).  Sections: meta.i32 /
+        meta.f32 (sizes, chains, latent format, step, seed, lod, Adam constants, loss weights),
+        net.W0..2 / net.b0..2 (fp16), latent0 / latent1 (fp16 chains or fp32 block records; with
+        latents="bc6h", BC6H blocks of value + bias from nt_bc6h_encode), with optimizer=True the
+        Adam moments (adam.*), with target=True the target chain.  Gradients are not stored: every
+        optimiser step consumes them."""
+        torch = self.torch
+        h = lambda t: t.detach().cpu().contiguous().numpy()
+        blocks_fmt = self.latent_format == N.NT_LATENT_BC6_BLOCKS
+        if latents not in ("native", "bc6h"):
+            raise ValueError("latents must be 'native' or 'bc6h'")
+        bc6h = latents == "bc6h"
+        if bc6h and (blocks_fmt or max(self.num_mips) > 1):
+            raise ValueError("latents='bc6h' stores single-level fp16 grids")
+        torch.cuda.synchronize(self.device)
+        meta = [1, self.image_w, self.image_h, self.C, self.cout, self.lattice[0], self.lattice[1],
+                *self.grid_sizes[0], *self.grid_sizes[1], *self.num_mips, self.target_num_mips,
+                int(self.latent_format), int(self.step), int(self.seed), int(bc6h), int(optimizer), int(target)]
+        metaf = [self.lod, *self.latent_adam, *self.network_adam, bias, getattr(self, "block_bias", 4.0),
+                 *([float(c) for c in self.channel_weights] + [0.0] * (16 - len(self.channel_weights)))]
+        sec = {"meta.i32": np.array(meta, np.int32), "meta.f32": np.array(metaf, np.float32)}
+        for l in range(3):
+            sec[f"net.W{l}"] = h(self.W[l])
+            sec[f"net.b{l}"] = h(self.b[l])
+        for g in range(2):
+            if blocks_fmt:
+                sec[f"latent{g}"] = h(self.blocks[g])
+            elif bc6h:
+                sec[f"latent{g}.bc6h"] = h(bc6h_encode(self.grids[g], "interleaved", bias))
+            else:
+                sec[f"latent{g}"] = h(self.grid_chains[g])
+        if optimizer:
+            for l in range(3):
+                sec[f"adam.mW{l}"], sec[f"adam.vW{l}"] = h(self.mW[l]), h(self.vW[l])
+                sec[f"adam.mb{l}"], sec[f"adam.vb{l}"] = h(self.mb[l]), h(self.vb[l])
+            for g in range(2):
+                sec[f"adam.m{g}"], sec[f"adam.v{g}"] = h(self.gm1[g]).reshape(-1), h(self.gm2[g]).reshape(-1)
+        if target:
+            sec["target"] = h(self.target_chain)
+        checkpoint_write(path, sec)
+
+    @classmethod
+    def load(cls, path, device="cuda"):
+        """A material from a checkpoint file written by save (checksums verified)."""
+        import torch
+        sec = checkpoint_read(path)
+        m = [int(x) for x in sec["meta.i32"]]
+        if m[0] != 1:
+            raise ValueError(f"{path}: material layout {m[0]} is not supported")
+        (_, iw, ih, Cc, cout, lw, lh, g0w, g0h, g1w, g1h, nm0, nm1, tnm, fmt, step, seed, bc6h, has_opt,
+         has_target) = m[:20]
+        f = [float(x) for x in sec["meta.f32"]]
+        tex = cls(iw, ih, grid_sizes=((g0w, g0h), (g1w, g1h)), latent_channels=Cc, output_channels=cout,
+                  device=device, lattice=(lw, lh), latent_lr=f[3], network_lr=f[7], beta1=f[5], beta2=f[6],
+                  eps=f[8], num_mips=(nm0, nm1), target_num_mips=tnm)
+        tex.latent_adam = tuple(f[1:5])
+        tex.network_adam = tuple(f[5:9])
+        tex.lod, tex.step, tex.seed = f[0], step, seed
+        tex.block_bias = f[10]
+        tex.channel_weights = f[11:11 + cout]
+        d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(tex.device)
+        for l in range(3):
+            tex.W[l].copy_(d(sec[f"net.W{l}"]))
+            tex.b[l].copy_(d(sec[f"net.b{l}"]))
+        if fmt == N.NT_LATENT_BC6_BLOCKS:
+            tex.use_blocks([d(sec["latent0"]), d(sec["latent1"])])
+        for g in range(2):
+            if fmt == N.NT_LATENT_BC6_BLOCKS:
+                continue
+            if bc6h:
+                bc6h_decode(d(sec[f"latent{g}.bc6h"]), tex.grids[g], "interleaved", f[9])
+            else:
+                tex.grid_chains[g].copy_(d(sec[f"latent{g}"]))
+        if has_opt:
+            for l in range(3):
+                tex.mW[l].copy_(d(sec[f"adam.mW{l}"]))
+                tex.vW[l].copy_(d(sec[f"adam.vW{l}"]))
+                tex.mb[l].copy_(d(sec[f"adam.mb{l}"]))
+                tex.vb[l].copy_(d(sec[f"adam.vb{l}"]))
+            for g in range(2):
+                tex.gm1[g].view(-1).copy_(d(sec[f"adam.m{g}"]))
+                tex.gm2[g].view(-1).copy_(d(sec[f"adam.v{g}"]))
+        if has_target:
+            tex.target_chain.copy_(d(sec["target"]))
+        return tex
 
     def load_host(self, grids, W, b, target=None):
         """Upload host fp16 arrays (grids [h][w][C], padded W, b, optional target)."""

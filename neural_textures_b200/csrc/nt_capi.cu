@@ -76,6 +76,20 @@ static nt_status fail(nt_status st, const char *fmt, ...)
     return st;
 }
 
+namespace nt {
+// The last-error string for code outside this file (the checkpoint reader and writer).
+nt_status set_error(nt_status st, const char *fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+}  // namespace nt
+
 static nt_status check_cuda(cudaError_t e, const char *what)
 {
     if (e == cudaSuccess) return NT_OK;

@@ -97,6 +97,22 @@ typedef struct NtFeature {
     int32_t num_mips;   /* train.h:61; 0 or 1: one level (see NtKernelParams.lod) */
 } NtFeature;
 
+/* train.h:69-77.  A reference texture: a CUDA texture object over an fp32 mip chain
+ * (nt_reference_texture_create), sampled like the reference: Catmull-Rom through 9 hardware
+ * bilinear fetches per level (filter/catmull_rom.h:39-89), the two levels of the mip coordinate
+ * blended (train.cu:78-103).  Its channels fill the next output channels of the target, each
+ * with the texture's loss weight (train.cu:105-157). */
+#define NT_MAX_REFERENCE_TEXTURES 16 /* train.h:20 */
+typedef struct NtReferenceTexture {
+    uint64_t texture;      /* cudaTextureObject_t; 0: skipped */
+    uint64_t storage;      /* the cudaMipmappedArray behind it (freed by nt_reference_texture_destroy) */
+    int32_t width, height; /* level 0 */
+    int32_t num_channels;  /* 1 .. 4 */
+    int32_t num_mips;
+    float loss_weight;
+    int32_t reserved;
+} NtReferenceTexture;
+
 /* train.h:120-157.  Passed by pointer; the library copies what it needs at launch, so the
  * struct may be modified or freed as soon as the call returns. */
 /* Latent representations (NtKernelParams.latent_format). */
@@ -186,6 +202,14 @@ typedef struct NtKernelParams {
     float lod;
     int32_t target_num_mips;
     int32_t target_width, target_height;
+
+    /* Reference textures (train.h:139-140).  With num_reference_textures > 0 the training target
+     * and the inference MSE come from them instead of `target`: texture i fills the next
+     * num_channels output channels (train.cu:105-157), each weighted by its loss_weight, and
+     * output channels past the textures' are trained towards 0 with weight 1 (train.cu:112-119);
+     * channel_loss_weights is then unused.  Needs an unsharded call. */
+    NtReferenceTexture reference_textures[NT_MAX_REFERENCE_TEXTURES];
+    int32_t num_reference_textures;
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */
@@ -272,6 +296,23 @@ NT_API nt_status nt_bc6h_decode_raw(const void *blocks, int64_t num_blocks, int3
  * writes [blocks_h*4][blocks_w*4][4] floats.  Synchronous; allocates and frees the array. */
 NT_API nt_status nt_bc6h_decode_hardware(const void *blocks, int32_t blocks_w, int32_t blocks_h,
                                          int32_t is_signed, float *rgba);
+
+/* ---- reference textures (main.cpp:558-637: UploadTexture) -------------------------------- */
+
+/* Texture object over an fp32 chain of num_mips levels (0 or 1: one level), level after level,
+ * each [h_m][w_m][c] with c = num_channels, or 4 for 3 channels (the reference uploads RGB as
+ * RGBA, main.cpp:216-224, :547), in host or device memory.  The texture uses the reference's
+ * descriptor: wrap addressing, linear filtering, normalized coordinates, linear mipmap
+ * filtering (main.cpp:609-619).  Allocates device memory: not for use inside a captured graph. */
+NT_API nt_status nt_reference_texture_create(const float *chain, int32_t width, int32_t height,
+                                             int32_t num_channels, int32_t num_mips, float loss_weight,
+                                             NtReferenceTexture *out);
+NT_API nt_status nt_reference_texture_destroy(NtReferenceTexture *texture);
+/* Samples texture at n coordinates (uv: n x 2 floats, device) and mip coordinate lod with the
+ * reference's filter (SampleReferenceTextureTrilinear, train.cu:78-103): out gets n x 4 floats
+ * (device; channels past num_channels are 0). */
+NT_API nt_status nt_reference_texture_sample(const NtReferenceTexture *texture, const float *uv, int64_t n,
+                                             float lod, float *out, nt_stream_t stream);
 
 /* ---- mip chains (no reference counterpart: the reference loads its chains from EXR files,
  * main.cpp:360-433) ------------------------------------------------------------------------ */

@@ -13,6 +13,7 @@ from .api import (  # noqa: F401
     InvokeOptimizeNetwork,
     InvokeTraining,
     NeuralTexture,
+    ReferenceTexture,
     RunForwardPassTest,
     TrainingKernelType,
     TrainStep,

@@ -31,6 +31,7 @@ NT_DTYPE_F32 = 1
 NT_DTYPE_U8 = 2
 NT_DTYPE_I32 = 3
 NT_CKPT_NAME_LEN = 32
+NT_MAX_REFERENCE_TEXTURES = 16
 
 
 class NtAdamConstants(C.Structure):
@@ -41,6 +42,12 @@ class NtAdamConstants(C.Structure):
 class NtFeature(C.Structure):
     _fields_ = [("grid", C.c_void_p), ("gradients", C.c_void_p), ("moment1", C.c_void_p),
                 ("moment2", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32), ("num_mips", C.c_int32)]
+
+
+class NtReferenceTexture(C.Structure):
+    _fields_ = [("texture", C.c_uint64), ("storage", C.c_uint64), ("width", C.c_int32), ("height", C.c_int32),
+                ("num_channels", C.c_int32), ("num_mips", C.c_int32), ("loss_weight", C.c_float),
+                ("reserved", C.c_int32)]
 
 
 class NtCheckpointSection(C.Structure):
@@ -89,6 +96,8 @@ class NtKernelParams(C.Structure):
         ("target_num_mips", C.c_int32),
         ("target_width", C.c_int32),
         ("target_height", C.c_int32),
+        ("reference_textures", NtReferenceTexture * NT_MAX_REFERENCE_TEXTURES),
+        ("num_reference_textures", C.c_int32),
     ]
 
 
@@ -129,6 +138,11 @@ SIGNATURES = {
     "nt_read_device_status": (C.c_int, [C.POINTER(C.c_uint32), C.c_int32]),
     "nt_flush_l2": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p]),
     "nt_mip_chain_texels": (C.c_int64, [C.c_int32, C.c_int32, C.c_int32]),
+    "nt_reference_texture_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float,
+                                             C.POINTER(NtReferenceTexture)]),
+    "nt_reference_texture_destroy": (C.c_int, [C.POINTER(NtReferenceTexture)]),
+    "nt_reference_texture_sample": (C.c_int, [C.POINTER(NtReferenceTexture), C.c_void_p, C.c_int64, C.c_float,
+                                             C.c_void_p, C.c_void_p]),
     "nt_checkpoint_write": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32]),
     "nt_checkpoint_index": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32,
                                       C.POINTER(C.c_int32)]),

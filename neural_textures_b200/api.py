@@ -161,6 +161,70 @@ def bc6f_to_bc6h(records, width: int, height: int, channels: int, blocks=None, s
 
 
 # ---------------------------------------------------------------------------------------
+# reference textures (train.h:69-77, main.cpp:558-637)
+
+def box_chain_f32(level0: np.ndarray, num_mips: int) -> np.ndarray:
+    """fp32 chain (levels one after another) of [h][w][c] level 0: 2x2 box average per level,
+    source texels clamped to the level below (the rule of nt_build_mips, in fp32)."""
+    levels = [np.ascontiguousarray(level0, np.float32)]
+    for _ in range(1, max(int(num_mips), 1)):
+        a = levels[-1]
+        h, w = a.shape[:2]
+        dh, dw = max(h >> 1, 1), max(w >> 1, 1)
+        ys0, xs0 = np.minimum(2 * np.arange(dh), h - 1), np.minimum(2 * np.arange(dw), w - 1)
+        ys1, xs1 = np.minimum(ys0 + 1, h - 1), np.minimum(xs0 + 1, w - 1)
+        p = lambda ys, xs: a[ys][:, xs]
+        levels.append(((p(ys0, xs0) + p(ys0, xs1)) + (p(ys1, xs0) + p(ys1, xs1))) * np.float32(0.25))
+    return np.concatenate([l.reshape(-1) for l in levels])
+
+
+class ReferenceTexture:
+    """A reference texture (train.h:69-77): a CUDA texture object over an fp32 mip chain with
+    the reference's descriptor (nt_reference_texture_create).  `chain` holds the levels one after
+    another, [h_m][w_m][c] with c = channels (4 for 3 channels); host (numpy) or device (torch)."""
+
+    def __init__(self, chain, width: int, height: int, channels: int, num_mips: int = 1, loss_weight: float = 1.0):
+        self._chain = chain if not isinstance(chain, np.ndarray) else np.ascontiguousarray(chain, np.float32)
+        ptr = self._chain.ctypes.data if isinstance(self._chain, np.ndarray) else self._chain.data_ptr()
+        self.desc = N.NtReferenceTexture()
+        check(load().nt_reference_texture_create(ptr, width, height, channels, num_mips, loss_weight,
+                                                 C.byref(self.desc)))
+        self._chain = None  # uploaded: the array owns a copy
+
+    @classmethod
+    def from_image(cls, image: np.ndarray, num_mips: int = 1, loss_weight: float = 1.0):
+        """From an fp32 [h][w][channels] image (1 .. 4 channels; RGB is padded with alpha 1, as
+        main.cpp:547 does), its chain built with the box filter."""
+        img = np.asarray(image, np.float32)
+        if img.ndim == 2:
+            img = img[:, :, None]
+        h, w, ch = img.shape
+        if ch == 3:
+            img = np.concatenate([img, np.ones((h, w, 1), np.float32)], axis=2)
+        return cls(box_chain_f32(img, num_mips), w, h, ch, num_mips, loss_weight)
+
+    def sample(self, uv, lod: float = 0.0, stream=None):
+        """SampleReferenceTextureTrilinear (train.cu:78-103) at device coordinates uv [n][2] ->
+        [n][4] float32 (channels past num_channels are 0)."""
+        import torch
+        uv = uv.contiguous()
+        out = torch.empty((uv.shape[0], 4), dtype=torch.float32, device=uv.device)
+        check(load().nt_reference_texture_sample(C.byref(self.desc), uv.data_ptr(), uv.shape[0], lod, out.data_ptr(),
+                                                 _stream(stream)))
+        return out
+
+    def close(self):
+        if getattr(self, "desc", None) is not None and self.desc.texture:
+            check(load().nt_reference_texture_destroy(C.byref(self.desc)))
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------------------
 # on-disk format (nt_checkpoint_write / _index / _read: named, typed, checksummed sections)
 
 _CKPT_DTYPES = {np.dtype(np.float16): N.NT_DTYPE_F16, np.dtype(np.float32): N.NT_DTYPE_F32,
@@ -291,6 +355,7 @@ class NeuralTexture:
         self.step = 0
         self.latent_format = N.NT_LATENT_GRID_F16
         self.blocks = None  # BC6 block-feature records per grid (fp32), when latent_format is 1
+        self.reference_textures = []  # ReferenceTexture list: replaces `target` when non-empty
 
     def use_blocks(self, records):
         """Switch the latents to BC6 block features: `records` holds, per grid, the fp32
@@ -541,6 +606,11 @@ class NeuralTexture:
         p.latent_format = self.latent_format
         p.lod = self.lod
         p.target_num_mips = self.target_num_mips
+        if len(self.reference_textures) > N.NT_MAX_REFERENCE_TEXTURES:
+            raise ValueError(f"at most {N.NT_MAX_REFERENCE_TEXTURES} reference textures")
+        for i, rt in enumerate(self.reference_textures):
+            p.reference_textures[i] = rt.desc
+        p.num_reference_textures = len(self.reference_textures)
         p.seed = self.seed
         if loss_accum:
             p.loss_accum = self.loss_accum.data_ptr()

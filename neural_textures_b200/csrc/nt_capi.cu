@@ -58,6 +58,11 @@ cudaError_t launch_target(void *out, int32_t w, int32_t h, int32_t c, uint32_t s
 cudaError_t launch_init_latents(void *grid, int64_t count, uint32_t seed, cudaStream_t st);
 cudaError_t launch_flush(void *scratch, size_t bytes, cudaStream_t st);
 cudaError_t launch_build_mips(__half *chain, int32_t w, int32_t h, int32_t c, int32_t num_mips, cudaStream_t st);
+cudaError_t ref_texture_create(const float *chain, int w, int h, int ch, int mips, NtReferenceTexture *out);
+cudaError_t ref_texture_destroy(NtReferenceTexture *t);
+RefTexView ref_view(const NtReferenceTexture &t);
+cudaError_t launch_ref_sample(const NtReferenceTexture &t, const float *uv, int64_t n, float lod, float *out,
+                              cudaStream_t st);
 
 }  // namespace nt
 
@@ -214,6 +219,22 @@ static LevelView feature_levels(const NtKernelParams *p, int f)
     return v;
 }
 
+// Reference textures of the call (train.h:139-140); returns the number used.
+static nt_status reference_views(const NtKernelParams *p, RefTexView (&ref)[kMaxRefTextures], int &n)
+{
+    NT_REQUIRE(p->num_reference_textures >= 0 && p->num_reference_textures <= NT_MAX_REFERENCE_TEXTURES,
+               "num_reference_textures must be in [0, %d]", NT_MAX_REFERENCE_TEXTURES);
+    n = p->num_reference_textures;
+    for (int i = 0; i < n; ++i) {
+        const NtReferenceTexture &t = p->reference_textures[i];
+        NT_REQUIRE(!t.texture || (t.num_channels >= 1 && t.num_channels <= 4 && t.width >= 1 && t.height >= 1 &&
+                                  t.num_mips >= 0 && t.num_mips <= 16),
+                   "reference_textures[%d]: 1 .. 4 channels, a positive size and 0 .. 16 mips are required", i);
+        ref[i] = ref_view(t);
+    }
+    return NT_OK;
+}
+
 static NetView net_view(const NtKernelParams *p)
 {
     NetView n;
@@ -348,6 +369,8 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(target_num_mips)
     NT_FIELD(target_width)
     NT_FIELD(target_height)
+    NT_FIELD(reference_textures)
+    NT_FIELD(num_reference_textures)
 #undef NT_FIELD
     return (size_t)-1;
 }
@@ -361,7 +384,8 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
                "unknown training kernel type %d", (int)type);
     nt_status st = validate_network(p);
     if (st != NT_OK) return st;
-    NT_REQUIRE(p->target && aligned16(p->target), "target must be a non-null 16-byte aligned device pointer");
+    NT_REQUIRE(p->num_reference_textures > 0 || (p->target && aligned16(p->target)),
+               "target must be a non-null 16-byte aligned device pointer (or reference textures given)");
     NT_REQUIRE(p->image_width >= 1 && p->image_height >= 1, "image size must be positive");
     NT_REQUIRE(p->lattice_width >= 1 && p->lattice_height >= 1, "lattice size must be positive");
     NT_REQUIRE((int64_t)p->lattice_width * p->lattice_height == p->num_samples,
@@ -403,7 +427,19 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
         L.gW[l] = p->network_weight_gradients[l];
         L.gb[l] = p->network_bias_gradients[l];
     }
-    {  // target chain at the same lod
+    if ((st = reference_views(p, L.ref, L.num_ref)) != NT_OK) return st;
+    L.ref_lod = p->lod;
+    if (L.num_ref > 0) {  // train.cu:105-157: texture channels in order, each with its loss weight
+        int oc = 0;
+        for (int c = 0; c < 16; ++c) L.cw[c] = 1.f;
+        for (int i = 0; i < L.num_ref && oc < 16; ++i) {
+            const NtReferenceTexture &t = p->reference_textures[i];
+            if (!t.texture) continue;
+            for (int c = 0; c < t.num_channels && oc < 16; ++c) L.cw[oc++] = t.loss_weight;
+        }
+        L.tw = p->image_width;
+        L.th = p->image_height;
+    } else {  // target chain at the same lod
         NT_REQUIRE(p->target_num_mips >= 0 && p->target_num_mips <= 16 && p->target_width >= 0 && p->target_height >= 0,
                    "target_num_mips must be in [0, 16] and the target size non-negative");
         const int tw = p->target_width ? p->target_width : p->image_width;
@@ -420,8 +456,9 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
             L.target_t = ts.t;
             fractional = true;
         }
-    }
-    for (int c = 0; c < 16; ++c) L.cw[c] = c < p->output_channels ? p->channel_loss_weights[c] : 0.f;
+    }  // target
+    if (!L.num_ref)
+        for (int c = 0; c < 16; ++c) L.cw[c] = c < p->output_channels ? p->channel_loss_weights[c] : 0.f;
     L.sampler.image_w = p->image_width;
     L.sampler.image_h = p->image_height;
     L.sampler.lattice_w = p->lattice_width;
@@ -456,6 +493,8 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
     NT_REQUIRE(!sharded || (p->lod == 0.f && L.th == p->image_height),
                "row sharding needs lod 0 and a target of the image's height");
     NT_REQUIRE(!fractional || train_engine() == 1, "a fractional lod needs the tcgen05 training engine");
+    NT_REQUIRE(!L.num_ref || (!sharded && train_engine() == 1),
+               "reference textures need the tcgen05 training engine and an unsharded call");
     // latent representation: UNCONSTRAINED trains fp16 grids, BLOCK_FEATURES trains BC6 block
     // features (train.cu:902-913), FINALIZE samples either and trains the network only
     NT_REQUIRE(type != NT_TRAIN_UNCONSTRAINED || p->latent_format == NT_LATENT_GRID_F16,
@@ -526,7 +565,8 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     NT_REQUIRE(!(p->inference_output_dtype == NT_DTYPE_F16 && p->output_channels == 8) ||
                    aligned16(p->inference_output),
                "inference_output must be 16-byte aligned");
-    NT_REQUIRE(!p->inference_mse_accum || p->target, "inference_mse_accum requires a target");
+    NT_REQUIRE(!p->inference_mse_accum || p->target || p->num_reference_textures > 0,
+               "inference_mse_accum requires a target or reference textures");
     DecodeLaunch L;
     memset(&L, 0, sizeof L);
     bool fractional = false;
@@ -548,7 +588,12 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     L.out = p->inference_output;
     L.out_f32 = p->inference_output_dtype == NT_DTYPE_F32;
     L.target = reinterpret_cast<const __half *>(p->target);
-    if (p->inference_mse_accum) {  // the target level of this lod, texel for texel
+    if ((st = reference_views(p, L.ref, L.num_ref)) != NT_OK) return st;
+    L.ref_lod = p->lod;
+    if (L.num_ref > 0) {
+        NT_REQUIRE(decode_engine() == 1, "reference textures need the tcgen05 decode engine");
+        L.target = nullptr;  // the MSE compares with the textures
+    } else if (p->inference_mse_accum) {  // the target level of this lod, texel for texel
         const int tw = p->target_width ? p->target_width : p->image_width;
         const int th = p->target_height ? p->target_height : p->image_height;
         const MipSel ts = mip_select(p->target_num_mips, p->lod);
@@ -673,6 +718,35 @@ nt_status nt_init_latents(void *grid, int64_t count, uint32_t seed, nt_stream_t 
     NT_REQUIRE(count >= 0, "count must be non-negative");
     if (count == 0) return NT_OK;
     return check_cuda(launch_init_latents(grid, count, seed, (cudaStream_t)stream), "latent init");
+}
+
+nt_status nt_reference_texture_create(const float *chain, int32_t width, int32_t height, int32_t num_channels,
+                                      int32_t num_mips, float loss_weight, NtReferenceTexture *out)
+{
+    NT_REQUIRE(chain && out, "chain and out are required");
+    NT_REQUIRE(width >= 1 && height >= 1 && width <= 65536 && height <= 65536, "texture size must be in [1, 65536]");
+    NT_REQUIRE(num_channels >= 1 && num_channels <= 4, "num_channels must be 1 .. 4");
+    NT_REQUIRE(num_mips >= 0 && num_mips <= 16, "num_mips must be in [0, 16]");
+    memset(out, 0, sizeof *out);
+    out->loss_weight = loss_weight;
+    return check_cuda(ref_texture_create(chain, width, height, num_channels, num_mips, out), "reference texture");
+}
+
+nt_status nt_reference_texture_destroy(NtReferenceTexture *texture)
+{
+    NT_REQUIRE(texture, "texture is null");
+    return check_cuda(ref_texture_destroy(texture), "reference texture release");
+}
+
+nt_status nt_reference_texture_sample(const NtReferenceTexture *texture, const float *uv, int64_t n, float lod,
+                                      float *out, nt_stream_t stream)
+{
+    NT_REQUIRE(texture && texture->texture, "texture is null");
+    NT_REQUIRE(n >= 0, "n must be non-negative");
+    if (n == 0) return NT_OK;
+    NT_REQUIRE(uv && out && aligned16(out) && (reinterpret_cast<uintptr_t>(uv) & 7u) == 0,
+               "uv (8-byte aligned) and out (16-byte aligned) device pointers are required");
+    return check_cuda(launch_ref_sample(*texture, uv, n, lod, out, (cudaStream_t)stream), "reference texture sample");
 }
 
 int64_t nt_mip_chain_texels(int32_t width, int32_t height, int32_t num_mips)

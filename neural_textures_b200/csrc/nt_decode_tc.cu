@@ -334,6 +334,20 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
                             const float d = yv[e] - __half2float(t[c0 + e]);
                             sse = fmaf(d, d, sse);
                         }
+                } else if (p.num_ref > 0 && p.mse_accum) {  // reference textures (train.cu:946-960)
+                    float uu, vv, ex[16];
+                    texel_uv(x, y, p.image_w, p.image_h, uu, vv);
+                    ref_expected(p.ref, p.num_ref, uu, vv, p.ref_lod, ex);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        if (c0 + e < c1) {
+                            float te = 0.f;
+#pragma unroll
+                            for (int k = 0; k < 16; ++k)
+                                if (k == c0 + e) te = ex[k];
+                            const float d = yv[e] - te;
+                            sse = fmaf(d, d, sse);
+                        }
                 }
             }
         }

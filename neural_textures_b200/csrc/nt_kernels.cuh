@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "nt_common.cuh"
+#include "nt_reftex.cuh"
 
 namespace nt {
 
@@ -49,6 +50,10 @@ struct TrainLaunch {
     const __half *target_b;
     int32_t tw_b, th_b;
     float target_t;
+    // reference textures (num_ref > 0): the target comes from them, at mip coordinate ref_lod
+    RefTexView ref[kMaxRefTextures];
+    int32_t num_ref;
+    float ref_lod;
 };
 
 struct DecodeLaunch {
@@ -65,6 +70,10 @@ struct DecodeLaunch {
     const __half *grid_b[2];
     int32_t gw_b[2], gh_b[2];
     float mip_t[2];
+    // reference textures for the MSE (num_ref > 0 and mse_accum)
+    RefTexView ref[kMaxRefTextures];
+    int32_t num_ref;
+    float ref_lod;
 };
 
 constexpr int kMaxAdamSegments = 8;

@@ -845,6 +845,8 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     shard_rows(p, 2, p.th, fp);
                     if constexpr (TC > 0)
                         gather_cr<TC>(p.target, p.tw, fp, tgt);
+                    else if (p.num_ref > 0)  // reference textures (train.cu:105-157)
+                        ref_expected(p.ref, p.num_ref, u, v, p.ref_lod, tgt);
                     else
                         gather_cr_any(p.target, p.tw, cout, fp, tgt);
                     if constexpr (MIP) {
@@ -1164,22 +1166,28 @@ cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t str
 {
     const int cout = p.net.cout;
     if (p.blocks) {  // BC6 block features
-        if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, true>(p, stream) : tc::launch_t<8, 0, true>(p, stream);
+        if (channels == 8)
+            return cout == 8 && !p.num_ref ? tc::launch_t<8, 8, true>(p, stream) : tc::launch_t<8, 0, true>(p, stream);
         if (channels == 12)
-            return cout == 12 ? tc::launch_t<12, 12, true>(p, stream) : tc::launch_t<12, 0, true>(p, stream);
+            return cout == 12 && !p.num_ref ? tc::launch_t<12, 12, true>(p, stream)
+                                            : tc::launch_t<12, 0, true>(p, stream);
         return cudaErrorInvalidValue;
     }
     if (p.mip_t[0] > 0.f || p.mip_t[1] > 0.f || p.target_t > 0.f) {  // two mip levels
         if (channels == 8)
-            return cout == 8 ? tc::launch_t<8, 8, false, true>(p, stream) : tc::launch_t<8, 0, false, true>(p, stream);
+            return cout == 8 && !p.num_ref ? tc::launch_t<8, 8, false, true>(p, stream)
+                                           : tc::launch_t<8, 0, false, true>(p, stream);
         if (channels == 12)
-            return cout == 12 ? tc::launch_t<12, 12, false, true>(p, stream)
-                              : tc::launch_t<12, 0, false, true>(p, stream);
+            return cout == 12 && !p.num_ref ? tc::launch_t<12, 12, false, true>(p, stream)
+                                            : tc::launch_t<12, 0, false, true>(p, stream);
         return cudaErrorInvalidValue;
     }
-    if (channels == 8) return cout == 8 ? tc::launch_t<8, 8, false>(p, stream) : tc::launch_t<8, 0, false>(p, stream);
+    // reference textures come through the generic target path (TC = 0)
+    if (channels == 8)
+        return cout == 8 && !p.num_ref ? tc::launch_t<8, 8, false>(p, stream) : tc::launch_t<8, 0, false>(p, stream);
     if (channels == 12)
-        return cout == 12 ? tc::launch_t<12, 12, false>(p, stream) : tc::launch_t<12, 0, false>(p, stream);
+        return cout == 12 && !p.num_ref ? tc::launch_t<12, 12, false>(p, stream)
+                                        : tc::launch_t<12, 0, false>(p, stream);
     return cudaErrorInvalidValue;
 }
 

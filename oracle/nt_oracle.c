@@ -634,16 +634,20 @@ double nto_train_pass_range(const nto_model *m, const nto_train_args *a, int64_t
             nto_fwd f;
             nto_forward_sample(m, u, v, &f);
             float t[16] = {0};
+            float rw[16];
             const int32_t tw = a->target_w > 0 ? a->target_w : s->image_w;
             const int32_t th = a->target_h > 0 ? a->target_h : s->image_h;
-            sample_target(a->target, tw, th, m->cout, u, v, t);
-            if (a->target_b && a->target_t > 0.f) {
+            if (a->num_ref > 0)
+                nto_ref_expected(a->ref, a->num_ref, u, v, a->lod, t, rw);
+            else
+                sample_target(a->target, tw, th, m->cout, u, v, t);
+            if (a->num_ref == 0 && a->target_b && a->target_t > 0.f) {
                 float tb[16] = {0};
                 sample_target(a->target_b, a->target_w_b, a->target_h_b, m->cout, u, v, tb);
                 for (int c = 0; c < m->cout; ++c) t[c] = mip_blend(t[c], tb[c], a->target_t);
             }
             float dx[32];
-            sse_total += backward_sample(m, &f, t, a->channel_weights, acc, dx);
+            sse_total += backward_sample(m, &f, t, a->num_ref > 0 ? rw : a->channel_weights, acc, dx);
             scatter_latent(m, &f, dx, scale, gg, a->finalize ? NULL : a->ggrid_b);
         }
     }
@@ -670,6 +674,106 @@ double nto_train_pass(const nto_model *m, const nto_train_args *a, float *gW[3],
 {
     const int64_t total = (int64_t)a->sampler.lattice_w * a->sampler.lattice_h;
     return nto_train_pass_range(m, a, 0, total, gW, gb, ggrid, threads);
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Reference textures                                                                    */
+/* ------------------------------------------------------------------------------------ */
+
+static int32_t g_tex_filter_mode = 1;
+
+void nto_set_texture_filter_mode(int32_t mode) { g_tex_filter_mode = mode; }
+
+static float tex_weight(float a)
+{
+    if (g_tex_filter_mode == 1) return floorf(a * 256.f + 0.5f) / 256.f;
+    if (g_tex_filter_mode == 2) return floorf(a * 256.f) / 256.f;
+    return a;
+}
+
+/* One hardware bilinear fetch of level m at normalized (x, y), wrap addressing. */
+static void ref_bilinear(const nto_ref_texture *t, int32_t m, float x, float y, float out[4])
+{
+    const int32_t cc = t->channels == 3 ? 4 : t->channels;
+    const int32_t lw = nto_mip_dim(t->w, m), lh = nto_mip_dim(t->h, m);
+    const float *lv = t->chain + nto_mip_offset(t->w, t->h, m) * cc;
+    const float xs = (x - floorf(x)) * (float)lw - 0.5f, ys = (y - floorf(y)) * (float)lh - 0.5f;
+    const float fx = floorf(xs), fy = floorf(ys);
+    const float a = tex_weight(xs - fx), b = tex_weight(ys - fy);
+    const int32_t x0 = nto_wrap((int32_t)fx, lw), x1 = nto_wrap((int32_t)fx + 1, lw);
+    const int32_t y0 = nto_wrap((int32_t)fy, lh), y1 = nto_wrap((int32_t)fy + 1, lh);
+    for (int c = 0; c < 4; ++c) {
+        if (c >= t->channels || (t->channels == 3 && c == 3)) {
+            out[c] = 0.f;
+            continue;
+        }
+        const float t00 = lv[((int64_t)y0 * lw + x0) * cc + c], t10 = lv[((int64_t)y0 * lw + x1) * cc + c];
+        const float t01 = lv[((int64_t)y1 * lw + x0) * cc + c], t11 = lv[((int64_t)y1 * lw + x1) * cc + c];
+        out[c] = (1.f - a) * (1.f - b) * t00 + a * (1.f - b) * t10 + (1.f - a) * b * t01 + a * b * t11;
+    }
+}
+
+/* filter/catmull_rom.h:39-89: Catmull-Rom from 9 bilinear fetches, the middle taps of each
+ * axis merged at w2 / (w1 + w2). */
+static void ref_catmull_rom(const nto_ref_texture *t, float u, float v, int32_t m, float out[4])
+{
+    const float size[2] = {(float)nto_mip_dim(t->w, m), (float)nto_mip_dim(t->h, m)};
+    const float uv[2] = {u, v};
+    float w[2][3], pos[2][3];
+    for (int a = 0; a < 2; ++a) {
+        const float sp = uv[a] * size[a];
+        const float t1 = floorf(sp - 0.5f) + 0.5f;
+        const float f = sp - t1;
+        float cr[4];
+        nto_catmull_rom_weights(f, cr);
+        const float w12 = cr[1] + cr[2];
+        w[a][0] = cr[0];
+        w[a][1] = w12;
+        w[a][2] = cr[3];
+        pos[a][0] = (t1 - 1.f) / size[a];
+        pos[a][1] = (t1 + cr[2] / w12) / size[a];
+        pos[a][2] = (t1 + 2.f) / size[a];
+    }
+    for (int c = 0; c < 4; ++c) out[c] = 0.f;
+    for (int j = 0; j < 3; ++j)
+        for (int i = 0; i < 3; ++i) {
+            float s[4];
+            ref_bilinear(t, m, pos[0][i], pos[1][j], s);
+            const float k = w[0][i] * w[1][j];
+            for (int c = 0; c < 4; ++c) out[c] += s[c] * k;
+        }
+}
+
+/* train.cu:78-103 */
+void nto_ref_trilinear(const nto_ref_texture *t, float u, float v, float lod, float out[4])
+{
+    int32_t m0, m1;
+    float f;
+    nto_mip_select(t->num_mips, lod, &m0, &m1, &f);
+    ref_catmull_rom(t, u, v, m0, out);
+    if (f <= 0.f) return;
+    float s1[4];
+    ref_catmull_rom(t, u, v, m1, s1);
+    for (int c = 0; c < 4; ++c) out[c] = out[c] * (1.f - f) + s1[c] * f;
+}
+
+void nto_ref_expected(const nto_ref_texture *t, int32_t n, float u, float v, float lod, float expected[16],
+                      float weights[16])
+{
+    for (int k = 0; k < 16; ++k) {
+        expected[k] = 0.f;
+        if (weights) weights[k] = 1.f;
+    }
+    int oc = 0;
+    for (int i = 0; i < n && oc < 16; ++i) {
+        if (!t[i].chain || t[i].channels <= 0) continue;
+        float s[4];
+        nto_ref_trilinear(&t[i], u, v, lod, s);
+        for (int c = 0; c < t[i].channels && c < 4 && oc < 16; ++c, ++oc) {
+            expected[oc] = s[c];
+            if (weights) weights[oc] = t[i].loss_weight;
+        }
+    }
 }
 
 /* ------------------------------------------------------------------------------------ */

@@ -99,6 +99,24 @@ void nto_decode(const nto_model *m, int32_t w, int32_t h, void *out, int32_t out
 void nto_decode_range(const nto_model *m, int32_t w, int32_t h, int64_t first, int64_t count,
                       void *out, int32_t out_f32, int32_t threads);
 
+/* ---- reference textures (train.cu:78-157, filter/catmull_rom.h:39-89) -----------------
+ * An fp32 chain, level after level, [h_m][w_m][cc] with cc = channels (4 for 3 channels).
+ * The texture unit's bilinear filter is emulated: wrap addressing of normalized coordinates,
+ * texel position x W - 0.5, weights of the two texels per axis from its fraction; the fraction
+ * is exact (mode 0), rounded to the nearest 1/256 (1) or truncated to 1/256 (2) -- the CUDA
+ * documentation gives 9-bit fixed-point weights with 8 fractional bits. */
+typedef struct nto_ref_texture {
+    const float *chain;
+    int32_t w, h, channels, num_mips;
+    float loss_weight;
+} nto_ref_texture;
+void nto_set_texture_filter_mode(int32_t mode);
+void nto_ref_trilinear(const nto_ref_texture *t, float u, float v, float lod, float out[4]);
+/* train.cu:105-157: the textures' channels fill expected[] in order, weights = loss_weight (1
+ * past the textures) */
+void nto_ref_expected(const nto_ref_texture *t, int32_t n, float u, float v, float lod, float expected[16],
+                      float weights[16]);
+
 typedef struct nto_train_args {
     const uint16_t *target;    /* fp16 [target_h][target_w][cout] */
     const float *channel_weights; /* [cout] or NULL */
@@ -110,6 +128,9 @@ typedef struct nto_train_args {
     int32_t target_w_b, target_h_b;
     float target_t;
     float *ggrid_b[2];                   /* gradients of the grids' second levels */
+    const nto_ref_texture *ref;          /* reference textures (num_ref > 0 replaces target) */
+    int32_t num_ref;
+    float lod;                           /* their mip coordinate */
 } nto_train_args;
 
 /* One training pass: accumulates network and latent gradients (fp32, already scaled by

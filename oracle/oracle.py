@@ -65,11 +65,17 @@ class Model(C.Structure):
                 ("grid_b", u16p * 2), ("gw_b", C.c_int32 * 2), ("gh_b", C.c_int32 * 2), ("mip_t", C.c_float * 2)]
 
 
+class RefTexture(C.Structure):
+    _fields_ = [("chain", f32p), ("w", C.c_int32), ("h", C.c_int32), ("channels", C.c_int32),
+                ("num_mips", C.c_int32), ("loss_weight", C.c_float)]
+
+
 class TrainArgs(C.Structure):
     _fields_ = [("target", u16p), ("channel_weights", f32p), ("sampler", Sampler),
                 ("finalize", C.c_int32), ("target_w", C.c_int32), ("target_h", C.c_int32),
                 ("target_b", u16p), ("target_w_b", C.c_int32), ("target_h_b", C.c_int32),
-                ("target_t", C.c_float), ("ggrid_b", f32p * 2)]
+                ("target_t", C.c_float), ("ggrid_b", f32p * 2), ("ref", C.POINTER(RefTexture)),
+                ("num_ref", C.c_int32), ("lod", C.c_float)]
 
 
 def lib():
@@ -98,6 +104,9 @@ def lib():
                                  u16p, C.POINTER(C.c_double), C.c_int32]
         L.nto_decode_range.argtypes = [C.POINTER(Model), C.c_int32, C.c_int32, C.c_int64,
                                        C.c_int64, C.c_void_p, C.c_int32, C.c_int32]
+        L.nto_set_texture_filter_mode.argtypes = [C.c_int32]
+        L.nto_ref_trilinear.argtypes = [C.POINTER(RefTexture), C.c_float, C.c_float, C.c_float, f32p]
+        L.nto_ref_expected.argtypes = [C.POINTER(RefTexture), C.c_int32, C.c_float, C.c_float, C.c_float, f32p, f32p]
         L.nto_mip_select.argtypes = [C.c_int32, C.c_float, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                      C.POINTER(C.c_float)]
         L.nto_mip_dim.restype = C.c_int32
@@ -242,6 +251,29 @@ def decode_range(model: OracleModel, w: int, h: int, first: int, count: int, thr
     return out
 
 
+def ref_textures(defs):
+    """ctypes array of reference textures from [(chain float32, w, h, channels, num_mips,
+    loss_weight)] (the chains must stay alive while the array is used)."""
+    arr = (RefTexture * max(len(defs), 1))()
+    for i, (chain, w, h, ch, nm, lw) in enumerate(defs):
+        arr[i].chain = _p(chain, f32p)
+        arr[i].w, arr[i].h, arr[i].channels, arr[i].num_mips, arr[i].loss_weight = w, h, ch, nm, lw
+    return arr
+
+
+def ref_sample(defs, uv: np.ndarray, lod: float, filter_mode: int = 1) -> np.ndarray:
+    """SampleReferenceTextureTrilinear (train.cu:78-103) of the first texture at uv ([n][2]) ->
+    [n][4]; emulated bilinear weights: 0 exact, 1 nearest 1/256, 2 truncated to 1/256."""
+    L = lib()
+    L.nto_set_texture_filter_mode(filter_mode)
+    arr = ref_textures(defs)
+    out = np.zeros((len(uv), 4), np.float32)
+    for i, (u, v) in enumerate(np.asarray(uv, np.float32)):
+        L.nto_ref_trilinear(arr, float(u), float(v), lod, _p(out[i], f32p))
+    L.nto_set_texture_filter_mode(1)
+    return out
+
+
 def mip_select(num_mips: int, lod: float):
     m0, m1, t = C.c_int32(), C.c_int32(), C.c_float()
     lib().nto_mip_select(num_mips, lod, C.byref(m0), C.byref(m1), C.byref(t))
@@ -267,7 +299,7 @@ def build_mips(level0: np.ndarray, n: int) -> list:
 
 def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel_weights=None,
                finalize: bool = False, threads: int = 1, first: int = 0, count: int | None = None,
-               target_mips: list | None = None):
+               target_mips: list | None = None, ref_textures_defs=None):
     """One training pass.  Returns (sse, gW[3], gb[3], ggrid[2]) with fresh fp32 grads; with
     model.mips, ggrid[g] is the list of per-level gradients of grid g's chain.  target_mips
     (list of levels, level 0 = target) is sampled at model.lod."""
@@ -282,7 +314,14 @@ def train_pass(model: OracleModel, target: np.ndarray, sampler: Sampler, channel
             a.target_b = _p(tb, u16p)
             a.target_h_b, a.target_w_b = tb.shape[0], tb.shape[1]
             a.target_t = tt
-    a.target = _p(target, u16p)
+    if target is not None:
+        a.target = _p(target, u16p)
+    refs = None
+    if ref_textures_defs:  # reference textures replace the target (train.cu:105-157)
+        refs = ref_textures(ref_textures_defs)
+        a.ref = C.cast(refs, C.POINTER(RefTexture))
+        a.num_ref = len(ref_textures_defs)
+        a.lod = model.lod
     cw = None
     if channel_weights is not None:
         cw = np.ascontiguousarray(channel_weights, np.float32)

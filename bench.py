@@ -381,6 +381,55 @@ def run_mips(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank, l
     return out
 
 
+def run_reftex(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank):
+    """Config-1 training with the target from reference textures on the texture units
+    (train.h:69-77, train.cu:78-157): albedo and normal (RGB, stored RGBA), roughness and
+    metalness (one channel each) = 8 output channels, 1024^2 with 11-level chains, 9 bilinear
+    fetches per texture and sample.  L2 flushed before every timed step."""
+    import numpy as np
+    rng = np.random.default_rng(100 + rank)
+    W, H = CFG1["image"]
+    texs = [nt.ReferenceTexture.from_image(rng.random((H, W, ch), dtype=np.float32), num_mips=11, loss_weight=lw)
+            for ch, lw in ((3, 1.0), (3, 1.0), (1, 0.5), (1, 0.5))]
+    tex = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                           output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
+    tex.init(seed=rank)
+    tex.reference_textures = texs
+    sptr = stream.cuda_stream
+    B = CFG1["lattice"][0] * CFG1["lattice"][1]
+
+    def step_once(step, ev=None):
+        p = tex.params(step=step)
+        if ev:
+            ev[0].record(stream)
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 0, sptr))
+        if ev:
+            ev[1].record(stream)
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), sptr))
+        if ev:
+            ev[2].record(stream)
+
+    for w in range(warmup):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(w + 1)
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for k in range(steps):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(warmup + k + 1, events[k])
+    torch.cuda.synchronize(dev)
+    t_train = sum(e[0].elapsed_time(e[1]) for e in events) / steps
+    t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / steps
+    out = {"workload": "config1_reference_textures_1024sq_8ch", "value": B / ((t_train + t_adam) * 1e-3),
+           "unit": "samples/s", "ms_per_step": t_train + t_adam, "steps": steps, "warmup": warmup,
+           "textures": "albedo RGB, normal RGB, roughness, metalness: fp32 1024^2, 11 levels, texture objects",
+           "kernels_ms": {"train_kernel_textures": t_train, "adam_kernel": t_adam},
+           "l2": "flushed (256 MB write) before every timed step"}
+    del tex
+    for t in texs:
+        t.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -394,6 +443,7 @@ def main():
     ap.add_argument("--sharded-steps", type=int, default=20, help="timed config-4b sharded steps (0: skip)")
     ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
     ap.add_argument("--mip-steps", type=int, default=50, help="timed steps at a fractional mip coordinate (0: skip)")
+    ap.add_argument("--texture-steps", type=int, default=50, help="timed steps with reference-texture targets (0: skip)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -517,6 +567,9 @@ def main():
     mips = None
     if args.mip_steps > 0:
         mips = run_mips(torch, dev, stream, L, nt, _native, scratch, args.mip_steps, 5, rank)
+    reftex = None
+    if args.texture_steps > 0:
+        reftex = run_reftex(torch, dev, stream, L, nt, _native, scratch, args.texture_steps, 5, rank)
     cfg4b = None
     if args.sharded_steps > 0:
         cfg4b = run_config4b(torch, dist, dev, stream, rank, world, args.sharded_steps, 10)
@@ -581,6 +634,8 @@ def main():
     if mips:
         mips["adam_hbm_frac"] = mips["adam_hbm_gbs"] / pk["hbm"]
         line["mips"] = mips
+    if reftex:
+        line["reference_textures"] = reftex
     if cfg4b:
         line["config4b"] = cfg4b
     if not args.no_cpu_baseline:

@@ -460,7 +460,10 @@ def main():
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        from torch.distributed import ProcessGroupNCCL
+        opts = ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True  # config 4b: halo exchanges overlap the interior Adam
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120), pg_options=opts)
     L = _native.load()
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream

@@ -182,7 +182,65 @@ class ShardedTexture:
         p.seed = self.seed
 
     def train_params(self) -> N.NtKernelParams:
-        """Training pass over this rank's lattice rows; sources addressed by full row."""
+        """Training pass over this rank's lattice rows; sources addressed by full row.  Built
+        once (every buffer keeps its address) and updated with the step; refresh_params()
+        rebuilds it after a hyper-parameter change."""
+        p = self.__dict__.get("_train_p")
+        if p is None:
+            p = self._train_p = self._build_train_params()
+        p.step = self.step
+        return p
+
+    def adam_params(self) -> N.NtKernelParams:
+        """Adam over the network and the owned band of each grid (halo rows excluded)."""
+        p = self.__dict__.get("_adam_p")
+        if p is None:
+            p = self._adam_p = self._build_adam_params()
+        p.step = self.step
+        return p
+
+    def refresh_params(self):
+        for k in ("_train_p", "_adam_p", "_adam_split"):
+            self.__dict__.pop(k, None)
+
+    def _adam_rows(self, rows, network: bool) -> N.NtKernelParams:
+        """Adam over band rows [r0, r1) of each grid (rows[i] for grid i, relative to the band),
+        with or without the network."""
+        p = N.NtKernelParams()
+        self._common(p)
+        for i in range(2):
+            band, f = self.bands[i], p.features[i]
+            r0, r1 = rows[i]
+            s0 = band.halo + r0
+            f.grid = self.grids[i][s0:].data_ptr()
+            f.gradients = self.ggrads[i][s0:].data_ptr()
+            f.moment1 = self.gm1[i][s0:].data_ptr()
+            f.moment2 = self.gm2[i][s0:].data_ptr()
+            f.width, f.height = self.grid_sizes[i][0], r1 - r0
+        p.target = self.target.data_ptr()
+        return p
+
+    def adam_split(self):
+        """Adam of a multi-rank step in three parts: (interior, first edge + network, last edge).
+        Halo gradients from the neighbours only reach the first and last HALO rows of each band,
+        so the interior rows can be updated while the exchange is in flight; Adam is elementwise,
+        so the parts give exactly the full update.  None when a band is too thin to split."""
+        sp = self.__dict__.get("_adam_split", 0)
+        if sp == 0:
+            sp = None
+            owned = [self.bands[i].owned for i in range(2)]
+            e = [min(self.bands[i].halo, owned[i]) for i in range(2)]
+            if all(o > 2 * ei for o, ei in zip(owned, e)):
+                sp = (self._adam_rows([(e[i], owned[i] - e[i]) for i in range(2)], False),
+                      self._adam_rows([(0, e[i]) for i in range(2)], True),
+                      self._adam_rows([(owned[i] - e[i], owned[i]) for i in range(2)], False))
+            self._adam_split = sp
+        if sp is not None:
+            for p in sp:
+                p.step = self.step
+        return sp
+
+    def _build_train_params(self) -> N.NtKernelParams:
         p = N.NtKernelParams()
         self._common(p)
         for i in range(2):
@@ -202,8 +260,7 @@ class ShardedTexture:
         p.loss_accum = self.loss_accum.data_ptr()
         return p
 
-    def adam_params(self) -> N.NtKernelParams:
-        """Adam over the network and the owned band of each grid (halo rows excluded)."""
+    def _build_adam_params(self) -> N.NtKernelParams:
         p = N.NtKernelParams()
         self._common(p)
         for i in range(2):
@@ -248,7 +305,9 @@ class ShardedTexture:
 # ---- communication -----------------------------------------------------------------------------------
 
 class DistComm:
-    """Exchanges over torch.distributed (one process per rank)."""
+    """Exchanges over torch.distributed (one process per rank).  A process group created with
+    ProcessGroupNCCL.Options(is_high_priority_stream=True) lets the exchanges run beside the
+    interior Adam of train_step instead of queueing behind its CTAs."""
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -260,43 +319,97 @@ class DistComm:
         its operations in the same order, so the k-th send to a peer meets that peer's k-th
         receive from this rank (which keeps two ranks, where both neighbours are the same
         peer, unambiguous)."""
+        self.wait(self.exchange_async(sends, recvs))
+
+    def exchange_async(self, sends, recvs):
+        """exchange() without the wait: returns the works (wait() orders the current stream after them)."""
         dist = self.dist
         ops = [dist.P2POp(dist.isend, t, d, self.group) for t, d in sends]
         ops += [dist.P2POp(dist.irecv, t, s, self.group) for t, s in recvs]
-        for r in dist.batch_isend_irecv(ops):
-            r.wait()
+        return list(dist.batch_isend_irecv(ops))
 
     def allreduce(self, t):
         self.dist.all_reduce(t, group=self.group)
 
+    def allreduce_async(self, t):
+        return [self.dist.all_reduce(t, group=self.group, async_op=True)]
 
-def _rx(shard, key, like):
-    """Receive buffer kept on the shard across steps."""
-    bufs = shard.__dict__.setdefault("_rx", {})
-    if key not in bufs:
-        bufs[key] = shard.torch.empty_like(like)
-    return bufs[key]
+    @staticmethod
+    def wait(works):
+        for w in works:
+            w.wait()
+
+
+class _Packed:
+    """One contiguous buffer holding the same rows of both grids (flat views), so that each
+    neighbour gets one message per exchange instead of one per grid."""
+
+    def __init__(self, views):
+        assert all(v.is_contiguous() for v in views), "band and halo rows must be contiguous row ranges"
+        self.views = [v.view(-1) for v in views]
+        sizes = [v.numel() for v in self.views]
+        self.buf = views[0].new_empty(sum(sizes))
+        self.parts = list(self.buf.split(sizes))
+
+    def pack(self, torch):
+        torch.cat(self.views, out=self.buf)
+
+    def unpack_add(self, torch):
+        torch._foreach_add_(self.views, self.parts)
+
+    def unpack_copy(self, torch):
+        torch._foreach_copy_(self.views, self.parts)
+
+
+def _plan(shard):
+    """Per-rank exchange buffers, built once: packed halo gradients to send up / down, packed
+    receives for the band edges, and the same for the latent rows."""
+    pl = shard.__dict__.get("_xplan")
+    if pl is not None:
+        return pl
+    g, lat = shard.ggrads, shard.grids
+    both = lambda f, t: [f(t, 0), f(t, 1)]
+    pl = shard._xplan = {
+        # gradients: my halo above belongs to the rank above (its last rows), my halo below to
+        # the rank below (its first rows)
+        "g_up": _Packed(both(shard.halo_above, g)), "g_dn": _Packed(both(shard.halo_below, g)),
+        "g_last": _Packed(both(shard.band_last, g)), "g_first": _Packed(both(shard.band_first, g)),
+        "g_halos": both(shard.halo_above, g) + both(shard.halo_below, g),
+        # latents: my first rows fill the upper rank's halo below, my last rows the lower rank's halo above
+        "l_first": _Packed(both(shard.band_first, lat)), "l_last": _Packed(both(shard.band_last, lat)),
+        "l_below": _Packed(both(shard.halo_below, lat)), "l_above": _Packed(both(shard.halo_above, lat)),
+    }
+    return pl
+
+
+def start_gradient_exchange(shard, comm):
+    """Packs the halo gradients and posts their exchange (dn's halo above = my last rows, up's
+    halo below = my first rows); returns the works to pass to finish_gradient_exchange."""
+    torch = shard.torch
+    r, n = shard.rank, shard.world
+    up, dn = (r - 1) % n, (r + 1) % n
+    pl = _plan(shard)
+    pl["g_up"].pack(torch)
+    pl["g_dn"].pack(torch)
+    return comm.exchange_async([(pl["g_up"].buf, up), (pl["g_dn"].buf, dn)],
+                               [(pl["g_last"].buf, dn), (pl["g_first"].buf, up)])
+
+
+def finish_gradient_exchange(shard, comm, works):
+    """Waits for the exchange, adds the received gradients to the band edges, clears the halos."""
+    torch = shard.torch
+    comm.wait(works)
+    pl = _plan(shard)
+    pl["g_last"].unpack_add(torch)
+    pl["g_first"].unpack_add(torch)
+    torch._foreach_zero_(pl["g_halos"])
 
 
 def exchange_gradients(shard, comm):
     """Halo gradients -> owners (added to their bands); halo gradients cleared."""
-    r, n = shard.rank, shard.world
-    if n == 1:
+    if shard.world == 1:
         return
-    up, dn = (r - 1) % n, (r + 1) % n
-    sends, recvs, adds = [], [], []
-    for i in range(2):
-        sends += [(shard.halo_above(shard.ggrads, i), up), (shard.halo_below(shard.ggrads, i), dn)]
-        a, b = _rx(shard, ("g", i, 0), shard.band_last(shard.ggrads, i)), _rx(shard, ("g", i, 1),
-                                                                              shard.band_first(shard.ggrads, i))
-        recvs += [(a, dn), (b, up)]  # dn's halo above = my last rows; up's halo below = my first rows
-        adds += [(shard.band_last(shard.ggrads, i), a), (shard.band_first(shard.ggrads, i), b)]
-    comm.exchange(sends, recvs)
-    for dst, src in adds:
-        dst.add_(src)
-    for i in range(2):
-        shard.halo_above(shard.ggrads, i).zero_()
-        shard.halo_below(shard.ggrads, i).zero_()
+    finish_gradient_exchange(shard, comm, start_gradient_exchange(shard, comm))
 
 
 def exchange_latents(shard, comm):
@@ -304,21 +417,40 @@ def exchange_latents(shard, comm):
     r, n = shard.rank, shard.world
     if n == 1:
         return
+    torch = shard.torch
     up, dn = (r - 1) % n, (r + 1) % n
-    sends, recvs = [], []
-    for i in range(2):
-        sends += [(shard.band_first(shard.grids, i), up), (shard.band_last(shard.grids, i), dn)]
-        recvs += [(shard.halo_below(shard.grids, i), dn), (shard.halo_above(shard.grids, i), up)]
-    comm.exchange(sends, recvs)
+    pl = _plan(shard)
+    pl["l_first"].pack(torch)
+    pl["l_last"].pack(torch)
+    comm.exchange([(pl["l_first"].buf, up), (pl["l_last"].buf, dn)],
+                  [(pl["l_below"].buf, dn), (pl["l_above"].buf, up)])
+    pl["l_below"].unpack_copy(torch)
+    pl["l_above"].unpack_copy(torch)
 
 
 def train_step(shard: ShardedTexture, comm, stream=None):
-    """One data-parallel step of the sharded material (every rank calls it)."""
+    """One data-parallel step of the sharded material (every rank calls it).  With several
+    ranks, Adam over the band interiors runs while the halo-gradient exchange and the
+    network-gradient allreduce are in flight; the band edges and the network follow them."""
     shard.train_pass(stream)
-    exchange_gradients(shard, comm)
-    if shard.world > 1:
-        comm.allreduce(shard.net_grad)
-    shard.adam(stream)
+    if shard.world == 1:
+        shard.adam(stream)
+        shard.step += 1
+        return
+    split = shard.adam_split()
+    works = start_gradient_exchange(shard, comm)
+    works_net = comm.allreduce_async(shard.net_grad)
+    if split is None:
+        finish_gradient_exchange(shard, comm, works)
+        comm.wait(works_net)
+        shard.adam(stream)
+    else:
+        L, s = load(), _stream(stream)
+        check(L.nt_invoke_optimize_features(C.byref(split[0]), N.NT_TRAIN_UNCONSTRAINED, s))  # interior
+        finish_gradient_exchange(shard, comm, works)
+        comm.wait(works_net)
+        check(L.nt_invoke_optimize_all(C.byref(split[1]), s))  # network + first edge rows
+        check(L.nt_invoke_optimize_features(C.byref(split[2]), N.NT_TRAIN_UNCONSTRAINED, s))  # last edge rows
     exchange_latents(shard, comm)
     shard.step += 1
 

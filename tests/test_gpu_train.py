@@ -216,3 +216,29 @@ def test_full_config1_step_identities(cuda):
         rhs = db1 @ W1[:, g * 8:(g + 1) * 8]
         tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
         assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)
+
+
+def test_full_config2_step_identities(cuda):
+    """BASELINE config 2 at full size (4096^2 PBR material with 12 channels, normals from the
+    height field; 1024^2x12 + 512^2x12 latents; 1,048,576 samples): the same identity per
+    latent channel, finite gradients, and unit-length target normals."""
+    import torch
+    import neural_textures_b200 as nt
+    tex = nt.NeuralTexture(4096, 4096, grid_sizes=((1024, 1024), (512, 512)), latent_channels=12,
+                           output_channels=12, device="cuda:0", lattice=(1024, 1024))
+    tex.init(seed=22, pbr_normals=True)
+    tgt = tex.target[::64, ::64].float().cpu().numpy().reshape(-1, 12)
+    n = np.linalg.norm(tgt[:, 3:6] * 2.0 - 1.0, axis=1)  # normals stored as n * 0.5 + 0.5
+    assert np.all(np.abs(n - 1.0) < 2e-2), (n.min(), n.max())
+    sse, gW, gb, gg = _train_pass_gpu(tex)
+    assert np.isfinite(sse) and sse > 0
+    for a in gW + gb + gg:
+        assert np.isfinite(a).all()
+    W1 = _host(tex.W[0]).astype(np.float64).reshape(64, 32)
+    db1 = gb[0].astype(np.float64)
+    for g in range(2):
+        flat = gg[g].astype(np.float64).reshape(-1, 12)
+        lhs = flat.sum(0)
+        rhs = db1 @ W1[:, g * 12:(g + 1) * 12]
+        tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
+        assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)

@@ -530,9 +530,10 @@ def main():
         dist.barrier()
     e2e_steps = args.steps
     t0 = time.perf_counter()
+    p = tex.params()  # one parameter block, its step advanced per call (main.cpp:1077)
     for k in range(e2e_steps):
         tex.loss_accum.zero_()
-        p = tex.params(step=10_000 + k)
+        p.step = 10_000 + k
         _native.check(L.nt_train_step(ctypes.byref(p), sptr))
         loss_host.copy_(tex.loss_accum, non_blocking=True)
         stream.synchronize()
@@ -616,8 +617,9 @@ def main():
                    "traffic": tr.get("decode_kernel", {}).get("bytes_per_launch")},
         "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": pbytes,
                 "d2h_bytes_per_step": 4,
-                "note": "nt_train_step through the C ABI per step: parameter block from host memory, loss copied "
-                        "to pinned host memory and synchronised; no L2 flush"},
+                "note": "nt_train_step through the C ABI per step: the parameter block read from host memory "
+                        "(kept by the caller, its step advanced per call as the reference driver does), loss "
+                        "copied to pinned host memory and synchronised; no L2 flush"},
         "gpu_launches": launches,
         "clocks": clk,
     }

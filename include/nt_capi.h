@@ -387,6 +387,10 @@ NT_API nt_status nt_umma_selftest(const void *a, const void *b, const void *h, f
  * then stops issuing work and returns.  Synchronises with the device; clear != 0 resets
  * the word. */
 NT_API nt_status nt_read_device_status(uint32_t *status, int32_t clear);
+/* Exercises the bounded-wait path without a fault: one thread waits on an mbarrier that
+ * nothing arrives on, gives up after `tries` polls (1 .. 1,000,000) and sets bit 0 of the
+ * status word, as the kernels do on a timeout.  Synchronous. */
+NT_API nt_status nt_wait_timeout_selftest(uint32_t tries);
 
 /* ---- seeded set-up helpers (not in the reference: it loads EXR files, main.cpp:436-556) -- */
 

@@ -143,6 +143,7 @@ SIGNATURES = {
     "nt_reference_texture_destroy": (C.c_int, [C.POINTER(NtReferenceTexture)]),
     "nt_reference_texture_sample": (C.c_int, [C.POINTER(NtReferenceTexture), C.c_void_p, C.c_int64, C.c_float,
                                              C.c_void_p, C.c_void_p]),
+    "nt_wait_timeout_selftest": (C.c_int, [C.c_uint32]),
     "nt_checkpoint_write": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32]),
     "nt_checkpoint_index": (C.c_int, [C.c_char_p, C.POINTER(NtCheckpointSection), C.c_int32,
                                       C.POINTER(C.c_int32)]),

@@ -1193,6 +1193,31 @@ cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t str
 
 }  // namespace nt
 
+namespace nt {
+
+// An mbarrier (count 1) that nothing arrives on: the bounded wait gives up after `tries` polls
+// and reports through the status word like the kernels' waits.
+__global__ void wait_timeout_kernel(uint32_t tries)
+{
+    __shared__ alignas(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        umma::mbar_init(smem_addr(&bar), 1);
+        umma::mbar_fence_init();
+        if (!umma::mbar_wait(smem_addr(&bar), 0, tries)) atomicOr(&g_device_status, 1u);
+    }
+}
+
+}  // namespace nt
+
+extern "C" nt_status nt_wait_timeout_selftest(uint32_t tries)
+{
+    if (tries < 1 || tries > 1000000) return NT_ERR_INVALID_ARG;
+    nt::wait_timeout_kernel<<<1, 32>>>(tries);
+    nt::count_launch();
+    if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) return NT_ERR_CUDA;
+    return NT_OK;
+}
+
 extern "C" nt_status nt_read_device_status(uint32_t *status, int32_t clear)
 {
     if (!status) return NT_ERR_INVALID_ARG;

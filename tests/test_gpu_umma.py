@@ -26,3 +26,21 @@ def test_umma_selftest(cuda):
     ref2 = H.astype(np.float64).T @ A.astype(np.float64)
     np.testing.assert_allclose(D1.cpu().numpy(), ref1, rtol=1e-4, atol=1e-3)
     np.testing.assert_allclose(D2.cpu().numpy(), ref2, rtol=1e-4, atol=1e-3)
+
+
+def test_bounded_wait_reports_a_timeout_and_the_context_survives(cuda):
+    """A wait that nothing satisfies gives up after its poll limit and sets bit 0 of the status
+    word (the kernels' timeout path), with no fault: the context keeps running work."""
+    import ctypes as C
+    import torch
+    from neural_textures_b200 import _native
+    L = _native.load()
+    st = C.c_uint32(0)
+    _native.check(L.nt_read_device_status(C.byref(st), 1))  # clear
+    _native.check(L.nt_wait_timeout_selftest(1000))
+    _native.check(L.nt_read_device_status(C.byref(st), 1))
+    assert st.value & 1
+    _native.check(L.nt_read_device_status(C.byref(st), 0))
+    assert st.value == 0
+    x = torch.arange(1024, device="cuda:0", dtype=torch.float32)
+    assert float((x * 2).sum()) == 1023.0 * 1024.0

@@ -48,6 +48,8 @@ CASES = [
     ((96, 80), ((48, 40), (24, 20)), 12, 12, (48, 40)),
     ((70, 50), ((35, 25), (17, 12)), 8, 10, (37, 23)),
     ((32, 32), ((32, 32), (8, 8)), 8, 8, (32, 32)),
+    ((1, 1), ((1, 1), (1, 1)), 8, 8, (1, 1)),   # every tap wraps onto the one texel
+    ((5, 3), ((3, 2), (1, 1)), 12, 3, (5, 3)),  # ragged, one-texel grid, 3 outputs
 ]
 
 

@@ -13,8 +13,10 @@ in libnt_b200.so.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import enum
+import functools
 import math
 import os
 
@@ -29,6 +31,23 @@ class TrainingKernelType(enum.IntEnum):
     UNCONSTRAINED = N.NT_TRAIN_UNCONSTRAINED
     BLOCK_FEATURES = N.NT_TRAIN_BLOCK_FEATURES
     FINALIZE = N.NT_TRAIN_FINALIZE
+
+
+def _device_guard(device):
+    """Make `device` current for calls into the library (its kernels launch on the current
+    device, so a material on another GPU must select its own)."""
+    if device is None or getattr(device, "type", None) != "cuda":
+        return contextlib.nullcontext()
+    import torch
+    return torch.cuda.device(device)
+
+
+def _on_device(fn):
+    @functools.wraps(fn)
+    def wrapped(self, *args, **kwargs):
+        with _device_guard(self.device):
+            return fn(self, *args, **kwargs)
+    return wrapped
 
 
 def _stream(stream) -> int | None:
@@ -183,16 +202,22 @@ class ReferenceTexture:
     the reference's descriptor (nt_reference_texture_create).  `chain` holds the levels one after
     another, [h_m][w_m][c] with c = channels (4 for 3 channels); host (numpy) or device (torch)."""
 
-    def __init__(self, chain, width: int, height: int, channels: int, num_mips: int = 1, loss_weight: float = 1.0):
-        self._chain = chain if not isinstance(chain, np.ndarray) else np.ascontiguousarray(chain, np.float32)
-        ptr = self._chain.ctypes.data if isinstance(self._chain, np.ndarray) else self._chain.data_ptr()
+    def __init__(self, chain, width: int, height: int, channels: int, num_mips: int = 1, loss_weight: float = 1.0,
+                 device=None):
+        import torch
+        host = isinstance(chain, np.ndarray)
+        data = np.ascontiguousarray(chain, np.float32) if host else chain.contiguous()
+        self.device = torch.device(device if device is not None else
+                                   ("cuda" if host else data.device))  # the texture lives on this GPU
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.desc = N.NtReferenceTexture()
-        check(load().nt_reference_texture_create(ptr, width, height, channels, num_mips, loss_weight,
-                                                 C.byref(self.desc)))
-        self._chain = None  # uploaded: the array owns a copy
+        with _device_guard(self.device):
+            check(load().nt_reference_texture_create(data.ctypes.data if host else data.data_ptr(), width, height,
+                                                     channels, num_mips, loss_weight, C.byref(self.desc)))
 
     @classmethod
-    def from_image(cls, image: np.ndarray, num_mips: int = 1, loss_weight: float = 1.0):
+    def from_image(cls, image: np.ndarray, num_mips: int = 1, loss_weight: float = 1.0, device=None):
         """From an fp32 [h][w][channels] image (1 .. 4 channels; RGB is padded with alpha 1, as
         main.cpp:547 does), its chain built with the box filter."""
         img = np.asarray(image, np.float32)
@@ -201,7 +226,7 @@ class ReferenceTexture:
         h, w, ch = img.shape
         if ch == 3:
             img = np.concatenate([img, np.ones((h, w, 1), np.float32)], axis=2)
-        return cls(box_chain_f32(img, num_mips), w, h, ch, num_mips, loss_weight)
+        return cls(box_chain_f32(img, num_mips), w, h, ch, num_mips, loss_weight, device=device)
 
     def sample(self, uv, lod: float = 0.0, stream=None):
         """SampleReferenceTextureTrilinear (train.cu:78-103) at device coordinates uv [n][2] ->
@@ -209,13 +234,15 @@ class ReferenceTexture:
         import torch
         uv = uv.contiguous()
         out = torch.empty((uv.shape[0], 4), dtype=torch.float32, device=uv.device)
-        check(load().nt_reference_texture_sample(C.byref(self.desc), uv.data_ptr(), uv.shape[0], lod, out.data_ptr(),
-                                                 _stream(stream)))
+        with _device_guard(self.device):
+            check(load().nt_reference_texture_sample(C.byref(self.desc), uv.data_ptr(), uv.shape[0], lod,
+                                                     out.data_ptr(), _stream(stream)))
         return out
 
     def close(self):
         if getattr(self, "desc", None) is not None and self.desc.texture:
-            check(load().nt_reference_texture_destroy(C.byref(self.desc)))
+            with _device_guard(self.device):
+                check(load().nt_reference_texture_destroy(C.byref(self.desc)))
 
     def __del__(self):
         try:
@@ -378,6 +405,7 @@ class NeuralTexture:
         b1 = self.b[0].float() + delta * W1[:, :2 * self.C].sum(dim=1)
         self.b[0].copy_(b1.to(torch.float16))
 
+    @_on_device
     def to_blocks(self, bias: float = 4.0, stream=None):
         """Switch from fp16 grids to BC6 block features for compression-aware fine-tuning
         (the reference's UNCONSTRAINED -> BLOCK_FEATURES schedule, main.cpp:1046-1061): each grid
@@ -392,6 +420,7 @@ class NeuralTexture:
         self.use_blocks(recs)
         self.block_bias = bias
 
+    @_on_device
     def export_bc6h(self, stream=None):
         """BC6H blocks of the block records (nt_bc6f_to_bc6h), one uint8 tensor per grid; they
         hold value + self.block_bias, as bc6h_encode(..., bias=self.block_bias) would."""
@@ -399,6 +428,7 @@ class NeuralTexture:
             raise RuntimeError("export_bc6h needs block features (call to_blocks first)")
         return [bc6f_to_bc6h(r, w, h, self.C, stream=stream) for r, (w, h) in zip(self.blocks, self.grid_sizes)]
 
+    @_on_device
     def from_bc6h(self, blocks, bias: float | None = None, stream=None):
         """Back to fp16 grids: decode BC6H blocks (value + bias) into the grids, undo the
         layer-1 shift of to_blocks and train / decode grids from here on."""
@@ -416,6 +446,7 @@ class NeuralTexture:
         self.latent_format = N.NT_LATENT_GRID_F16
 
     # -- initialisation -------------------------------------------------------------------
+    @_on_device
     def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False,
              stream=None):
         torch = self.torch
@@ -450,17 +481,20 @@ class NeuralTexture:
         lw, lh = max(self.image_w >> m, 1), max(self.image_h >> m, 1)
         return self.target_chain[off * self.cout:(off + lw * lh) * self.cout].view(lh, lw, self.cout)
 
+    @_on_device
     def build_target_mips(self, stream=None):
         """Levels 1 .. target_num_mips - 1 of the target from level 0 (nt_build_mips)."""
         check(load().nt_build_mips(self.target_chain.data_ptr(), self.image_w, self.image_h, self.cout,
                                    self.target_num_mips, _stream(stream)))
 
+    @_on_device
     def build_latent_mips(self, stream=None):
         """Latent levels 1 .. n - 1 from level 0 (box filter), e.g. after training level 0."""
         for c, (w, h), n in zip(self.grid_chains, self.grid_sizes, self.num_mips):
             check(load().nt_build_mips(c.data_ptr(), w, h, self.C, n, _stream(stream)))
 
     # -- checkpoints ------------------------------------------------------------------------------
+    @_on_device
     def save(self, path, optimizer: bool = True, latents: str = "native", bias: float = 4.0,
              target: bool = False):
         """Write the material to a checkpoint file (nt_checkpoint_write).  Sections: meta.i32 /
@@ -617,10 +651,12 @@ class NeuralTexture:
         return p
 
     # -- operations ---------------------------------------------------------------------------
+    @_on_device
     def train_step(self, stream=None, params: NtKernelParams | None = None):
         TrainStep(params or self.params(), stream)
         self.step += 1
 
+    @_on_device
     def decode(self, dtype=None, stream=None, out=None):
         torch = self.torch
         if out is None:

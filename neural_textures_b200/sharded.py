@@ -31,7 +31,7 @@ import numpy as np
 
 from . import _native as N
 from ._native import check, load
-from .api import PAD_IN, PAD_OUT, _stream, he_normal_weights, zero_padded_inputs
+from .api import PAD_IN, PAD_OUT, _device_guard, _on_device, _stream, he_normal_weights, zero_padded_inputs
 
 HALO = 3  # filter reach beyond a band: taps at -2.5 .. +1.5 rows of the band's sample range
 
@@ -132,6 +132,7 @@ class ShardedTexture:
         self.step = 0
 
     # -- initialisation: the same material as NeuralTexture.init(seed), cut to the stored rows --
+    @_on_device
     def init(self, seed: int = 0, target_seed: int | None = None, pbr_normals: bool = False, stream=None):
         torch = self.torch
         L = load()
@@ -295,9 +296,11 @@ class ShardedTexture:
         return tensors[i][b.owned:b.owned + b.halo]
 
     # -- the step ------------------------------------------------------------------------------------
+    @_on_device
     def train_pass(self, stream=None):
         check(load().nt_invoke_training(C.byref(self.train_params()), N.NT_TRAIN_UNCONSTRAINED, _stream(stream)))
 
+    @_on_device
     def adam(self, stream=None):
         check(load().nt_invoke_optimize_all(C.byref(self.adam_params()), _stream(stream)))
 
@@ -432,6 +435,11 @@ def train_step(shard: ShardedTexture, comm, stream=None):
     """One data-parallel step of the sharded material (every rank calls it).  With several
     ranks, Adam over the band interiors runs while the halo-gradient exchange and the
     network-gradient allreduce are in flight; the band edges and the network follow them."""
+    with _device_guard(shard.device):
+        _train_step(shard, comm, stream)
+
+
+def _train_step(shard, comm, stream):
     shard.train_pass(stream)
     if shard.world == 1:
         shard.adam(stream)

@@ -12,7 +12,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
-from tests.model_utils import make_texture, oracle_model, rel_l2, target_host
+from tests.model_utils import make_texture, max_rel, oracle_model, rel_l2, target_host
 
 pytestmark = pytest.mark.gpu
 
@@ -244,3 +244,22 @@ def test_full_config2_step_identities(cuda):
         rhs = db1 @ W1[:, g * 12:(g + 1) * 12]
         tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
         assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)
+
+
+def test_material_on_another_device(cuda):
+    """A material on cuda:1 trains and decodes while cuda:0 is current (the library launches on
+    the current device; the texture selects its own) and matches its twin on cuda:0."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    torch.cuda.set_device(0)
+    a = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=9, device="cuda:0")
+    b = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=9, device="cuda:1")
+    for t in (a, b):
+        t.loss_accum.zero_()
+        t.train_step()
+    assert torch.cuda.current_device() == 0
+    la, lb = a.loss_accum.item(), b.loss_accum.item()
+    assert abs(la - lb) <= 1e-5 * la
+    da, db = a.decode(dtype=torch.float32).cpu().numpy(), b.decode(dtype=torch.float32).cpu().numpy()
+    assert max_rel(db, da) <= 1e-3

@@ -233,19 +233,34 @@ __device__ __forceinline__ void window_cands(Smem<C> &s, int gi, int lane)
 
 // ---- latent-gradient column sweep (see nt_train.cu for the derivation) -------------------
 
+// Gradient buffer, size and stored row of grid g at the call's first mip level (LB false) or at
+// the second level of a fractional mip coordinate (LB true; such calls are unsharded).
+template <bool LB>
+__device__ __forceinline__ float *lvl_grad(const TrainLaunch &p, int g) { return LB ? p.ggrid_b[g] : p.ggrid[g]; }
+template <bool LB>
+__device__ __forceinline__ int lvl_w(const TrainLaunch &p, int g) { return LB ? p.gw_b[g] : p.gw[g]; }
+template <bool LB>
+__device__ __forceinline__ int lvl_h(const TrainLaunch &p, int g) { return LB ? p.gh_b[g] : p.gh[g]; }
+template <bool LB>
+__device__ __forceinline__ int lvl_row(const TrainLaunch &p, int g, int row, int h)
+{
+    if constexpr (LB) return wrap_coord(row, h);
+    return stored_row(p, g, row, h);
+}
+
 // Latent gradient sum of one texel (x 1 / num_samples) into the grid gradients, or, for block
 // features, through the BC6 backward into the texel's block records (train.cu:436-454; the
 // backward is linear in the feature gradient, so summing a texel's taps first is exact).
-template <int C, bool BLK>
+template <int C, bool BLK, bool LB = false>
 __device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, int ty, const float (&row)[C])
 {
     bool any = false;
 #pragma unroll
     for (int c = 0; c < C; ++c) any |= row[c] != 0.f;
     if (!any) return;
-    const int gw = p.gw[gi], gh = p.gh[gi];
+    const int gw = lvl_w<LB>(p, gi), gh = lvl_h<LB>(p, gi);
     const float sc = p.inv_num_samples;
-    const int sy = stored_row(p, gi, ty, gh);
+    const int sy = lvl_row<LB>(p, gi, ty, gh);
     if (sy < 0) return;
     if constexpr (BLK) {
         float fg[C];
@@ -254,13 +269,13 @@ __device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, 
         bc6f_backward_texel<C>(reinterpret_cast<const float *>(p.grid[gi]), p.ggrid[gi], gw, wrap_coord(tx, gw), sy, fg);
         return;
     }
-    float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)sy * gw + wrap_coord(tx, gw)) * C);
+    float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, gi) + ((size_t)sy * gw + wrap_coord(tx, gw)) * C);
 #pragma unroll
     for (int q = 0; q < C / 4; ++q)
         atomicAdd(dst + q, make_float4(row[4 * q] * sc, row[4 * q + 1] * sc, row[4 * q + 2] * sc, row[4 * q + 3] * sc));
 }
 
-template <int C, int L, bool BLK>
+template <int C, int L, bool BLK, bool LB = false>
 __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p, int r)
 {
     constexpr int kRows = 2, kChunks = kTileH / kRows, DXS = Cfg<C>::DXS;
@@ -290,7 +305,7 @@ __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p,
             const int fy = rmin - 1;
             if (fy_cur == INT_MIN) fy_cur = fy;
             while (fy > fy_cur) {
-                flush_row<C, BLK>(p, gi, tx, fy_cur, R[0]);
+                flush_row<C, BLK, LB>(p, gi, tx, fy_cur, R[0]);
 #pragma unroll
                 for (int m = 0; m < 4; ++m)
 #pragma unroll
@@ -329,21 +344,21 @@ __device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p,
         }
         if (fy_cur == INT_MIN) continue;
 #pragma unroll
-        for (int m = 0; m < 5; ++m) flush_row<C, BLK>(p, gi, tx, fy_cur + m, R[m]);
+        for (int m = 0; m < 5; ++m) flush_row<C, BLK, LB>(p, gi, tx, fy_cur + m, R[m]);
     }
 }
 
 // Per-sample, per-tap vector atomics (windows the sweep does not handle); block features
 // take the BC6 backward per tap.
-template <int C, bool BLK>
+template <int C, bool BLK, bool LB = false>
 __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLaunch &p, int gi, int r)
 {
     const float *dxr = reinterpret_cast<const float *>(s.t.m.H2) + r * Cfg<C>::DXS + gi * C;
-    const int gw = p.gw[gi], gh = p.gh[gi];
+    const int gw = lvl_w<LB>(p, gi), gh = lvl_h<LB>(p, gi);
     const short2 b = s.base[gi][r];
     const float scale = p.inv_num_samples;
     for (int j = 0; j < 4; ++j) {
-        const int yy = stored_row(p, gi, b.y - 1 + j, gh);
+        const int yy = lvl_row<LB>(p, gi, b.y - 1 + j, gh);
         if (yy < 0) continue;
         for (int i = 0; i < 4; ++i) {
             const int xx = wrap_coord(b.x - 1 + i, gw);
@@ -356,7 +371,7 @@ __device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLau
                 continue;
             }
             const float wgt = s.wts[gi][r][i] * s.wts[gi][r][4 + j] * scale;
-            float4 *dst = reinterpret_cast<float4 *>(p.ggrid[gi] + ((size_t)yy * gw + xx) * C);
+            float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, gi) + ((size_t)yy * gw + xx) * C);
 #pragma unroll
             for (int q = 0; q < C / 4; ++q)
                 atomicAdd(dst + q, make_float4(wgt * dxr[4 * q], wgt * dxr[4 * q + 1], wgt * dxr[4 * q + 2],
@@ -499,7 +514,7 @@ __device__ __forceinline__ void scatter_reduce_blocks(const Smem<C> &s, const Tr
 
 // Staged window sums -> global latent gradients (x 1 / num_samples), one float4 reduction
 // per 4 channels of every window texel.
-template <int C>
+template <int C, bool LB = false>
 __device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaunch &p, int tid)
 {
     constexpr int n0 = sc_h(0) * sc_w(0) * 2, n1 = sc_h(1) * sc_w(1) * 2;  // (row, column, quad) slots
@@ -518,10 +533,10 @@ __device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaun
         const float *src = (g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * 8 : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * 8) + 4 * q;
         const float4 v = *reinterpret_cast<const float4 *>(src);
         if (v.x == 0.f && v.y == 0.f && v.z == 0.f && v.w == 0.f) continue;
-        const int gw = p.gw[g], gh = p.gh[g];
-        const int sy = stored_row(p, g, W.y0 + y, gh);
+        const int gw = lvl_w<LB>(p, g), gh = lvl_h<LB>(p, g);
+        const int sy = lvl_row<LB>(p, g, W.y0 + y, gh);
         if (sy < 0) continue;
-        float4 *dst = reinterpret_cast<float4 *>(p.ggrid[g] + ((size_t)sy * gw + wrap_coord(W.x0 + x, gw)) * C) + q;
+        float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, g) + ((size_t)sy * gw + wrap_coord(W.x0 + x, gw)) * C) + q;
         atomicAdd(dst, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc));
     }
 }
@@ -660,6 +675,70 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
     ph ^= 1u;
     umma::fence_after();
     return true;
+}
+
+// ---- second mip level of a fractional mip coordinate (MIP) ---------------------------------
+//
+// After the first level's scatter, each sample's footprint in the second level replaces the
+// first level's in shared memory, the tile's windows are rebuilt from it, and the same scatter
+// (tensor-core or column sweep) runs on the second level's gradients with the weight-t share of
+// dX.  A grid whose t is 0 (its chain ended) contributes nothing.  Returns false when a stage
+// failed (the caller leaves the tile loop).
+template <int C>
+__device__ bool scatter_second_level(Smem<C> &s, const TrainLaunch &p, const Descs<C> &d, uint32_t tmem, bool &first,
+                                     uint32_t done, uint32_t dwdone, uint32_t &ph, bool &failed, int tid, int warp,
+                                     int lane, int r, int half, int ix, int iy, bool sample_valid, const float (&dxo)[C])
+{
+    using K = Cfg<C>;
+    const float t = p.mip_t[half];
+    const bool valid = sample_valid && t > 0.f;
+    float dxb[C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) dxb[k] = valid ? __fmul_rn(dxo[k], t) : 0.f;
+    {
+        float u = 0.f, v = 0.f;
+        if (valid) sample_uv(p.sampler, ix, iy, u, v);
+        Footprint fb;
+        footprint(u, v, max(p.gw_b[half], 1), max(p.gh_b[half], 1), fb);
+        s.base[half][r] = make_short2((short)fb.bx, (short)fb.by);
+        float4 *wr = reinterpret_cast<float4 *>(s.wts[half][r]);
+        wr[0] = make_float4(fb.wx[0], fb.wx[1], fb.wx[2], fb.wx[3]);
+        wr[1] = make_float4(fb.wy[0], fb.wy[1], fb.wy[2], fb.wy[3]);
+        extents_partial(s.part[half], fb.bx, fb.by, valid, warp & 3, lane);
+    }
+    if (__syncthreads_or(failed)) return false;
+    if (warp < 2) finalize_window_tc<C>(s, warp, lane);
+    if (__syncthreads_or(failed)) return false;
+    bool tc = false;
+    if constexpr (C == 8) tc = (s.win[0].tc || s.win[0].w == 0) && (s.win[1].tc || s.win[1].w == 0);
+    if (tc) {
+        if constexpr (C == 8) {
+            if (half) scatter_rows<C, 1>(s, r, valid, dxb);
+            else scatter_rows<C, 0>(s, r, valid, dxb);
+        }
+        if (!run_stage<C>(6, d, tmem, first, done, dwdone, ph, failed, tid)) return false;
+        scatter_stage_out<C>(s, tmem, warp, lane, half);
+        if (__syncthreads_or(failed)) return false;
+        scatter_reduce<C, true>(s, p, tid);
+    } else {
+        float *dxr = reinterpret_cast<float *>(s.t.m.H2) + r * K::DXS + half * C;
+#pragma unroll
+        for (int q = 0; q < C / 4; ++q)
+            *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(dxb[4 * q], dxb[4 * q + 1], dxb[4 * q + 2], dxb[4 * q + 3]);
+        if (warp < 2) window_cands<C>(s, warp, lane);
+        if (__syncthreads_or(failed)) return false;
+        const bool both = s.win[0].ok && s.win[1].ok;
+        const int span = max(s.win[0].span, s.win[1].span);
+        if (both && span <= 5) {
+            sweep_tc<C, 5, false, true>(s, p, tid);
+        } else if (both && span <= 10) {
+            sweep_tc<C, 10, false, true>(s, p, tid);
+        } else if (valid) {
+            scatter_taps_tc<C, false, true>(s, p, half, r);
+        }
+    }
+    umma::fence_before();
+    return !__syncthreads_or(failed);  // the next tile (or pass) overwrites the footprints and windows
 }
 
 // ---- block-feature gather through a decoded window ----------------------------------------
@@ -971,6 +1050,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             atomicOr(&g_device_status, 1u);
         }
         dph ^= 1u;
+        float dxo[C];  // MIP: dX of grid `half` before the split between the two levels
         if (!p.finalize) {
             // dX columns [half * C, half * C + C): the latents of grid `half`
             float dxv[C];
@@ -983,29 +1063,11 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 for (int e = 0; e < C; ++e) dxv[e] = __uint_as_float(half ? v[C + e] : v[e]);
             }
             if constexpr (MIP) {
+#pragma unroll
+                for (int k = 0; k < C; ++k) dxo[k] = dxv[k];
                 const float t = p.mip_t[half];
-                if (t > 0.f) {
-                    if (valid) {  // level m1 of grid `half`: per-tap atomics at weight t
-                        float u = 0.f, v = 0.f;
-                        sample_uv(p.sampler, ix, iy, u, v);
-                        Footprint fb;
-                        footprint(u, v, p.gw_b[half], p.gh_b[half], fb);
-                        float db[C];
-#pragma unroll
-                        for (int k = 0; k < C; ++k) db[k] = __fmul_rn(dxv[k], t);
-                        for (int j = 0; j < 4; ++j) {
-                            for (int i = 0; i < 4; ++i) {
-                                const float wgt = fb.wx[i] * fb.wy[j] * p.inv_num_samples;
-                                float4 *dst = reinterpret_cast<float4 *>(
-                                    p.ggrid_b[half] + ((size_t)fb.ys[j] * p.gw_b[half] + fb.xs[i]) * C);
-#pragma unroll
-                                for (int q = 0; q < C / 4; ++q)
-                                    atomicAdd(dst + q, make_float4(wgt * db[4 * q], wgt * db[4 * q + 1],
-                                                                   wgt * db[4 * q + 2], wgt * db[4 * q + 3]));
-                            }
-                        }
-                    }
-                    const float omt = __fsub_rn(1.f, t);  // level m0 takes the usual scatter
+                if (t > 0.f) {  // level m0 takes weight 1 - t here, level m1 weight t after it
+                    const float omt = __fsub_rn(1.f, t);
 #pragma unroll
                     for (int k = 0; k < C; ++k) dxv[k] = __fmul_rn(dxv[k], omt);
                 }
@@ -1032,6 +1094,14 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 if (__syncthreads_or(failed)) {
                     failed = true;
                     break;
+                }
+                if constexpr (MIP) {
+                    if ((p.mip_t[0] > 0.f || p.mip_t[1] > 0.f) &&
+                        !scatter_second_level<C>(s, p, d, tmem, first, done, dwdone, ph, failed, tid, warp, lane, r,
+                                                 half, ix, iy, valid, dxo)) {
+                        failed = true;
+                        break;
+                    }
                 }
                 continue;
             }
@@ -1060,6 +1130,14 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         if (__syncthreads_or(failed)) {
             failed = true;
             break;
+        }
+        if constexpr (MIP) {
+            if (!p.finalize && (p.mip_t[0] > 0.f || p.mip_t[1] > 0.f) &&
+                !scatter_second_level<C>(s, p, d, tmem, first, done, dwdone, ph, failed, tid, warp, lane, r, half, ix,
+                                         iy, valid, dxo)) {
+                failed = true;
+                break;
+            }
         }
     }
 

@@ -81,16 +81,14 @@ __device__ __forceinline__ void relu_store32(uint32_t taddr, uint8_t *H, int r, 
     umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
     umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
     umma::wait_ld();
-    const __half2 zero = __float2half2_rn(0.f);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         uint32_t h[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const __half2 x = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
-            const __half2 y = __hmax2(x, zero);
-            h[e] = *reinterpret_cast<const uint32_t *>(&y);
-        }
+        for (int e = 0; e < 4; ++e)  // cvt.rn.relu: both lanes rounded to fp16, negatives to 0, in one step
+            asm("cvt.rn.relu.f16x2.f32 %0, %1, %2;"
+                : "=r"(h[e])
+                : "f"(__uint_as_float(v[8 * q + 2 * e + 1])), "f"(__uint_as_float(v[8 * q + 2 * e])));
         st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
     }
 }

@@ -5,9 +5,11 @@
 // latent grids, positional features, the 32 -> 64 -> 64 -> cout network, fp16 (or fp32)
 // outputs and an optional squared error against a target.
 //
-// A CTA of 8 warps owns one 16 x 8 texel tile (M = 128, texel r = TMEM lane r) at a time;
-// two CTAs share an SM.  The two threads of a texel split the gather (grid 0 / grid 1 and
-// the positional features) and the epilogue columns.  Per tile:
+// A CTA of 4 warps owns one 16 x 8 texel tile (M = 128, texel r = TMEM lane r, one thread per
+// texel) at a time; four CTAs share an SM (a fifth measured 37% slower: its shared memory
+// leaves the gathers too little L1).  With NT_DEC_SPLIT=2 a CTA has 8 warps and the two
+// threads of a texel split the gather (grid 0 / grid 1 and the positional features) and the
+// epilogue columns.  Per tile:
 //     gather -> F1 -> E1 -> F2 -> E2 -> F3 -> outputs
 // with the products of nt_train_tc.cu's forward half (biases folded in as a constant-1
 // input column; H2 overwrites H1, whose last reader is F2).  Every wait is bounded.

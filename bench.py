@@ -431,6 +431,32 @@ def run_reftex(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank)
     return out
 
 
+def run_tensor_peak_check(n=8192, reps=10):
+    """The training and decode products are fp16 x fp16 with fp32 accumulation, while the
+    tensor peak is measured with a bf16 GEMM.  Time one library GEMM of each type at the same
+    shape (best of `reps`, CUDA events) to show the two rates agree."""
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    out = {"check": "tensor peak, fp16 vs bf16 (torch.matmul, fp32 accumulate)", "shape": [n, n, n]}
+    for name, dt in (("bf16", torch.bfloat16), ("fp16", torch.float16)):
+        a = torch.randn(n, n, device=dev).to(dt)
+        b = torch.randn(n, n, device=dev).to(dt)
+        for _ in range(3):
+            torch.matmul(a, b)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch.matmul(a, b)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1))
+        out[name + "_tflops"] = 2.0 * n ** 3 / (best * 1e-3) / 1e12
+    out["fp16_over_bf16"] = out["fp16_tflops"] / out["bf16_tflops"]
+    print(json.dumps(out))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -445,7 +471,11 @@ def main():
     ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
     ap.add_argument("--mip-steps", type=int, default=50, help="timed steps at a fractional mip coordinate (0: skip)")
     ap.add_argument("--texture-steps", type=int, default=50, help="timed steps with reference-texture targets (0: skip)")
+    ap.add_argument("--tensor-peak-check", action="store_true",
+                    help="only time torch fp16 and bf16 matmuls (fp32 accumulate) and print one JSON line")
     args = ap.parse_args()
+    if args.tensor_peak_check:
+        return run_tensor_peak_check()
     if args.impl == "reference":
         return run_reference(args)
 

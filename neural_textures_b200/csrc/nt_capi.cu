@@ -22,18 +22,21 @@ namespace nt {
 static std::atomic<uint64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+// SM count of the current device, cached per device (host threads may drive devices
+// concurrently: the cache is atomic, and a race only repeats the same query).
 int sm_count()
 {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
-    if (!cached[dev]) {
-        int n = 0;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (!n) {
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cached[dev] = n > 0 ? n : 148;
+        n = n > 0 ? n : 148;
+        cached[dev].store(n, std::memory_order_relaxed);
     }
-    return cached[dev];
+    return n;
 }
 
 cudaError_t set_smem_limit(const void *kernel, size_t bytes)

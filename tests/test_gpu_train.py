@@ -8,6 +8,7 @@
   sum_i db1[i] W1[i][k]; gradients finite; loss finite).
 """
 import ctypes as C
+import os
 
 import numpy as np
 import pytest
@@ -160,11 +161,14 @@ def test_separate_optimizers_equal_fused(cuda):
 
 
 def test_multi_step_loss_matches_oracle(cuda, oracle):
-    """Run 2,000 steps on both sides with identical sampling; compare the mean loss of the last
-    10 steps (2% tolerance: the criterion is the loss after 2,000 steps) and the loss decrease."""
+    """Run 2,000 steps on both sides with identical sampling; compare the loss level at step
+    2,000 (2% tolerance: the criterion is the loss after 2,000 steps) and the loss decrease.
+    The level is the mean over steps 1,900-1,999 at 4,096 samples per step: single-step losses
+    swing by tens of percent with the jitter of the step's samples, and the two trajectories,
+    which differ in fp32 summation order, put those swings on different steps."""
     import torch
     n_steps = 2000
-    tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=12)
+    tex = make_texture((128, 128), ((64, 64), (32, 32)), 8, 8, lattice=(64, 64), seed=12)
     model_grids, model_W, model_b = tex.host_model()
     tgt = target_host(tex)
     losses_gpu = []
@@ -185,8 +189,8 @@ def test_multi_step_loss_matches_oracle(cuda, oracle):
     losses_ref = []
     for step in range(n_steps):
         model = oracle.OracleModel(channels=8, cout=8, grids=grids, W=W, b=b)
-        s = oracle.make_sampler(64, 64, 32, 32, step=step)
-        sse, gW, gb, gg = oracle.train_pass(model, tgt, s, threads=8)
+        s = oracle.make_sampler(128, 128, 64, 64, step=step)
+        sse, gW, gb, gg = oracle.train_pass(model, tgt, s, threads=min(os.cpu_count() or 1, 16))
         losses_ref.append(sse)
         for l in range(3):
             oracle.adam_f16(W[l], gW[l], mW[l], vW[l], lr_n, b1, b2, eps, step)
@@ -195,7 +199,9 @@ def test_multi_step_loss_matches_oracle(cuda, oracle):
             flat = grids[gi].reshape(-1)
             oracle.adam_f16(flat, gg[gi].reshape(-1), mg[gi].reshape(-1), vg[gi].reshape(-1), lr_l, b1, b2, eps,
                             step)
-    lg, lr_ = np.mean(losses_gpu[-10:]), np.mean(losses_ref[-10:])
+    for n in (10, 100, 200):
+        print(f"last {n} steps: gpu {np.mean(losses_gpu[-n:]):.4f} oracle {np.mean(losses_ref[-n:]):.4f}")
+    lg, lr_ = np.mean(losses_gpu[-100:]), np.mean(losses_ref[-100:])
     assert lg < 0.5 * losses_gpu[0], "training must reduce the loss"
     assert abs(lg - lr_) <= 0.02 * lr_, (lg, lr_)
 

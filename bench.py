@@ -431,6 +431,51 @@ def run_reftex(torch, dev, stream, L, nt, _native, scratch, steps, warmup, rank)
     return out
 
 
+def run_config4b_dist(n_dev, steps=20, warmup=10):
+    """Config 4b through the C ABI's one-thread sharded step (nt_dist_train_step): one process,
+    one band per visible device (n_dev of them), exchanges by kernels that read the
+    neighbouring devices' memory, phases ordered by events.  Timed with CUDA events on every
+    device; the step time is the max over devices.  Prints one JSON line."""
+    import torch
+    from neural_textures_b200 import _native
+    from neural_textures_b200.sharded import ShardedTexture, dist_train_step
+    devs = [torch.device("cuda", d) for d in range(n_dev)]
+    sh = [ShardedTexture(r, n_dev, *CFG4B["image"], CFG4B["grids"], CFG4B["C"], CFG4B["cout"], CFG4B["lattice"],
+                         device=devs[r]) for r in range(n_dev)]
+    for s in sh:
+        s.init(seed=11)
+    for _ in range(warmup):
+        dist_train_step(sh)
+    for d in devs:
+        torch.cuda.synchronize(d)
+    ev = []
+    for d in devs:
+        with torch.cuda.device(d):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ev.append((e0, e1))
+    launches0 = _native.load().nt_launch_count()
+    for _ in range(steps):
+        dist_train_step(sh)
+    for d, (e0, e1) in zip(devs, ev):
+        with torch.cuda.device(d):
+            e1.record()
+    for d in devs:
+        torch.cuda.synchronize(d)
+    launches = _native.load().nt_launch_count() - launches0
+    t = max(e0.elapsed_time(e1) for e0, e1 in ev) / steps
+    B = CFG4B["lattice"][0] * CFG4B["lattice"][1]
+    print(json.dumps({"metric": "config 4b train samples/s (fwd+bwd+Adam), one host thread", "value": B / (t * 1e-3),
+                      "unit": "samples/s", "n_gpus": n_dev, "steps": steps, "warmup": warmup, "ms_per_step": t,
+                      "higher_is_better": True, "scaling": "strong", "dtype": "f16 operands, f32 accumulate",
+                      "data": "synthetic", "gpu_launches": launches,
+                      "config": {"workload": CFG4B["workload"], "global_batch": B,
+                                 "latents": "4096^2x12 + 2048^2x12 fp16, row bands per device", "mlp": "32-64-64-12",
+                                 "parallelism": f"row shards x{n_dev}: nt_dist_train_step (peer-memory exchange "
+                                                "kernels, event-ordered phases)",
+                                 "l2": "state per device far above L2 (no flush)"}}))
+
+
 def run_tensor_peak_check(n=8192, reps=10):
     """The training and decode products are fp16 x fp16 with fp32 accumulation, while the
     tensor peak is measured with a bf16 GEMM.  Time one library GEMM of each type at the same
@@ -471,11 +516,15 @@ def main():
     ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
     ap.add_argument("--mip-steps", type=int, default=50, help="timed steps at a fractional mip coordinate (0: skip)")
     ap.add_argument("--texture-steps", type=int, default=50, help="timed steps with reference-texture targets (0: skip)")
+    ap.add_argument("--dist-devices", type=int, default=0,
+                    help="only time config 4b through nt_dist_train_step over this many devices (one process)")
     ap.add_argument("--tensor-peak-check", action="store_true",
                     help="only time torch fp16 and bf16 matmuls (fp32 accumulate) and print one JSON line")
     args = ap.parse_args()
     if args.tensor_peak_check:
         return run_tensor_peak_check()
+    if args.dist_devices > 0:
+        return run_config4b_dist(args.dist_devices, steps=max(args.steps // 10, 5), warmup=max(args.warmup // 2, 3))
     if args.impl == "reference":
         return run_reference(args)
 

@@ -373,6 +373,46 @@ NT_API nt_status nt_bc6f_from_bc6h(const void *blocks, int32_t width, int32_t he
 NT_API nt_status nt_bc6f_to_bc6h(const float *records, int32_t width, int32_t height, int32_t channels,
                                  void *blocks, nt_stream_t stream);
 
+/* ---- row-sharded training from one host thread (no reference counterpart) -----------------
+ *
+ * The reference trains one material on one device (main.cpp:1071-1077).  A material split
+ * into bands of lattice rows, one band per shard, trains here with one call per step; the
+ * shards may share a device or sit on several.  Shard r of n stores, for each latent grid,
+ * `halo_rows` rows above its owned band, the band, and `halo_rows` rows below (its training
+ * pass reads and accumulates into all of them); shard r + 1's band follows shard r's, and
+ * shard 0's follows shard n - 1's (the grids wrap).  A step is:
+ *   1. every shard's training pass (nt_invoke_training with its params);
+ *   2. per shard, one kernel that reads its neighbours' memory: the gradients they left in
+ *      their halo rows are added to this shard's band edges, and Adam updates this shard's
+ *      copy of the network with the sum, in shard order, of every shard's network gradients
+ *      (so the copies stay bit-identical); then Adam over the owned band (zero-skip and
+ *      gradient zeroing as nt_invoke_optimize_features);
+ *   3. per shard, one kernel that copies the neighbours' updated band edges into its halo
+ *      rows and zeroes its halo and network gradients.
+ * The phases are ordered by events between the shards' streams; no kernel waits on another
+ * device.  Shards on different devices need peer access between them, which the call enables
+ * (NT_ERR_CUDA if the devices cannot reach each other).  Every shard's buffers must be on its
+ * device.  As with nt_train_step the caller advances params.step (main.cpp:1077); all shards
+ * must carry the same step, network Adam constants and network shape. */
+#define NT_DIST_MAX_SHARDS 16
+typedef struct NtShard {
+    NtKernelParams params;  /* the band's training pass: lattice_row0 / lattice_rows, and per source
+                             * row_origin / stored_rows, as for nt_invoke_training */
+    int32_t halo_rows[NT_NUM_FEATURES]; /* per latent grid: stored_rows = owned + 2 * halo_rows */
+    int32_t device;         /* CUDA device holding the shard's buffers */
+    nt_stream_t stream;     /* a stream on that device (NULL: its default stream) */
+} NtShard;
+
+/* The band split used for shards: lattice rows [rank * H / world, (rank + 1) * H / world) of
+ * an H-row lattice reach rows [lo, hi) of a source of `height` rows (the range scaled and
+ * rounded to the nearest row, so consecutive ranks partition the source).  NT_ERR_INVALID_ARG
+ * if a band would be thinner than `halo` rows or its stored rows taller than the source. */
+NT_API nt_status nt_dist_band(int32_t rank, int32_t world, int32_t lattice_height, int32_t height, int32_t halo,
+                              int32_t *lo, int32_t *hi);
+/* One training step of a row-sharded material (count 1 .. NT_DIST_MAX_SHARDS; count 1 is
+ * nt_train_step).  Returns once every phase is queued; the current device is restored. */
+NT_API nt_status nt_dist_train_step(const NtShard *shards, int32_t count);
+
 /* ---- tensor-core self-test (no reference counterpart) ---------------------------------- */
 
 /* Runs the tcgen05 operand layouts of the fused kernels on small known matrices (device

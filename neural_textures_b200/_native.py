@@ -101,6 +101,14 @@ class NtKernelParams(C.Structure):
     ]
 
 
+NT_DIST_MAX_SHARDS = 16
+
+
+class NtShard(C.Structure):
+    _fields_ = [("params", NtKernelParams), ("halo_rows", C.c_int32 * NT_NUM_FEATURES), ("device", C.c_int32),
+                ("stream", C.c_void_p)]
+
+
 class NtBc6hSurface(C.Structure):
     _fields_ = [("data", C.c_void_p), ("width", C.c_int32), ("height", C.c_int32), ("channels", C.c_int32),
                 ("channel_stride", C.c_int64), ("row_stride", C.c_int64), ("texel_stride", C.c_int64)]
@@ -121,6 +129,8 @@ SIGNATURES = {
     "nt_invoke_optimize_all": (C.c_int, [_P, C.c_void_p]),
     "nt_invoke_inference": (C.c_int, [_P, C.c_void_p]),
     "nt_train_step": (C.c_int, [_P, C.c_void_p]),
+    "nt_dist_band": (C.c_int, [C.c_int32] * 5 + [C.POINTER(C.c_int32)] * 2),
+    "nt_dist_train_step": (C.c_int, [C.POINTER(NtShard), C.c_int32]),
     "nt_run_forward_pass_test": (C.c_int32, []),
     "nt_forward_pass_12x16x16": (C.c_int, [C.c_void_p] * 6 + [C.c_void_p]),
     "nt_generate_target": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_uint32,

@@ -9,19 +9,14 @@
 // 16-byte vector accesses.  The float operations are written out with explicit rounding in
 // the order of the reference expression so the result is bit-identical to the CPU oracle;
 // the bias corrections 1 - beta^t are computed once per step on the host.
+#include "nt_adam_math.cuh"
 #include "nt_kernels.cuh"
 
 namespace nt {
 
 __device__ __forceinline__ float adam_one(float w, float g, float &m, float &v, const AdamSegment &s)
 {
-    const float m1 = __fadd_rn(__fmul_rn(s.beta1, m), __fmul_rn(__fsub_rn(1.f, s.beta1), g));
-    const float m2 = __fadd_rn(__fmul_rn(s.beta2, v), __fmul_rn(__fmul_rn(__fsub_rn(1.f, s.beta2), g), g));
-    m = m1;
-    v = m2;
-    const float mhat = __fdiv_rn(m1, s.bc1);
-    const float vhat = __fdiv_rn(m2, s.bc2);
-    return __fsub_rn(w, __fdiv_rn(__fmul_rn(s.lr, mhat), __fadd_rn(__fsqrt_rn(vhat), s.eps)));
+    return adam_update(w, g, m, v, s.lr, s.beta1, s.beta2, s.eps, s.bc1, s.bc2);
 }
 
 constexpr int kAdamThreads = 256;

@@ -511,3 +511,26 @@ class LocalShards:
     def gather(self, tensors_of, i: int):
         """Full-height tensor of grid i assembled from the owned bands."""
         return self.shards[0].torch.cat([s.band_view(tensors_of(s), i) for s in self.shards], 0)
+
+
+def dist_train_step(shards: list[ShardedTexture], streams=None):
+    """One step of every shard of a material, driven from this thread through
+    nt_dist_train_step: the training passes, then per shard one kernel that adds the
+    neighbours' halo gradients to its band edges and runs Adam on the network with the sum
+    of all shards' network gradients (read from their memory), Adam over the band, and one
+    kernel that refreshes its halo rows from the neighbours' updated bands.  The shards may
+    share a device or sit on several; `streams` (one per shard) defaults to each device's
+    current stream."""
+    torch = shards[0].torch
+    n = len(shards)
+    arr = (N.NtShard * n)()
+    for r, s in enumerate(shards):
+        arr[r].params = s.train_params()
+        for i in range(2):
+            arr[r].halo_rows[i] = s.bands[i].halo
+        dev = s.device.index if s.device.index is not None else torch.cuda.current_device()
+        arr[r].device = dev
+        arr[r].stream = (streams[r] if streams is not None else torch.cuda.current_stream(dev).cuda_stream)
+    check(load().nt_dist_train_step(arr, n))
+    for s in shards:
+        s.step += 1

@@ -74,14 +74,19 @@ def _compare(ref, got):
     assert abs(loss_got - loss_ref) <= 1e-3 * loss_ref
 
 
-def _run(case, world, ref_devices, got_devices, seed):
+def _run(case, world, ref_devices, got_devices, seed, own_streams=False):
     import torch
     from neural_textures_b200.sharded import LocalShards, dist_train_step
     ref = LocalShards(_make(case, world, seed, ref_devices))
     got = _make(case, world, seed, got_devices)
+    streams = None
+    if own_streams:  # one stream per shard: only the events order the phases across shards
+        torch.cuda.synchronize()
+        held = [torch.cuda.Stream(device=s.device) for s in got]
+        streams = [st.cuda_stream for st in held]
     for _ in range(STEPS):
         ref.step()
-        dist_train_step(got)
+        dist_train_step(got, streams)
     for d in set(ref_devices) | set(got_devices):
         torch.cuda.synchronize(d)
     assert _status(sorted(set(got_devices))) == 0
@@ -92,6 +97,13 @@ def _run(case, world, ref_devices, got_devices, seed):
 @pytest.mark.parametrize("case", range(len(CASES)))
 def test_dist_step_matches_local_shards(cuda, world, case):
     _run(case, world, ["cuda:0"], ["cuda:0"], seed=7)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_dist_step_with_a_stream_per_shard(cuda, world):
+    """Shards on one GPU, each on its own stream: the phases are ordered only by the events
+    between the streams."""
+    _run(0, world, ["cuda:0"], ["cuda:0"], seed=11, own_streams=True)
 
 
 @pytest.mark.parametrize("world", [2, 4])

@@ -259,6 +259,11 @@ nt_status validate_shards(const NtShard *sh, int n)
         DIST_REQUIRE(p.latent_channels == p0.latent_channels && p.output_channels == p0.output_channels,
                      "shard %d: network shape differs from shard 0", r);
         DIST_REQUIRE(p.step == p0.step, "shard %d: step %d differs from shard 0's %d", r, p.step, p0.step);
+        DIST_REQUIRE(p.num_samples == p0.num_samples && p.lattice_width == p0.lattice_width &&
+                         p.lattice_height == p0.lattice_height && p.image_width == p0.image_width &&
+                         p.image_height == p0.image_height,
+                     "shard %d: image, lattice or num_samples differs from shard 0 (every band scales its "
+                     "gradients by the whole material's sample count)", r);
         DIST_REQUIRE(!memcmp(&p.network_adam, &p0.network_adam, sizeof p.network_adam),
                      "shard %d: network Adam constants differ from shard 0", r);
         DIST_REQUIRE(sh[r].device >= 0, "shard %d: device %d", r, sh[r].device);

@@ -75,6 +75,11 @@ def test_dist_step_rejects_bad_sets(native):
     assert native.nt_dist_train_step(bad, 3) != 0
     assert b"does not start where" in native.nt_get_last_error_string()
 
+    bad = _shard_set(3)
+    bad[2].params.num_samples = 5
+    assert native.nt_dist_train_step(bad, 3) != 0
+    assert b"num_samples" in native.nt_get_last_error_string()
+
     bad = _shard_set(2)
     bad[1].halo_rows[1] = 2
     assert native.nt_dist_train_step(bad, 2) != 0

@@ -36,6 +36,11 @@ CFG1 = dict(workload="config1_train_1024sq_8ch", image=(1024, 1024), grids=((512
             cout=8, lattice=(512, 512))
 CFG0 = dict(workload="config0_decode_1024sq_8ch", image=(1024, 1024), grids=((512, 512), (256, 256)), C=8,
             cout=8)
+CFG2 = dict(workload="config2_train_4096sq_pbr_12ch", image=(4096, 4096), grids=((1024, 1024), (512, 512)), C=12,
+            cout=12, lattice=(1024, 1024))
+# 2048^2 materials with config 2's texel / latent ratio (4:1 and 8:1) and 12 latent channels
+CFG4A = dict(workload="config4a_8x_2048sq_10ch_per_gpu", image=(2048, 2048), grids=((512, 512), (256, 256)), C=12,
+             cout=10, lattice=(1024, 512), materials_per_gpu=8)
 CFG4B = dict(workload="config4b_sharded_16384sq_12ch", image=(16384, 16384), grids=((4096, 4096), (2048, 2048)),
              C=12, cout=12, lattice=(2048, 2048))
 L2_FLUSH_BYTES = 256 << 20
@@ -43,6 +48,20 @@ L2_FLUSH_BYTES = 256 << 20
 # algorithmic work per unit (basis of roofline.achieved)
 MLP_FLOP_FWD = 2 * (32 * 64 + 64 * 64 + 64 * 8)          # 13,312 per texel / sample
 MLP_FLOP_TRAIN = 3 * MLP_FLOP_FWD                         # fwd + dX + dW = 39,936 per sample
+HEADLINE_METRIC = "train samples/s (fwd+bwd+Adam), config 1"
+E2E_MATERIALS = 4  # config-1 materials the e2e loop rotates over: 4 x 51 MB of state > 126 MB L2
+
+
+def mlp_flop_train(cout):
+    return 3 * 2 * (32 * 64 + 64 * 64 + 64 * cout)
+
+
+def step_bytes(grids, C, batch, cout):
+    """Algorithmic HBM bytes of one training step: 30 B per latent parameter (gather read 2,
+    gradient write 4, Adam reads w 2 g 4 m 4 v 4 and writes w 2 m 4 v 4) + the batch's
+    target reads (2 B per channel)."""
+    P = sum(w * h for (w, h) in grids) * C
+    return 30 * P + batch * cout * 2
 
 
 def peaks():
@@ -171,6 +190,43 @@ def cpu_train_baseline(O, seconds=12.0):
                       f"+ one Adam pass over all {P} latent params; step time extrapolated to the full batch"}
 
 
+def cpu_decode_baseline(O, seconds=10.0):
+    """Oracle (CPU port of the reference's forward pass: Catmull-Rom latent sampling, the
+    32-64-64-8 MLP, train.cu:917-961) decoding a bounded run of config-0 texels on all host
+    cores."""
+    import numpy as np
+    from neural_textures_b200.api import he_normal_weights, zero_padded_inputs
+    threads = os.cpu_count() or 1
+    C, cout = CFG0["C"], CFG0["cout"]
+    rng = np.random.default_rng(100)
+    grids = [O.f2h(rng.uniform(-1, 1, (h, w, C))) for (w, h) in CFG0["grids"]]
+    Ws = he_normal_weights(100, cout)
+    Ws[0] = zero_padded_inputs(Ws[0], 2 * C + 8)
+    W = [w.view(np.uint16).copy() for w in Ws]
+    b = [np.zeros(64, np.uint16), np.zeros(64, np.uint16), np.zeros(cout, np.uint16)]
+    model = O.OracleModel(C, cout, grids, W, b)
+    iw, ih = CFG0["image"]
+    n = 16384
+    t0 = time.perf_counter()
+    O.decode_range(model, iw, ih, 0, n, threads=threads)
+    dt = time.perf_counter() - t0
+    n = int(min(iw * ih, max(16384, n * seconds / max(dt, 1e-6) * 0.8)))
+    t0 = time.perf_counter()
+    O.decode_range(model, iw, ih, 0, n, threads=threads)
+    dt = time.perf_counter() - t0
+    cpu = ""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                cpu = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"value": n / dt, "unit": "texels/s", "cores": threads, "kind": "port", "cpu": cpu,
+            "sample": f"texels 0..{n} of the {iw * ih}-texel config-0 image (oracle/nt_oracle.c forward pass, "
+                      f"fp32 with fp16 rounding, OpenMP)"}
+
+
 CFG3 = dict(workload="config3_bc6h_16x4096sq", planes=16, size=4096)
 
 
@@ -237,7 +293,7 @@ def run_reference(args):
         vals.append(cpu_train_baseline(O, seconds=max(1.0, 60.0 / max(args.steps, 1)))["value"])
     last = cpu_train_baseline(O, seconds=1.0)
     value = statistics.median(vals)
-    line = {"impl": "reference", "metric": "train samples/s (fwd+bwd+Adam), config 1", "value": value,
+    line = {"impl": "reference", "metric": HEADLINE_METRIC, "value": value,
             "unit": "samples/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * CFG1["lattice"][0] * CFG1["lattice"][1] / value, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -286,6 +342,121 @@ def run_config4b(torch, dist, dev, stream, rank, world, steps, warmup):
            "parallelism": f"row shards x{world}: halo exchange (NCCL send/recv) + network-gradient allreduce",
            "l2": "state per rank far above L2 (no flush)"}
     del sh
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_config2(torch, dev, stream, L, nt, _native, steps, warmup, rank, peak_hbm):
+    """a 4096^2 PBR material (12 channels, normals from the height field),
+    1024^2x12 + 512^2x12 fp16 latents, 1,048,576 samples per step; one step = fused training
+    pass + fused Adam.  The state (~220 MB of latent state + 403 MB of target) is above the
+    126 MB L2, so no flush is needed."""
+    tex = nt.NeuralTexture(*CFG2["image"], grid_sizes=CFG2["grids"], latent_channels=CFG2["C"],
+                           output_channels=CFG2["cout"], device=dev, lattice=CFG2["lattice"])
+    tex.init(seed=200 + rank, pbr_normals=True)
+    sptr = stream.cuda_stream
+    B = CFG2["lattice"][0] * CFG2["lattice"][1]
+    ps = [tex.params(step=k + 1) for k in range(warmup + steps)]
+    for w in range(warmup):
+        _native.check(L.nt_invoke_training(ctypes.byref(ps[w]), 0, sptr))
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(ps[w]), sptr))
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
+    for k in range(steps):
+        p = ps[warmup + k]
+        ev[k][0].record(stream)
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 0, sptr))
+        ev[k][1].record(stream)
+        _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), sptr))
+        ev[k][2].record(stream)
+    torch.cuda.synchronize(dev)
+    t_train = sum(e[0].elapsed_time(e[1]) for e in ev) / steps
+    t_adam = sum(e[1].elapsed_time(e[2]) for e in ev) / steps
+    t = t_train + t_adam
+    nbytes = step_bytes(CFG2["grids"], CFG2["C"], B, CFG2["cout"])
+    flop = mlp_flop_train(CFG2["cout"]) * B
+    out = {"workload": CFG2["workload"], "value": B / (t * 1e-3), "unit": "samples/s", "ms_per_step": t,
+           "steps": steps, "warmup": warmup, "global_batch": B,
+           "latents": "1024^2x12 + 512^2x12 fp16", "mlp": "32-64-64-12",
+           "kernels_ms": {"train_kernel": t_train, "adam_kernel": t_adam},
+           "roofline": {"bound": "hbm", "achieved": nbytes / (t * 1e-3) / 1e9, "peak": peak_hbm, "unit": "GB/s",
+                        "frac": nbytes / (t * 1e-3) / 1e9 / peak_hbm,
+                        "algorithmic": f"30 B x {sum(w * h for (w, h) in CFG2['grids']) * CFG2['C']} latent params "
+                                       f"+ {B} x {CFG2['cout']} x 2 B of target = {nbytes} B per step"},
+           "train_kernel_tflops": flop / (t_train * 1e-3) / 1e12,
+           "l2": "state above L2 (no flush)"}
+    del tex, ps
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_config4a(torch, dist, dev, L, nt, _native, steps, warmup, rank, world, peak_hbm):
+    """BASELINE config 4a on this GPU: 8 independent 2048^2 materials with 10 output channels
+    (config 2's network scaled to 10 outputs; latents 512^2x12 + 256^2x12, config 2's texel /
+    latent ratio), 524,288 samples per material and step, no communication.  A step trains
+    every material once (training pass + fused Adam each), the materials spread over 4
+    streams.  The 8 materials' state (~1.1 GB) is far above L2.  Weak scaling: every rank
+    trains its own 8 materials."""
+    M = CFG4A["materials_per_gpu"]
+    B = CFG4A["lattice"][0] * CFG4A["lattice"][1]
+    texs = []
+    for i in range(M):
+        t = nt.NeuralTexture(*CFG4A["image"], grid_sizes=CFG4A["grids"], latent_channels=CFG4A["C"],
+                             output_channels=CFG4A["cout"], device=dev, lattice=CFG4A["lattice"])
+        t.init(seed=1000 + rank * M + i)
+        texs.append(t)
+    streams = [torch.cuda.Stream(dev) for _ in range(4)]
+    main = torch.cuda.current_stream(dev)
+
+    def step_all(step):
+        for i, t in enumerate(texs):
+            st = streams[i % len(streams)]
+            p = t.params(step=step)
+            _native.check(L.nt_invoke_training(ctypes.byref(p), 0, st.cuda_stream))
+            _native.check(L.nt_invoke_optimize_all(ctypes.byref(p), st.cuda_stream))
+
+    def fork():
+        e = torch.cuda.Event()
+        e.record(main)
+        for st in streams:
+            st.wait_event(e)
+
+    def join():
+        for st in streams:
+            e = torch.cuda.Event()
+            e.record(st)
+            main.wait_event(e)
+
+    fork()
+    for w in range(warmup):
+        step_all(w + 1)
+    join()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(main)
+    fork()
+    for k in range(steps):
+        step_all(warmup + k + 1)
+    join()
+    e1.record(main)
+    torch.cuda.synchronize(dev)
+    t = e0.elapsed_time(e1) / steps
+    if world > 1:
+        tt = torch.tensor([t], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t = tt.item()
+    nbytes = M * step_bytes(CFG4A["grids"], CFG4A["C"], B, CFG4A["cout"])
+    out = {"workload": CFG4A["workload"], "value": world * M * B / (t * 1e-3), "unit": "samples/s",
+           "ms_per_step": t, "steps": steps, "warmup": warmup, "scaling": "weak",
+           "materials": world * M, "materials_per_gpu": M, "batch_per_material": B,
+           "latents": "512^2x12 + 256^2x12 fp16 per material", "mlp": "32-64-64-10",
+           "roofline_per_gpu": {"bound": "hbm", "achieved": nbytes / (t * 1e-3) / 1e9, "peak": peak_hbm,
+                                "unit": "GB/s", "frac": nbytes / (t * 1e-3) / 1e9 / peak_hbm,
+                                "algorithmic": f"{M} materials x {nbytes // M} B per material step"},
+           "parallelism": f"materials x{world * M} ({M} per GPU, 4 streams), no collective",
+           "l2": "8 materials' state far above L2 (no flush)"}
+    del texs
     torch.cuda.empty_cache()
     return out
 
@@ -516,6 +687,8 @@ def main():
     ap.add_argument("--block-steps", type=int, default=50, help="timed BLOCK_FEATURES steps (0: skip)")
     ap.add_argument("--mip-steps", type=int, default=50, help="timed steps at a fractional mip coordinate (0: skip)")
     ap.add_argument("--texture-steps", type=int, default=50, help="timed steps with reference-texture targets (0: skip)")
+    ap.add_argument("--config2-steps", type=int, default=20, help="timed config-2 steps (0: skip)")
+    ap.add_argument("--config4a-steps", type=int, default=10, help="timed config-4a steps, 8 materials each (0: skip)")
     ap.add_argument("--dist-devices", type=int, default=0,
                     help="only time config 4b through nt_dist_train_step over this many devices (one process)")
     ap.add_argument("--tensor-peak-check", action="store_true",
@@ -607,6 +780,9 @@ def main():
     # memory (its step advanced per call, main.cpp:1077) and copies the loss into a pinned
     # host slot.  Pipelined: the host reads step k-1's loss after queuing step k, as a
     # training loop that logs its loss does.  Synchronous: the host waits for every step.
+    # The loop rotates over E2E_MATERIALS config-1 materials (one step each in turn), whose
+    # state together exceeds the L2, so each step starts with its material's state evicted,
+    # the cache condition the flushed device timing above has, without a flush kernel.
     pbytes = ctypes.sizeof(_native.NtKernelParams)
     slots = 2
     loss_dev = torch.zeros(slots, dtype=torch.float32, device=dev)
@@ -614,7 +790,13 @@ def main():
     dev_slot = [loss_dev[i] for i in range(slots)]
     host_slot = [loss_host[i] for i in range(slots)]
     done = [torch.cuda.Event() for _ in range(slots)]
-    p = tex.params()
+    e2e_texs = [tex]
+    for i in range(1, E2E_MATERIALS):
+        t = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                             output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
+        t.init(seed=rank + 17 * i)
+        e2e_texs.append(t)
+    e2e_params = [t.params() for t in e2e_texs]
     e2e_steps = args.steps
 
     def e2e_pass(pipelined):
@@ -625,9 +807,10 @@ def main():
         t0 = time.perf_counter()
         for k in range(e2e_steps):
             i = k % slots
+            p = e2e_params[k % E2E_MATERIALS]
             dev_slot[i].zero_()
             p.loss_accum = dev_slot[i].data_ptr()
-            p.step = 10_000 + k
+            p.step = 10_000 + k // E2E_MATERIALS
             _native.check(L.nt_train_step(ctypes.byref(p), sptr))
             host_slot[i].copy_(dev_slot[i], non_blocking=True)
             done[i].record(stream)
@@ -648,9 +831,11 @@ def main():
             raise RuntimeError("e2e: a step's loss did not come back")
         return world * B / e2e_t
 
+    e2e_pass(True)  # untimed: every material's first steps
     e2e_sync_value = e2e_pass(False)
     e2e_value = e2e_pass(True)
-    p.loss_accum = tex.loss_accum.data_ptr()
+    del e2e_texs[1:], e2e_params
+    torch.cuda.empty_cache()
 
     # ---- config 0 decode -----------------------------------------------------------------
     dtex = nt.NeuralTexture(*CFG0["image"], grid_sizes=CFG0["grids"], latent_channels=CFG0["C"],
@@ -682,6 +867,13 @@ def main():
     reftex = None
     if args.texture_steps > 0:
         reftex = run_reftex(torch, dev, stream, L, nt, _native, scratch, args.texture_steps, 5, rank)
+    pk = peaks()
+    cfg2 = None
+    if args.config2_steps > 0:
+        cfg2 = run_config2(torch, dev, stream, L, nt, _native, args.config2_steps, 3, rank, pk["hbm"])
+    cfg4a = None
+    if args.config4a_steps > 0:
+        cfg4a = run_config4a(torch, dist, dev, L, nt, _native, args.config4a_steps, 3, rank, world, pk["hbm"])
     cfg4b = None
     if args.sharded_steps > 0:
         cfg4b = run_config4b(torch, dist, dev, stream, rank, world, args.sharded_steps, 10)
@@ -694,7 +886,6 @@ def main():
     if rank != 0:
         return 0
 
-    pk = peaks()
     tr = ncu_traffic()
     train_flop = MLP_FLOP_TRAIN * B
     achieved_tf = train_flop / (t_train * 1e-3) / 1e12
@@ -702,7 +893,7 @@ def main():
     adam_bytes = 28 * P  # w 2 + g 4 + m 4 + v 4 read, w 2 + m 4 + v 4 + g 4 written
     dec_bytes = sum(w * h for (w, h) in CFG0["grids"]) * CFG0["C"] * 2 + texels * CFG0["cout"] * 2
     line = {
-        "metric": "train samples/s (fwd+bwd+Adam), config 1; decoded texels/s, config 0",
+        "metric": HEADLINE_METRIC,
         "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": t_step_max, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
@@ -715,6 +906,11 @@ def main():
                      "peak_source": pk["source"] + " burst bf16",
                      "algorithmic": f"{MLP_FLOP_TRAIN} FLOP/sample x {B} samples"},
         "kernels_ms": {"train_kernel": t_train, "adam_kernel": t_adam},
+        "step_roofline": {"bound": "hbm", "achieved": step_bytes(CFG1["grids"], CFG1["C"], B, CFG1["cout"]) /
+                          (t_step * 1e-3) / 1e9, "peak": pk["hbm"], "unit": "GB/s",
+                          "frac": step_bytes(CFG1["grids"], CFG1["C"], B, CFG1["cout"]) / (t_step * 1e-3) / 1e9 /
+                          pk["hbm"],
+                          "algorithmic": "30 B per latent parameter + 2 B per target channel read, per step"},
         "adam_roofline": {"bound": "hbm", "achieved": adam_bytes / (t_adam * 1e-3) / 1e9, "peak": pk["hbm"],
                           "unit": "GB/s", "frac": adam_bytes / (t_adam * 1e-3) / 1e9 / pk["hbm"],
                           "traffic": tr.get("adam_kernel", {}).get("bytes_per_launch"),
@@ -729,7 +925,8 @@ def main():
                         "(kept by the caller, its step advanced per call as the reference driver does), the "
                         "step's loss copied to a pinned host slot and read on the host one step behind (the "
                         "next step already queued); sync_every_step_value waits for each step before the "
-                        "next; no L2 flush"},
+                        f"next. Steps rotate over {E2E_MATERIALS} config-1 materials whose state (4 x 51 MB) "
+                        "exceeds the L2, so no step finds its material cached (no flush kernel in the loop)"},
         "gpu_launches": launches,
         "clocks": clk,
     }
@@ -751,12 +948,17 @@ def main():
         line["mips"] = mips
     if reftex:
         line["reference_textures"] = reftex
+    if cfg2:
+        line["config2"] = cfg2
+    if cfg4a:
+        line["config4a"] = cfg4a
     if cfg4b:
         line["config4b"] = cfg4b
     if not args.no_cpu_baseline:
         from oracle import oracle as O
         O.build()
         line["cpu_baseline"] = cpu_train_baseline(O)
+        line["decode"]["cpu_baseline"] = cpu_decode_baseline(O)
     print(json.dumps(line), flush=True)
     return 0
 

@@ -210,6 +210,11 @@ typedef struct NtKernelParams {
      * channel_loss_weights is then unused.  Needs an unsharded call. */
     NtReferenceTexture reference_textures[NT_MAX_REFERENCE_TEXTURES];
     int32_t num_reference_textures;
+
+    /* Elements per texel in inference_output (0: output_channels).  A larger stride writes
+     * channels output_channels .. stride - 1 as 0, so a caller laid out like the reference
+     * (train.cu:950-955: NT_OUTPUT_SIZE = 16 fp32 values per texel) reads its layout. */
+    int32_t inference_output_stride;
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */
@@ -406,11 +411,16 @@ typedef struct NtShard {
 /* The band split used for shards: lattice rows [rank * H / world, (rank + 1) * H / world) of
  * an H-row lattice reach rows [lo, hi) of a source of `height` rows (the range scaled and
  * rounded to the nearest row, so consecutive ranks partition the source).  NT_ERR_INVALID_ARG
- * if a band would be thinner than `halo` rows or its stored rows taller than the source. */
+ * if a band would be thinner than 2 x `halo` rows (nt_dist_train_step adds halo gradients to
+ * both band edges at once) or its stored rows taller than the source. */
 NT_API nt_status nt_dist_band(int32_t rank, int32_t world, int32_t lattice_height, int32_t height, int32_t halo,
                               int32_t *lo, int32_t *hi);
 /* One training step of a row-sharded material (count 1 .. NT_DIST_MAX_SHARDS; count 1 is
- * nt_train_step).  Returns once every phase is queued; the current device is restored. */
+ * nt_train_step).  Returns once every phase is queued; the current device is restored.  Every
+ * shard owns its buffers (two shards passing the same buffer are rejected).  The argument
+ * checks run before anything is queued; an error returned after that (a failed launch or
+ * event record) can leave some shards stepped and others not: the material must then be
+ * reloaded (from a checkpoint) before training goes on. */
 NT_API nt_status nt_dist_train_step(const NtShard *shards, int32_t count);
 
 /* ---- tensor-core self-test (no reference counterpart) ---------------------------------- */

@@ -98,6 +98,7 @@ class NtKernelParams(C.Structure):
         ("target_height", C.c_int32),
         ("reference_textures", NtReferenceTexture * NT_MAX_REFERENCE_TEXTURES),
         ("num_reference_textures", C.c_int32),
+        ("inference_output_stride", C.c_int32),
     ]
 
 

@@ -374,6 +374,7 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(target_height)
     NT_FIELD(reference_textures)
     NT_FIELD(num_reference_textures)
+    NT_FIELD(inference_output_stride)
 #undef NT_FIELD
     return (size_t)-1;
 }
@@ -492,12 +493,9 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
         L.rows[s] = p->stored_rows[s] ? p->stored_rows[s] : h;
         sharded = sharded || L.rows[s] != h;
     }
-    NT_REQUIRE(!sharded || train_engine() == 1, "row sharding needs the tcgen05 training engine (NT_TRAIN_ENGINE=mma is set)");
     NT_REQUIRE(!sharded || (p->lod == 0.f && L.th == p->image_height),
                "row sharding needs lod 0 and a target of the image's height");
-    NT_REQUIRE(!fractional || train_engine() == 1, "a fractional lod needs the tcgen05 training engine");
-    NT_REQUIRE(!L.num_ref || (!sharded && train_engine() == 1),
-               "reference textures need the tcgen05 training engine and an unsharded call");
+    NT_REQUIRE(!L.num_ref || !sharded, "reference textures need an unsharded call");
     // latent representation: UNCONSTRAINED trains fp16 grids, BLOCK_FEATURES trains BC6 block
     // features (train.cu:902-913), FINALIZE samples either and trains the network only
     NT_REQUIRE(type != NT_TRAIN_UNCONSTRAINED || p->latent_format == NT_LATENT_GRID_F16,
@@ -505,12 +503,11 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
     NT_REQUIRE(type != NT_TRAIN_BLOCK_FEATURES || p->latent_format == NT_LATENT_BC6_BLOCKS,
                "BLOCK_FEATURES training needs latent_format NT_LATENT_BC6_BLOCKS");
     L.blocks = p->latent_format == NT_LATENT_BC6_BLOCKS;
-    NT_REQUIRE(!L.blocks || (!sharded && train_engine() == 1),
-               "BC6 block features need the tcgen05 engine and an unsharded call");
+    NT_REQUIRE(!L.blocks || !sharded, "BC6 block features need an unsharded call");
     if (type == NT_TRAIN_BLOCK_FEATURES) L.finalize = 0;
     L.tiles_x = (p->lattice_width + kTileSide - 1) / kTileSide;
     L.tiles_y = (p->lattice_height + kTileSide - 1) / kTileSide;
-    return check_cuda(launch_train(L, p->latent_channels, (cudaStream_t)stream), "training kernel");
+    return check_cuda(launch_train_tc(L, p->latent_channels, (cudaStream_t)stream), "training kernel");
 }
 
 nt_status nt_invoke_optimize_network(const NtKernelParams *p, nt_stream_t stream)
@@ -565,8 +562,12 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
                "inference samples fp16 latent grids (train.cu:935, SampleUnconstrainedFeaturesTrilinear)");
     NT_REQUIRE(p->inference_output_dtype == NT_DTYPE_F16 || p->inference_output_dtype == NT_DTYPE_F32,
                "inference_output_dtype must be NT_DTYPE_F16 or NT_DTYPE_F32");
-    NT_REQUIRE(!(p->inference_output_dtype == NT_DTYPE_F16 && p->output_channels == 8) ||
-                   aligned16(p->inference_output),
+    NT_REQUIRE(p->inference_output_stride == 0 ||
+                   (p->inference_output_stride >= p->output_channels && p->inference_output_stride <= NT_MAX_OUTPUT),
+               "inference_output_stride (%d) must be 0 or in [output_channels, %d]", p->inference_output_stride,
+               NT_MAX_OUTPUT);
+    const int out_stride = p->inference_output_stride ? p->inference_output_stride : p->output_channels;
+    NT_REQUIRE(!(p->inference_output_dtype == NT_DTYPE_F16 && out_stride == 8) || aligned16(p->inference_output),
                "inference_output must be 16-byte aligned");
     NT_REQUIRE(!p->inference_mse_accum || p->target || p->num_reference_textures > 0,
                "inference_mse_accum requires a target or reference textures");
@@ -586,15 +587,14 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
             fractional = true;
         }
     }
-    NT_REQUIRE(!fractional || decode_engine() == 1, "a fractional lod needs the tcgen05 decode engine");
     L.net = net_view(p);
     L.out = p->inference_output;
     L.out_f32 = p->inference_output_dtype == NT_DTYPE_F32;
+    L.out_stride = out_stride;
     L.target = reinterpret_cast<const __half *>(p->target);
     if ((st = reference_views(p, L.ref, L.num_ref)) != NT_OK) return st;
     L.ref_lod = p->lod;
     if (L.num_ref > 0) {
-        NT_REQUIRE(decode_engine() == 1, "reference textures need the tcgen05 decode engine");
         L.target = nullptr;  // the MSE compares with the textures
     } else if (p->inference_mse_accum) {  // the target level of this lod, texel for texel
         const int tw = p->target_width ? p->target_width : p->image_width;
@@ -609,7 +609,7 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     L.image_h = p->image_height;
     L.tiles_x = (p->image_width + kTileSide - 1) / kTileSide;
     L.tiles_y = (p->image_height + kTileSide - 1) / kTileSide;
-    return check_cuda(launch_decode(L, p->latent_channels, (cudaStream_t)stream), "decode kernel");
+    return check_cuda(launch_decode_tc(L, p->latent_channels, (cudaStream_t)stream), "decode kernel");
 }
 
 nt_status nt_train_step(const NtKernelParams *p, nt_stream_t stream)

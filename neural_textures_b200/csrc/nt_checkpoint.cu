@@ -10,6 +10,9 @@
 //   ...  index: per section name[32], i32 dtype, i32 ndim, i64 shape[4], u64 offset, u64 bytes,
 //        u64 FNV-1a 64 of the payload
 // FNV-1a 64 (Fowler, Noll, Vo: offset basis 14695981039346656037, prime 1099511628211).
+#include <fcntl.h>
+#include <unistd.h>
+
 #include <cerrno>
 #include <cstdint>
 #include <cstdio>
@@ -151,7 +154,10 @@ nt_status nt_checkpoint_write(const char *path, const NtCheckpointSection *secti
     }
     const std::string tmp = std::string(path) + ".tmp";
     std::vector<Entry> entries((size_t)count);
-    {
+    // The file is written to path + ".tmp", flushed to the device, then renamed over path
+    // and the directory entry flushed too, so that a crash leaves either the old file or the
+    // new one.  A failed write removes the .tmp file.
+    const auto write_tmp = [&]() -> nt_status {
         File out;
         out.f = fopen(tmp.c_str(), "wb");
         if (!out.f) return set_error(NT_ERR_IO, "%s: cannot create (%s)", tmp.c_str(), strerror(errno));
@@ -187,11 +193,32 @@ nt_status nt_checkpoint_write(const char *path, const NtCheckpointSection *secti
         h.index_checksum = fnv1a(entries.data(), (uint64_t)count * sizeof(Entry));
         if (fseek(out.f, 0, SEEK_SET) != 0 || fwrite(&h, sizeof h, 1, out.f) != 1 || fflush(out.f) != 0)
             return set_error(NT_ERR_IO, "%s: write failed", tmp.c_str());
+        if (fsync(fileno(out.f)) != 0) return set_error(NT_ERR_IO, "%s: fsync failed (%s)", tmp.c_str(), strerror(errno));
         const int rc = fclose(out.f);
         out.f = nullptr;
         if (rc != 0) return set_error(NT_ERR_IO, "%s: close failed", tmp.c_str());
+        return NT_OK;
+    };
+    nt_status st = write_tmp();
+    if (st != NT_OK) {
+        remove(tmp.c_str());
+        return st;
     }
-    if (rename(tmp.c_str(), path) != 0) return set_error(NT_ERR_IO, "%s: rename failed (%s)", path, strerror(errno));
+    if (rename(tmp.c_str(), path) != 0) {
+        const int err = errno;
+        remove(tmp.c_str());
+        return set_error(NT_ERR_IO, "%s: rename failed (%s)", path, strerror(err));
+    }
+    {  // flush the directory entry of the rename
+        std::string dir(path);
+        const size_t slash = dir.find_last_of('/');
+        dir = slash == std::string::npos ? std::string(".") : (slash == 0 ? std::string("/") : dir.substr(0, slash));
+        const int fd = open(dir.c_str(), O_RDONLY | O_DIRECTORY);
+        if (fd >= 0) {
+            fsync(fd);
+            close(fd);
+        }
+    }
     return NT_OK;
 }
 

@@ -313,20 +313,27 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
                 float yv[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) yv[e] = round_half(__uint_as_float(h8 ? v[8 + e] : v[e]));
-                if (!p.out_f32 && cout == 8 && h8 == 0) {
+                const int ostride = p.out_stride;
+                if (!p.out_f32 && ostride == 8 && h8 == 0) {
                     *reinterpret_cast<uint4 *>(reinterpret_cast<__half *>(p.out) + texel * 8) =
                         make_uint4(pack_half2(yv[0], yv[1]), pack_half2(yv[2], yv[3]), pack_half2(yv[4], yv[5]),
                                    pack_half2(yv[6], yv[7]));
                 } else if (!p.out_f32) {
-                    __half *o = reinterpret_cast<__half *>(p.out) + texel * cout;
+                    __half *o = reinterpret_cast<__half *>(p.out) + texel * ostride;
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         if (c0 + e < c1) o[c0 + e] = __float2half_rn(yv[e]);
                 } else {
-                    float *o = reinterpret_cast<float *>(p.out) + texel * cout;
+                    float *o = reinterpret_cast<float *>(p.out) + texel * ostride;
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         if (c0 + e < c1) o[c0 + e] = yv[e];
+                }
+                if (ostride > cout && h8 == (cout - 1) / 8) {  // zero channels cout .. stride - 1
+                    for (int c = cout; c < ostride; ++c) {
+                        if (p.out_f32) reinterpret_cast<float *>(p.out)[texel * ostride + c] = 0.f;
+                        else reinterpret_cast<__half *>(p.out)[texel * ostride + c] = __float2half_rn(0.f);
+                    }
                 }
                 if (p.target) {
                     const __half *t = p.target + texel * cout;
@@ -406,15 +413,6 @@ cudaError_t read_decode_status(uint32_t *status, bool clear)
     if (e != cudaSuccess || !clear) return e;
     const uint32_t zero = 0;
     return cudaMemcpyToSymbol(g_decode_status, &zero, sizeof(uint32_t));
-}
-
-int decode_engine()
-{
-    static const int engine = [] {
-        const char *e = getenv("NT_DECODE_ENGINE");
-        return (e && strcmp(e, "mma") == 0) ? 0 : 1;
-    }();
-    return engine;
 }
 
 }  // namespace nt

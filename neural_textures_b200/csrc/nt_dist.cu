@@ -281,6 +281,31 @@ nt_status validate_shards(const NtShard *sh, int n)
                          r, g, stored - 2 * halo, halo);
         }
     }
+    // every shard owns its buffers: two shards updating one buffer in place would race (their
+    // Adam kernels run on different streams) and apply the update once per shard
+    for (int r = 0; r < n; ++r) {
+        const NtKernelParams &p = sh[r].params;
+        for (int q = 0; q < r; ++q) {
+            const NtKernelParams &o = sh[q].params;
+            for (int l = 0; l < NT_NUM_NETWORK_LAYERS; ++l) {
+                const void *a[8] = {p.network_weights[l], p.network_weight_gradients[l], p.network_weight_moment1[l],
+                                    p.network_weight_moment2[l], p.network_biases[l], p.network_bias_gradients[l],
+                                    p.network_bias_moment1[l], p.network_bias_moment2[l]};
+                const void *b[8] = {o.network_weights[l], o.network_weight_gradients[l], o.network_weight_moment1[l],
+                                    o.network_weight_moment2[l], o.network_biases[l], o.network_bias_gradients[l],
+                                    o.network_bias_moment1[l], o.network_bias_moment2[l]};
+                for (int i = 0; i < 8; ++i)
+                    DIST_REQUIRE(!a[i] || a[i] != b[i], "shards %d and %d share a network buffer of layer %d", q, r, l);
+            }
+            for (int g = 0; g < NT_NUM_FEATURES; ++g) {
+                const NtFeature &f = p.features[g], &e = o.features[g];
+                const void *a[4] = {f.grid, f.gradients, f.moment1, f.moment2};
+                const void *b[4] = {e.grid, e.gradients, e.moment1, e.moment2};
+                for (int i = 0; i < 4; ++i)
+                    DIST_REQUIRE(!a[i] || a[i] != b[i], "shards %d and %d share a buffer of latent grid %d", q, r, g);
+            }
+        }
+    }
     for (int g = 0; g < NT_NUM_FEATURES; ++g) {  // bands tile the grid in a ring
         const int h = p0.features[g].height, halo = sh[0].halo_rows[g];
         int64_t total = 0;
@@ -356,9 +381,11 @@ nt_status nt_dist_band(int32_t rank, int32_t world, int32_t lattice_height, int3
         l = 0;
         h = height;
     } else {
-        DIST_REQUIRE(h - l >= halo && h - l + 2 * halo <= height,
-                     "rank %d: a band of %lld rows of a %d-row source cannot be sharded %d ways with a %d-row halo", rank,
-                     (long long)(h - l), height, world, halo);
+        // nt_dist_train_step adds the neighbours' halo gradients to the first and the last
+        // `halo` rows of a band in one launch, so a band holds at least two halos
+        DIST_REQUIRE(h - l >= 2 * halo && h - l + 2 * halo <= height,
+                     "rank %d: a band of %lld rows of a %d-row source cannot be sharded %d ways with a %d-row halo "
+                     "(a band needs at least %d rows)", rank, (long long)(h - l), height, world, halo, 2 * halo);
     }
     *lo = (int32_t)l;
     *hi = (int32_t)h;

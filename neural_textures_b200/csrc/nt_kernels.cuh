@@ -62,6 +62,7 @@ struct DecodeLaunch {
     NetView net;
     void *out;
     int32_t out_f32;
+    int32_t out_stride;    // elements per texel of out (>= cout; channels past cout are written as 0)
     const __half *target;  // optional, fp16 [h][w][cout]
     float *mse_accum;      // optional
     int32_t image_w, image_h;
@@ -94,19 +95,12 @@ struct AdamLaunch {
     int32_t total_blocks;
 };
 
-// Returns the number of CTAs used (0 on launch failure; cudaGetLastError holds the error).
-cudaError_t launch_train(const TrainLaunch &p, int channels, cudaStream_t stream);
 // tcgen05 / TMEM training kernel (16 x 8 tiles; recomputes tiles_x / tiles_y itself)
 cudaError_t launch_train_tc(const TrainLaunch &p, int channels, cudaStream_t stream);
-// Training engine: 1 = tcgen05 (default), 0 = per-warp mma.sync (NT_TRAIN_ENGINE=mma)
-int train_engine();
 // tcgen05 / TMEM decode kernel (16 x 8 tiles; recomputes tiles_x / tiles_y itself)
 cudaError_t launch_decode_tc(const DecodeLaunch &p, int channels, cudaStream_t stream);
-// Decode engine: 1 = tcgen05 (default), 0 = per-warp mma.sync (NT_DECODE_ENGINE=mma)
-int decode_engine();
 // Status word of the decode kernel's bounded waits (host read, optionally cleared).
 cudaError_t read_decode_status(uint32_t *status, bool clear);
-cudaError_t launch_decode(const DecodeLaunch &p, int channels, cudaStream_t stream);
 cudaError_t launch_adam(const AdamLaunch &p, cudaStream_t stream);
 int sm_count();
 // Raise the dynamic shared-memory limit of `kernel` once per device.

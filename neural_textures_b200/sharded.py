@@ -77,9 +77,9 @@ def source_band(rank: int, world: int, lattice_h: int, height: int) -> Band:
     lo, hi = rnd(a), rnd(b)
     if world == 1:
         return Band(height, 0, height, 0)
-    if hi - lo < HALO or hi - lo + 2 * HALO > height:
+    if hi - lo < 2 * HALO or hi - lo + 2 * HALO > height:  # the halo adds at both band edges must not overlap
         raise ValueError(f"rank {rank}: band of {hi - lo} rows of a {height}-row source cannot be sharded "
-                         f"{world} ways with a {HALO}-row halo")
+                         f"{world} ways with a {HALO}-row halo (a band needs at least {2 * HALO} rows)")
     return Band(height, lo, hi, HALO)
 
 

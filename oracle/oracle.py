@@ -41,9 +41,11 @@ def _stale() -> bool:
 
 
 def build_ref(reference_root: str | None = None) -> str | None:
-    """Build oracle/_ref from the reference sources when they are present (this container)."""
-    root = reference_root or os.environ.get("NT_REFERENCE_ROOT", "/root/reference")
-    if not os.path.exists(os.path.join(root, "train.cu")):
+    """Build oracle/_ref from the reference sources in `reference_root` (else the directory
+    named by $NT_REFERENCE_ROOT).  Returns None, building nothing, when neither names a
+    checkout of the reference (GPU hosts carry no reference sources)."""
+    root = reference_root or os.environ.get("NT_REFERENCE_ROOT")
+    if not root or not os.path.exists(os.path.join(root, "train.cu")):
         return None
     subprocess.run([os.path.join(HERE, "build_ref.sh"), root], check=True,
                    stdout=subprocess.DEVNULL)

@@ -1,17 +1,22 @@
-// driver_loop.cpp -- the reference driver's training loop (mavenkim2/neural_textures
-// main.cpp:1037-1091) written against the C++ drop-in headers: KernelParams by value, the four
-// Invoke* entry points, RunForwardPassTest, std::runtime_error on failure.
+// driver_loop.cpp -- a reference-style driver written against the C++ drop-in headers: the
+// set-up of mavenkim2/neural_textures main.cpp:680-812 (caller-allocated buffers in
+// KernelParams' reference fields, reference textures as the target) and its loop
+// main.cpp:1037-1091 (texelOffsetX/Y per iteration, featureAdam learning-rate decay,
+// InvokeTraining, InvokeOptimizeNetwork, InvokeOptimizeFeatures, step++, then InvokeInference
+// with the MSE), with std::runtime_error on failure.
 //
 //   driver_loop --invalid   a rejected call surfaces as std::runtime_error (no GPU needed)
-//   driver_loop [iters]     known-answer test, `iters` training steps on a synthetic 256^2
-//                           material, inference with MSE; prints one JSON line
+//   driver_loop [iters]     known-answer test, `iters` training steps on a 768^2 material with
+//                           four reference textures, inference with MSE; prints one JSON line
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <random>
 #include <stdexcept>
 #include <vector>
 
@@ -36,27 +41,32 @@ T *device_zeros(size_t n)
     return p;
 }
 
-// fp16 bits of a float (round to nearest even; normal range only, enough for small weights)
-uint16_t to_half(float f)
-{
-    uint32_t x;
-    std::memcpy(&x, &f, 4);
-    const uint32_t sign = (x >> 16) & 0x8000u;
-    int32_t exp = (int32_t)((x >> 23) & 0xff) - 127 + 15;
-    uint32_t mant = x & 0x7fffffu;
-    if (exp <= 0) return (uint16_t)sign;
-    uint32_t h = sign | ((uint32_t)exp << 10) | (mant >> 13);
-    const uint32_t rest = mant & 0x1fffu;
-    if (rest > 0x1000u || (rest == 0x1000u && (h & 1u))) ++h;
-    return (uint16_t)h;
-}
-
 KernelParams invalid_params()
 {
-    KernelParams p{};
-    p.latent_channels = 7;  // rejected: 8 or 12 only
-    p.output_channels = 8;
+    KernelParams p;
+    p.latentChannels = 7;  // rejected: 8 or 12 only
+    p.usedOutputChannels = 8;
     return p;
+}
+
+// A smooth seeded fp32 image of `ch` channels in [0, 1].
+std::vector<float> image(int w, int h, int ch, uint32_t seed)
+{
+    std::vector<float> v((size_t)w * h * ch);
+    std::mt19937 rng(seed);
+    std::uniform_real_distribution<float> U(0.f, 6.2831853f);
+    float ph[4][3];
+    for (auto &c : ph)
+        for (float &x : c) x = U(rng);
+    for (int y = 0; y < h; ++y)
+        for (int x = 0; x < w; ++x)
+            for (int c = 0; c < ch; ++c) {
+                const float u = (x + 0.5f) / w * 6.2831853f, t = (y + 0.5f) / h * 6.2831853f;
+                v[((size_t)y * w + x) * ch + c] =
+                    0.5f + 0.25f * std::sin(2.f * u + ph[c][0]) * std::cos(3.f * t + ph[c][1]) +
+                    0.2f * std::sin(5.f * u + 4.f * t + ph[c][2]);
+            }
+    return v;
 }
 
 }  // namespace
@@ -73,85 +83,121 @@ int main(int argc, char **argv)
         return 1;
     }
     const int iters = argc > 1 ? std::atoi(argv[1]) : 200;
+    std::vector<NtReferenceTexture> uploaded;
     try {
         if (!RunForwardPassTest()) throw std::runtime_error("forward-pass known-answer test failed");
 
-        const int W = 256, H = 256, C = 8, COUT = 8;
-        const int gw[2] = {128, 64}, gh[2] = {128, 64};
-        KernelParams params{};
-        params.latent_channels = C;
-        params.output_channels = COUT;
+        const int W = 768, H = 768, C = 8;
+        KernelParams params;
+        params.latentChannels = C;
+        // reference textures (main.cpp:558-637, 813-850): albedo RGB, normal RGB, roughness, metalness
+        const int chans[4] = {3, 3, 1, 1};
+        const float weights[4] = {1.f, 1.f, 0.5f, 0.5f};
+        int used = 0;
+        for (int i = 0; i < 4; ++i) {
+            std::vector<float> img = image(W, H, chans[i], 7u + i);
+            NtReferenceTexture t;
+            if (nt_reference_texture_create(img.data(), W, H, chans[i], 1, weights[i], &t) != NT_OK)
+                throw std::runtime_error(std::string("nt_reference_texture_create: ") + nt_get_last_error_string());
+            uploaded.push_back(t);
+            params.referenceTextures[i].texture = (cudaTextureObject_t)t.texture;
+            params.referenceTextures[i].width = W;
+            params.referenceTextures[i].height = H;
+            params.referenceTextures[i].numChannels = chans[i];
+            params.referenceTextures[i].numMipLevels = 1;
+            params.referenceTextures[i].lossWeight = weights[i];
+            used += chans[i];
+        }
+        params.numReferenceTextures = 4;
+        params.usedOutputChannels = used;
+
+        // latents (main.cpp:657-738, one fp16 grid per feature here)
+        const int gw[2] = {384, 192}, gh[2] = {384, 192};
         for (int f = 0; f < NT_NUM_FEATURES; ++f) {
             const size_t n = (size_t)gw[f] * gh[f] * C;
-            void *grid = device_zeros<uint16_t>(n);
-            check(nt_init_latents(grid, (int64_t)n, 17u + f, nullptr) == NT_OK ? cudaSuccess : cudaErrorUnknown,
+            Feature &feature = params.features[f];
+            feature.width = gw[f];
+            feature.height = gh[f];
+            feature.numMips = 1;
+            feature.unconstrainedGrid = device_zeros<half>(n);
+            check(nt_init_latents(feature.unconstrainedGrid, (int64_t)n, 17u + f, nullptr) == NT_OK
+                      ? cudaSuccess
+                      : cudaErrorUnknown,
                   "nt_init_latents");
-            params.features[f] = {grid, device_zeros<float>(n), device_zeros<float>(n), device_zeros<float>(n),
-                                  gw[f], gh[f], 1};
+            feature.unconstrainedGradients = device_zeros<float>(n);
+            feature.unconstrainedMoment1 = device_zeros<float>(n);
+            feature.unconstrainedMoment2 = device_zeros<float>(n);
         }
+        // network (main.cpp:740-788): padded column-major fp16 weights, zero biases (16 for layer 3)
         const int pad_in[3] = {32, 64, 64}, pad_out[3] = {64, 64, 16}, n_in[3] = {2 * C + 8, 64, 64};
-        uint32_t lcg = 12345u;
-        for (int l = 0; l < NT_NUM_NETWORK_LAYERS; ++l) {  // He-normal-like uniform weights, zero biases
+        std::mt19937 rng(1337u);
+        for (int l = 0; l < NT_NUM_NETWORK_LAYERS; ++l) {
             const size_t n = (size_t)pad_in[l] * pad_out[l];
-            std::vector<uint16_t> w(n, 0);
-            const float scale = std::sqrt(6.0f / (float)pad_in[l]);
-            for (int o = 0; o < (l == 2 ? COUT : 64); ++o)
-                for (int i = 0; i < n_in[l]; ++i) {
-                    lcg = lcg * 1664525u + 1013904223u;
-                    w[(size_t)o * pad_in[l] + i] = to_half(scale * ((float)(lcg >> 8) / 16777216.0f * 2.f - 1.f));
-                }
-            uint16_t *dw = device_zeros<uint16_t>(n);
-            check(cudaMemcpy(dw, w.data(), n * 2, cudaMemcpyHostToDevice), "weights");
-            const size_t nb = l == 2 ? COUT : 64;
-            params.network_weights[l] = dw;
-            params.network_weight_gradients[l] = device_zeros<float>(n);
-            params.network_weight_moment1[l] = device_zeros<float>(n);
-            params.network_weight_moment2[l] = device_zeros<float>(n);
-            params.network_biases[l] = device_zeros<uint16_t>(nb);
-            params.network_bias_gradients[l] = device_zeros<float>(nb);
-            params.network_bias_moment1[l] = device_zeros<float>(nb);
-            params.network_bias_moment2[l] = device_zeros<float>(nb);
+            std::vector<half> w(n, __float2half(0.f));
+            std::normal_distribution<float> N(0.f, std::sqrt(2.f / (float)pad_in[l]));
+            for (int o = 0; o < (l == 2 ? used : 64); ++o)
+                for (int i = 0; i < n_in[l]; ++i) w[(size_t)o * pad_in[l] + i] = __float2half(N(rng));
+            params.networkWeights[l] = device_zeros<half>(n);
+            check(cudaMemcpy(params.networkWeights[l], w.data(), n * sizeof(half), cudaMemcpyHostToDevice), "weights");
+            const size_t nb = l == 2 ? NT_OUTPUT_SIZE : 64;
+            params.networkWeightGradients[l] = device_zeros<float>(n);
+            params.networkWeightMoment1[l] = device_zeros<float>(n);
+            params.networkWeightMoment2[l] = device_zeros<float>(n);
+            params.networkBiases[l] = device_zeros<half>(nb);
+            params.networkBiasGradients[l] = device_zeros<float>(nb);
+            params.networkBiasMoment1[l] = device_zeros<float>(nb);
+            params.networkBiasMoment2[l] = device_zeros<float>(nb);
         }
-        params.network_adam = {0.9f, 0.99f, 5e-3f, 1e-8f};
-        params.feature_adam = {0.9f, 0.99f, 1e-2f, 1e-8f};
-        void *target = device_zeros<uint16_t>((size_t)W * H * COUT);
-        check(nt_generate_target(target, W, H, COUT, 3u, 0, nullptr) == NT_OK ? cudaSuccess : cudaErrorUnknown,
-              "nt_generate_target");
-        params.target = target;
-        for (int c = 0; c < COUT; ++c) params.channel_loss_weights[c] = 1.f;
-        params.image_width = W;
-        params.image_height = H;
-        params.lattice_width = params.lattice_height = 128;
-        params.sample_stride_x = params.sample_stride_y = 2.f;
-        params.num_samples = 128 * 128;
+        params.networkAdam = {0.9f, 0.99f, 5e-3f, 1e-8f};
+        params.featureAdam = {0.9f, 0.99f, 1e-2f, 1e-8f};
+        params.imageWidth = W;
+        params.imageHeight = H;
+        params.numSamples = 512 * 512;
         float *loss = device_zeros<float>(1);
-        params.loss_accum = loss;
+        params.lossAccum = loss;
 
+        // main.cpp:1037-1077
+        std::mt19937 regionRng(20260411u);
+        std::uniform_int_distribution<int> randomRegionX(0, std::max(0, params.imageWidth - 512));
+        std::uniform_int_distribution<int> randomRegionY(0, std::max(0, params.imageHeight - 512));
+        const float baseFeatureLearningRate = params.featureAdam.learningRate;
         float first = 0.f, last = 0.f;
-        for (int iter = 0; iter < iters; ++iter) {  // main.cpp:1037-1077
+        for (int iter = 0; iter < iters; ++iter) {
+            params.texelOffsetX = randomRegionX(regionRng);
+            params.texelOffsetY = randomRegionY(regionRng);
+            const TrainingKernelType type = TrainingKernelType::UNCONSTRAINED;
+            params.featureAdam.learningRate = baseFeatureLearningRate * std::pow(0.9995f, (float)iter);
             check(cudaMemset(loss, 0, sizeof(float)), "cudaMemset");
-            InvokeTraining(params, TrainingKernelType::UNCONSTRAINED);
+            InvokeTraining(params, type);
             InvokeOptimizeNetwork(params);
-            InvokeOptimizeFeatures(params, TrainingKernelType::UNCONSTRAINED);
+            InvokeOptimizeFeatures(params, type);
             params.step++;
             float l = 0.f;
             check(cudaMemcpy(&l, loss, sizeof(float), cudaMemcpyDeviceToHost), "loss");
             if (iter == 0) first = l;
             last = l;
         }
-        float *out = device_zeros<float>((size_t)W * H * COUT);
-        float *mse = device_zeros<float>(1);
-        params.inference_output = out;
-        params.inference_output_dtype = NT_DTYPE_F32;
-        params.inference_mse_accum = mse;
-        InvokeInference(params);  // main.cpp:1091
+        // main.cpp:1011-1016, :1089-1100: [N][NT_OUTPUT_SIZE] fp32 output and the MSE accumulator
+        const size_t count = (size_t)W * H;
+        params.inferenceOutput = device_zeros<float>(count * NT_OUTPUT_SIZE);
+        params.inferenceMseAccum = device_zeros<float>(1);
+        InvokeInference(params);
+        check(cudaDeviceSynchronize(), "cudaDeviceSynchronize(inference)");
+        std::vector<float> out(count * NT_OUTPUT_SIZE);
         float sse = 0.f;
-        check(cudaMemcpy(&sse, mse, sizeof(float), cudaMemcpyDeviceToHost), "mse");
-        std::printf("{\"iters\": %d, \"loss_first\": %.6g, \"loss_last\": %.6g, \"mse\": %.6g}\n", iters, first,
-                    last, sse / (float)(W * H * COUT));
-        return last < first && std::isfinite(sse) ? 0 : 2;
+        check(cudaMemcpy(out.data(), params.inferenceOutput, out.size() * sizeof(float), cudaMemcpyDeviceToHost),
+              "inferenceOutput");
+        check(cudaMemcpy(&sse, params.inferenceMseAccum, sizeof(float), cudaMemcpyDeviceToHost), "mse");
+        bool zero_tail = true;  // channels past usedOutputChannels are written as 0
+        for (size_t i = 0; i < count; ++i)
+            for (int c = used; c < NT_OUTPUT_SIZE; ++c) zero_tail = zero_tail && out[i * NT_OUTPUT_SIZE + c] == 0.f;
+        std::printf("{\"iters\": %d, \"loss_first\": %.6g, \"loss_last\": %.6g, \"mse\": %.6g, \"zero_tail\": %s}\n",
+                    iters, first, last, sse / (float)(count * used), zero_tail ? "true" : "false");
+        for (NtReferenceTexture &t : uploaded) nt_reference_texture_destroy(&t);
+        return last < first && std::isfinite(sse) && zero_tail ? 0 : 2;
     } catch (const std::exception &e) {
         std::fprintf(stderr, "error: %s\n", e.what());
+        for (NtReferenceTexture &t : uploaded) nt_reference_texture_destroy(&t);
         return 3;
     }
 }

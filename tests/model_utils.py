@@ -35,7 +35,18 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / den) if den > 0 else float(np.linalg.norm(a))
 
 
-def max_rel(a, b, floor=1.0):
+# Denominator floor of the decode comparisons.  The decoded outputs of the BASELINE networks
+# span about +-4; 99.7% of the config-0 outputs are bit-identical to the oracle's and the rest
+# differ by one fp16 rounding step of a hidden activation or of the output (at most 2^-9 at
+# |y| in [2, 4)), which the tensor cores' fp32 sums and the oracle's exact sums can resolve
+# differently.  Relative to max(|ref|, 0.25), the 1e-2 tolerance holds every output of
+# magnitude >= 0.25 to 1% and the smaller ones to 2.5e-3 absolute (about one fp16 step at the
+# top of the output range).
+DECODE_FLOOR = 0.25
+
+
+def max_rel(a, b, floor=DECODE_FLOOR):
+    """Max over elements of |a - b| / max(|b|, floor)."""
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.max(np.abs(a - b) / np.maximum(np.abs(b), floor)))

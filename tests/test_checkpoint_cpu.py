@@ -118,3 +118,16 @@ def test_invalid_section_tables_are_rejected(native, tmp_path, bad, needle):
         tab2[i].name, tab2[i].dtype, tab2[i].ndim = b"same", _native.NT_DTYPE_F32, 1
         tab2[i].shape[0], tab2[i].bytes, tab2[i].data = 6, a.nbytes, a.ctypes.data
     _expect(native, native.nt_checkpoint_write(path, tab2, 2), 1, "twice")
+
+
+def test_failed_write_leaves_no_temporary(native, tmp_path):
+    """A write that cannot be completed (here the rename: the destination is a directory)
+    returns NT_ERR_IO, removes its .tmp file and leaves the destination untouched."""
+    import neural_textures_b200 as nt
+    from neural_textures_b200 import _native
+    dst = tmp_path / "ckpt"
+    dst.mkdir()
+    with pytest.raises(_native.NtError):
+        nt.api.checkpoint_write(dst, {"a": np.arange(4, dtype=np.int32)})
+    assert not os.path.exists(str(dst) + ".tmp")
+    assert dst.is_dir()

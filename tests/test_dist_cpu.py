@@ -30,13 +30,27 @@ def test_band_split_rejects_thin_bands(native):
     lo, hi = C.c_int32(), C.c_int32()
     assert native.nt_dist_band(0, 8, 64, 16, HALO, C.byref(lo), C.byref(hi)) != 0
     assert b"cannot be sharded" in native.nt_get_last_error_string()
+    # owned rows between one and two halos: rejected (the step adds halo gradients to both
+    # band edges at once), and a band of exactly two halos is accepted
+    assert native.nt_dist_band(0, 2, 16, 10, 3, C.byref(lo), C.byref(hi)) != 0  # 5 rows, halo 3
+    assert b"at least 6 rows" in native.nt_get_last_error_string()
+    assert native.nt_dist_band(0, 2, 16, 12, 3, C.byref(lo), C.byref(hi)) == 0  # 6 rows, halo 3
+    assert (lo.value, hi.value) == (0, 6)
     assert native.nt_dist_band(3, 2, 64, 16, 3, C.byref(lo), C.byref(hi)) != 0
     assert native.nt_dist_band(0, 2, 64, 16, 3, None, None) != 0
 
 
+def _band(r, world, lattice_h, h, halo):
+    """source_band's rounding without its thickness check (to build invalid sets too)."""
+    a, b = r * lattice_h // world, (r + 1) * lattice_h // world
+    rnd = lambda x: (2 * x * h + lattice_h) // (2 * lattice_h)
+    lo, hi = rnd(a), rnd(b)
+    return type("B", (), {"origin": (lo - halo) % h, "stored": hi - lo + 2 * halo})
+
+
 def _shard_set(world, grids=((128, 128), (64, 64)), C_=8, halo=HALO, lattice_h=128):
     """A consistent shard set on host-only fake pointers (never dereferenced: the layout checks
-    run first and the CUDA calls fail without a GPU)."""
+    run first and the CUDA calls fail without a GPU); every shard has its own pointers."""
     from neural_textures_b200 import _native as N
     arr = (N.NtShard * world)()
     for r in range(world):
@@ -45,10 +59,21 @@ def _shard_set(world, grids=((128, 128), (64, 64)), C_=8, halo=HALO, lattice_h=1
         p.lattice_width, p.lattice_height = lattice_h, lattice_h
         a, b = r * lattice_h // world, (r + 1) * lattice_h // world
         p.lattice_row0, p.lattice_rows = a, b - a
+        for l in range(3):
+            base = 0x100000 * (r + 1) + 0x1000 * l
+            p.network_weights[l] = base + 0x10
+            p.network_weight_gradients[l] = base + 0x20
+            p.network_weight_moment1[l] = base + 0x30
+            p.network_weight_moment2[l] = base + 0x40
+            p.network_biases[l] = base + 0x50
+            p.network_bias_gradients[l] = base + 0x60
+            p.network_bias_moment1[l] = base + 0x70
+            p.network_bias_moment2[l] = base + 0x80
         for i, (w, h) in enumerate(grids):
-            band = source_band(r, world, lattice_h, h)
+            band = _band(r, world, lattice_h, h, halo)
             f = p.features[i]
-            f.grid = f.gradients = f.moment1 = f.moment2 = 0x1000
+            base = 0x100000 * (r + 1) + 0x10000 * (i + 1)
+            f.grid, f.gradients, f.moment1, f.moment2 = base, base + 0x100, base + 0x200, base + 0x300
             f.width, f.height = w, h
             p.row_origin[i] = band.origin
             p.stored_rows[i] = band.stored
@@ -94,6 +119,16 @@ def test_dist_step_rejects_bad_sets(native):
     thin = _shard_set(8, grids=((128, 128), (32, 32)), lattice_h=128)
     assert native.nt_dist_train_step(thin, 8) != 0
     assert b"thinner than two" in native.nt_get_last_error_string()
+
+    # two shards passing the same buffer
+    shared = _shard_set(3)
+    shared[2].params.network_weight_moment1[1] = shared[0].params.network_weight_moment1[1]
+    assert native.nt_dist_train_step(shared, 3) != 0
+    assert b"share a network buffer" in native.nt_get_last_error_string()
+    shared = _shard_set(2)
+    shared[1].params.features[0].gradients = shared[0].params.features[0].gradients
+    assert native.nt_dist_train_step(shared, 2) != 0
+    assert b"share a buffer of latent grid 0" in native.nt_get_last_error_string()
 
 
 def test_dist_step_layout_accepted(native):

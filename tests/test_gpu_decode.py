@@ -1,6 +1,10 @@
 """Decode (train.cu:917-961) parity: the CUDA decode kernel against the CPU oracle on the
 same seeded latents and weights.  Tolerance: max relative error 1e-2 (fp16), relative to
-max(|ref|, 1) so that outputs near zero are held to 1e-2 absolute."""
+max(|ref|, 0.25) (tests/model_utils.py DECODE_FLOOR: outputs below 0.25 are held to 2.5e-3
+absolute, about one fp16 step at the top of the output range); the full config-0 image is
+also held to at most 1% of its outputs differing from the oracle's at all."""
+import os
+
 import numpy as np
 import pytest
 
@@ -48,23 +52,24 @@ def test_decode_mse_accumulator(cuda, oracle):
     assert abs(mse.item() - want) <= 1e-4 * want
 
 
-def test_decode_full_config0_subset(cuda, oracle):
-    """BASELINE config 0 (1024^2 texels, 512^2x8 + 256^2x8 latents, 8 outputs): the whole
-    image is decoded on the GPU and a seeded subset of 20,000 texels is checked against the
-    oracle; every output is finite."""
+@pytest.mark.parametrize("f32", [False, True])
+def test_decode_full_config0(cuda, oracle, f32):
+    """BASELINE config 0 (1024^2 texels, 512^2x8 + 256^2x8 latents, 8 outputs, He-normal
+    weights from the seed): every one of the 1,048,576 x 8 outputs against the oracle."""
     import torch
     tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, seed=11)
-    out = tex.decode()
+    out = tex.decode(dtype=torch.float32 if f32 else torch.float16)
     torch.cuda.synchronize()
     got = out.cpu().numpy().astype(np.float32)
     assert np.isfinite(got).all()
-    model = oracle_model(oracle, tex)
-    rng = np.random.default_rng(0)
-    starts = rng.integers(0, 1024 * 1024 - 200, 100)
-    for s in starts:
-        ref = oracle.decode_range(model, 1024, 1024, int(s), 200).view(np.float16).astype(np.float32)
-        err = max_rel(got[s:s + 200], ref)
-        assert err <= TOL, f"texels {s}..{s + 200}: max rel err {err}"
+    ref = oracle.decode(oracle_model(oracle, tex), 1024, 1024, out_f32=True, threads=os.cpu_count() or 1)
+    assert got.shape == ref.shape == (1024 * 1024, 8)
+    err = max_rel(got, ref)
+    differ = float(np.mean(got != ref))
+    print(f"config 0 full image ({'fp32' if f32 else 'fp16'} output): max rel err {err:.3e}, "
+          f"max abs err {float(np.max(np.abs(got - ref))):.3e}, outputs differing {differ:.4%}")
+    assert err <= TOL, f"max rel err {err}"
+    assert differ <= 0.01, differ
 
 
 def test_decode_is_deterministic(cuda):
@@ -73,3 +78,22 @@ def test_decode_is_deterministic(cuda):
     a = tex.decode().cpu()
     b = tex.decode().cpu()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("f32", [False, True])
+def test_decode_output_stride(cuda, f32):
+    """inference_output_stride > output_channels (the reference's [N][16] fp32 layout,
+    train.cu:950-955): the first output_channels of every texel equal the packed decode and
+    the channels past them are written as 0."""
+    import torch
+    import neural_textures_b200 as nt
+    tex = make_texture((40, 24), ((20, 12), (10, 6)), 8, 8, seed=4)
+    dt = torch.float32 if f32 else torch.float16
+    packed = tex.decode(dtype=dt)
+    wide = torch.full((40 * 24, 16), 7.0, dtype=dt, device=cuda)
+    p = tex.params(inference_output=wide)
+    p.inference_output_stride = 16
+    nt.InvokeInference(p)
+    torch.cuda.synchronize()
+    assert torch.equal(wide[:, :8], packed)
+    assert torch.all(wide[:, 8:] == 0)

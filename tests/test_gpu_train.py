@@ -3,9 +3,11 @@
 - one training pass (train.cu:818-915 semantics): network and latent gradients, relative
   L2 error <= 2e-2 per buffer; the sum of squared errors within 1e-3 relative;
 - Adam (train.cu:521-588): bit-exact, including the zero-gradient skip and the zeroing;
-- a multi-step run: the loss after N steps within 2% of the oracle's;
-- full BASELINE config-1 size: size-independent identities (every latent gradient sums to
-  sum_i db1[i] W1[i][k]; gradients finite; loss finite).
+- a multi-step run: the loss after 2,000 steps within 2% of the oracle's, on a 128^2 material
+  against the C oracle and at full BASELINE config-1 size against its tensor restatement
+  (oracle/torch_oracle.py, pinned to the C oracle by tests/test_torch_oracle_cpu.py);
+- full BASELINE config-1 and config-2 size: one pass against the C oracle (same tolerances),
+  plus size-independent identities (every latent gradient sums to sum_i db1[i] W1[i][k]).
 """
 import ctypes as C
 import os
@@ -35,12 +37,25 @@ def _train_pass_gpu(tex, finalize=False):
             [_host(g) for g in tex.ggrads])
 
 
-def _oracle_pass(oracle, tex, finalize=False):
+def _oracle_pass(oracle, tex, finalize=False, threads=8):
     s = oracle.make_sampler(tex.image_w, tex.image_h, tex.lattice[0], tex.lattice[1], step=tex.step,
                             seed=tex.seed)
     return oracle.train_pass(oracle_model(oracle, tex), target_host(tex), s,
                              channel_weights=np.array(tex.channel_weights, np.float32), finalize=finalize,
-                             threads=8)
+                             threads=threads)
+
+
+def _assert_pass_matches(got, ref, label):
+    sse, gW, gb, gg = got
+    rsse, rW, rb, rg = ref
+    print(f"{label}: sse {sse:.6g} vs oracle {rsse:.6g}; rel-L2 dW {[round(rel_l2(gW[l], rW[l]), 6) for l in range(3)]}"
+          f" db {[round(rel_l2(gb[l], rb[l]), 6) for l in range(3)]} latents {[round(rel_l2(gg[g], rg[g]), 6) for g in range(2)]}")
+    assert abs(sse - rsse) <= 1e-3 * rsse, (sse, rsse)
+    for l in range(3):
+        assert rel_l2(gW[l], rW[l]) <= GRAD_TOL, f"dW{l}: {rel_l2(gW[l], rW[l])}"
+        assert rel_l2(gb[l], rb[l]) <= GRAD_TOL, f"db{l}: {rel_l2(gb[l], rb[l])}"
+    for g in range(2):
+        assert rel_l2(gg[g], rg[g]) <= GRAD_TOL, f"latent grid {g}: {rel_l2(gg[g], rg[g])}"
 
 
 CASES = [
@@ -206,50 +221,101 @@ def test_multi_step_loss_matches_oracle(cuda, oracle):
     assert abs(lg - lr_) <= 0.02 * lr_, (lg, lr_)
 
 
-def test_full_config1_step_identities(cuda):
-    """BASELINE config 1 at full size (1024^2 image, 512^2x8 + 256^2x8 latents, 262,144
-    samples): one pass; sum over texels of each latent gradient channel equals
-    sum_i db1[i] W1[i][k] (the Catmull-Rom weights of every sample sum to one)."""
-    import torch
-    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=21)
-    sse, gW, gb, gg = _train_pass_gpu(tex)
-    assert np.isfinite(sse) and sse > 0
-    for a in gW + gb + gg:
-        assert np.isfinite(a).all()
+def _latent_sum_identity(tex, gb, gg):
+    """Sum over texels of each latent gradient channel = sum_i db1[i] W1[i][k]: the
+    Catmull-Rom weights of every sample sum to one."""
+    C = tex.C
     W1 = _host(tex.W[0]).astype(np.float64).reshape(64, 32)
     db1 = gb[0].astype(np.float64)
     for g in range(2):
-        flat = gg[g].astype(np.float64).reshape(-1, 8)
+        flat = gg[g].astype(np.float64).reshape(-1, C)
         lhs = flat.sum(0)
-        rhs = db1 @ W1[:, g * 8:(g + 1) * 8]
+        rhs = db1 @ W1[:, g * C:(g + 1) * C]
         tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
         assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)
 
 
-def test_full_config2_step_identities(cuda):
+def test_full_config1_pass_matches_oracle(cuda, oracle):
+    """BASELINE config 1 at full size (1024^2 image, 512^2x8 + 256^2x8 latents, He-normal
+    weights, 262,144 samples): one training pass against the C oracle, every gradient buffer
+    at rel-L2 <= 2e-2 and the sum of squared errors within 1e-3."""
+    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=21)
+    tex.step = 5
+    got = _train_pass_gpu(tex)
+    for a in got[1] + got[2] + got[3]:
+        assert np.isfinite(a).all()
+    _latent_sum_identity(tex, got[2], got[3])
+    _assert_pass_matches(got, _oracle_pass(oracle, tex, threads=os.cpu_count() or 1), "config 1 pass")
+
+
+def test_full_config2_pass_matches_oracle(cuda, oracle):
     """BASELINE config 2 at full size (4096^2 PBR material with 12 channels, normals from the
-    height field; 1024^2x12 + 512^2x12 latents; 1,048,576 samples): the same identity per
-    latent channel, finite gradients, and unit-length target normals."""
-    import torch
+    height field; 1024^2x12 + 512^2x12 latents; 1,048,576 samples): unit-length target
+    normals, then one training pass against the C oracle with the config-1 tolerances."""
     import neural_textures_b200 as nt
     tex = nt.NeuralTexture(4096, 4096, grid_sizes=((1024, 1024), (512, 512)), latent_channels=12,
                            output_channels=12, device="cuda:0", lattice=(1024, 1024))
     tex.init(seed=22, pbr_normals=True)
+    tex.step = 2
     tgt = tex.target[::64, ::64].float().cpu().numpy().reshape(-1, 12)
     n = np.linalg.norm(tgt[:, 3:6] * 2.0 - 1.0, axis=1)  # normals stored as n * 0.5 + 0.5
     assert np.all(np.abs(n - 1.0) < 2e-2), (n.min(), n.max())
-    sse, gW, gb, gg = _train_pass_gpu(tex)
-    assert np.isfinite(sse) and sse > 0
-    for a in gW + gb + gg:
+    got = _train_pass_gpu(tex)
+    for a in got[1] + got[2] + got[3]:
         assert np.isfinite(a).all()
-    W1 = _host(tex.W[0]).astype(np.float64).reshape(64, 32)
-    db1 = gb[0].astype(np.float64)
-    for g in range(2):
-        flat = gg[g].astype(np.float64).reshape(-1, 12)
-        lhs = flat.sum(0)
-        rhs = db1 @ W1[:, g * 12:(g + 1) * 12]
-        tol = 1e-3 * np.abs(flat).sum(0) + 1e-2 * np.abs(rhs)
-        assert np.all(np.abs(lhs - rhs) <= tol), (lhs, rhs, tol)
+    _latent_sum_identity(tex, got[2], got[3])
+    _assert_pass_matches(got, _oracle_pass(oracle, tex, threads=os.cpu_count() or 1), "config 2 pass")
+
+
+def test_config1_2000_steps_loss_matches_oracle(cuda):
+    """North-star criterion at BASELINE config-1 size: 2,000 training steps (fused pass + fused
+    Adam, lr 1e-2 latents / 5e-3 network, beta1 0.9, beta2 0.99) on the 1024^2 material with
+    262,144 samples per step, against the same 2,000 steps of the oracle's tensor restatement
+    (oracle/torch_oracle.py) from the same fp16 state with the same samples.
+
+    - Steps 0-399: every step's loss agrees within 1e-3 (the two trainings follow the same
+      trajectory).
+    - After that the trajectories decorrelate: the float atomics of both sides sum in an
+      order that changes from run to run, and with these Adam settings the training shows
+      isolated loss spikes (single steps up to ~3x the level) whose timing follows from
+      those last-bit differences.  The loss after 2,000 steps is therefore measured as a
+      level: the mean of the losses of steps 1,500-1,999 without the 10% largest (the spike
+      steps).  The two levels agree within 2%.  Plain means and medians of several windows
+      are printed beside it."""
+    import torch
+    from oracle.torch_oracle import TorchTrainer
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n_steps = 2000
+    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=31)
+    grids, W, b = tex.host_model()
+    ref = TorchTrainer(grids, W, b, target_host(tex), 8, 8, (1024, 1024), (512, 512), tex.latent_adam,
+                       tex.network_adam, device="cuda:0")
+    losses_gpu = torch.zeros(n_steps, dtype=torch.float32, device="cuda:0")
+    for step in range(n_steps):
+        p = tex.params(step=step)
+        p.loss_accum = losses_gpu[step].data_ptr()
+        tex.train_step(params=p)
+    B = 512 * 512
+    losses_gpu = losses_gpu.cpu().numpy().astype(np.float64) / B
+    losses_ref = np.array([ref.step(step) for step in range(n_steps)]) / B
+    out = os.environ.get("NT_LOSS_CURVES")
+    if out:
+        np.savez(out, gpu=losses_gpu, oracle=losses_ref)
+
+    def level(x):
+        return float(x[x <= np.percentile(x, 90)].mean())
+
+    early = float(np.max(np.abs(losses_gpu[:400] / losses_ref[:400] - 1.0)))
+    print(f"config 1, steps 0-399: max per-step relative loss difference {early:.2e}")
+    for lo, hi in ((1000, 2000), (1500, 2000), (1900, 2000)):
+        g, r = losses_gpu[lo:hi], losses_ref[lo:hi]
+        print(f"config 1, steps {lo}-{hi - 1}, loss per sample: level gpu {level(g):.6f} oracle {level(r):.6f}; "
+              f"mean gpu {np.mean(g):.6f} oracle {np.mean(r):.6f}; median gpu {np.median(g):.6f} "
+              f"oracle {np.median(r):.6f}")
+    assert early <= 1e-3, early
+    lg, lr_ = level(losses_gpu[1500:]), level(losses_ref[1500:])
+    assert lg < 0.01 * losses_gpu[0], "training must reduce the loss"
+    assert abs(lg - lr_) <= 0.02 * lr_, (lg, lr_)
 
 
 def test_material_on_another_device(cuda):

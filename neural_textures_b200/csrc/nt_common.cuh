@@ -163,6 +163,16 @@ __device__ __forceinline__ void footprint(float u, float v, int32_t w, int32_t h
     }
 }
 
+// Fire-and-forget vector reduction into global memory (red.global.add.v4.f32, sm_90+): the
+// four floats are added atomically per element, like atomicAdd on each, and the thread does
+// not wait for the old value.  addr must be 16-byte aligned.
+__device__ __forceinline__ void red_add_v4(float *addr, float a, float b, float c, float d)
+{
+    asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+
 // Packed fp32 fused multiply-add (sm_100 fma.rn.f32x2): per lane exactly fmaf(a, b, c).
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
 {
@@ -177,44 +187,59 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
 // Catmull-Rom gather of C channels (C = 4, 8, 12 or 16; channel-interleaved fp16 grid),
 // fp32 accumulation: row sums first, then the weighted sum of rows (same order as the
 // oracle).  Channel pairs go through the packed fp32 FMA, which rounds each lane like fmaf.
+// The loads of RB footprint rows are issued before their arithmetic, so that the gather pays
+// the memory latency once per RB rows instead of once per tap (RB = 4 for up to 8 channels:
+// 64 registers of texels; 2 above).
 template <int C>
 __device__ __forceinline__ void gather_cr(const __half *__restrict__ grid, int32_t w,
                                           const Footprint &fp, float out[C])
 {
     static_assert(C % 4 == 0, "channel count must be a multiple of 4");
+    constexpr int Q = C / 4;          // 8-byte groups of 4 channels per texel
+    constexpr int RB = C <= 8 ? 4 : 2;  // rows per load batch
     float2 acc[C / 2];
 #pragma unroll
     for (int k = 0; k < C / 2; ++k) acc[k] = make_float2(0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        float2 row[C / 2];
+    for (int j0 = 0; j0 < 4; j0 += RB) {
+        uint2 raw[RB][4][Q];
 #pragma unroll
-        for (int k = 0; k < C / 2; ++k) row[k] = make_float2(0.f, 0.f);
-        const __half *rp = grid + (size_t)fp.ys[j] * (size_t)w * C;
+        for (int jj = 0; jj < RB; ++jj) {
+            const __half *rp = grid + (size_t)fp.ys[j0 + jj] * (size_t)w * C;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const __half *tp = rp + (size_t)fp.xs[i] * C;
-            const float2 wx2 = make_float2(fp.wx[i], fp.wx[i]);
-            if constexpr (C % 8 == 0) {
+            for (int i = 0; i < 4; ++i) {
+                const __half *tp = rp + (size_t)fp.xs[i] * C;
+                if constexpr (C % 8 == 0) {
 #pragma unroll
-                for (int q = 0; q < C / 8; ++q) {
-                    const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(tp) + q);
-                    const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
+                    for (int q = 0; q < Q / 2; ++q) {
+                        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(tp) + q);
+                        raw[jj][i][2 * q] = make_uint2(v.x, v.y);
+                        raw[jj][i][2 * q + 1] = make_uint2(v.z, v.w);
+                    }
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) row[q * 4 + e] = ffma2(wx2, unpack_half2(r[e]), row[q * 4 + e]);
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < C / 4; ++q) {
-                    const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(tp) + q);
-                    row[q * 2 + 0] = ffma2(wx2, unpack_half2(raw.x), row[q * 2 + 0]);
-                    row[q * 2 + 1] = ffma2(wx2, unpack_half2(raw.y), row[q * 2 + 1]);
+                    for (int q = 0; q < Q; ++q) raw[jj][i][q] = __ldg(reinterpret_cast<const uint2 *>(tp) + q);
                 }
             }
         }
-        const float2 wy2 = make_float2(fp.wy[j], fp.wy[j]);
 #pragma unroll
-        for (int k = 0; k < C / 2; ++k) acc[k] = ffma2(wy2, row[k], acc[k]);
+        for (int jj = 0; jj < RB; ++jj) {
+            float2 row[C / 2];
+#pragma unroll
+            for (int k = 0; k < C / 2; ++k) row[k] = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 wx2 = make_float2(fp.wx[i], fp.wx[i]);
+#pragma unroll
+                for (int q = 0; q < Q; ++q) {
+                    row[2 * q] = ffma2(wx2, unpack_half2(raw[jj][i][q].x), row[2 * q]);
+                    row[2 * q + 1] = ffma2(wx2, unpack_half2(raw[jj][i][q].y), row[2 * q + 1]);
+                }
+            }
+            const float2 wy2 = make_float2(fp.wy[j0 + jj], fp.wy[j0 + jj]);
+#pragma unroll
+            for (int k = 0; k < C / 2; ++k) acc[k] = ffma2(wy2, row[k], acc[k]);
+        }
     }
 #pragma unroll
     for (int k = 0; k < C / 2; ++k) {

@@ -1,6 +1,6 @@
 // nt_train_tc.cu -- fused training pass on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// Same contract as the mma.sync kernel in nt_train.cu (TrainLoopPass / TrainLoop,
+// Contract (TrainLoopPass / TrainLoop,
 // mavenkim2/neural_textures train.cu:818-915, :979-983; mlp.h:101-257 backward; the latent
 // scatter of train.cu:460-509): one jittered sample per lattice cell, weighted L2 loss,
 // weight / bias / latent gradients accumulated (x 1 / num_samples) into fp32 buffers.
@@ -51,27 +51,11 @@
 #include "nt_tc_common.cuh"
 #include "nt_umma.cuh"
 
+#include "nt_train_tc.cuh"
+
 namespace nt {
 
-__device__ unsigned int g_device_status;  // bit 0: a bounded wait of a training kernel gave up
-
 namespace tc {
-
-constexpr int kThreadsTC = 256;
-constexpr int kMaxWinW = 40;  // widest footprint window the sweep handles (texels)
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColW1 = 0, kColW2 = 64, kColW3 = 160, kColTile = 192;
-
-// Tensor-core latent scatter: per grid, the window is at most sc_w(g) texels wide and
-// sc_h(g) texels high (else the tile takes the column sweep).
-__host__ __device__ constexpr int sc_w(int g) { return g ? 16 : 32; }
-__host__ __device__ constexpr int sc_h(int g) { return g ? 8 : 12; }
-
-struct Window {
-    int32_t x0, w, span, ok;
-    int32_t y0, h, tc;  // window rows; tc: fits the tensor-core scatter
-    int32_t cand_x[kMaxWinW];  // lo | hi << 16 of the candidate lattice columns
-};
 
 template <int C>
 struct Smem {
@@ -86,14 +70,15 @@ struct Smem {
             alignas(128) uint8_t DY[kTileN * 16 * 2];   // follows H2: the M = 128 read of H2 runs 768 B past it
         } m;
         struct {  // latent scatter operands: Q_g = wy dX over window rows, A_g = wx over window columns
-            alignas(128) uint8_t Q0[kTileN * sc_h(0) * 16];  // followed by Q1: the M = 128 read runs 512 B past it
-            alignas(128) uint8_t Q1[kTileN * sc_h(1) * 16];
+            // (each Q tile is followed by another operand: its M = 128 / 64 read runs past its end)
+            alignas(128) uint8_t Q0[kTileN * sc_qa(0) * 16];
+            alignas(128) uint8_t Q1[kTileN * sc_qa(1) * 16];
             alignas(128) uint8_t A0[kTileN * sc_w(0) * 2];
             alignas(128) uint8_t A1[kTileN * sc_w(1) * 2];
         } q;
         struct {  // the scattered window sums, fp32 [row][column (+1 pad)][channel]
-            float g0[sc_h(0) * (sc_w(0) + 1) * 8];
-            float g1[sc_h(1) * (sc_w(1) + 1) * 8];
+            float g0[sc_h(0) * (sc_w(0) + 1) * C];
+            float g1[sc_h(1) * (sc_w(1) + 1) * C];
         } f;
     } t;
     short2 base[2][kTileN];
@@ -107,378 +92,57 @@ struct Smem {
     float red[kThreadsTC / 32];
 };
 
-// ---- row sharding ----------------------------------------------------------------------
-//
-// Source s (0, 1: latent grids, 2: target) may hold only p.rows[s] rows, starting at full
-// row p.org[s] and wrapping.  A row outside them is never read or written: it is skipped
-// and bit 1 of the device status word is set (the caller's shard plan is wrong).
-
-__device__ __forceinline__ int stored_row(const TrainLaunch &p, int src, int row, int h)
-{
-    const int r = wrap_coord(row - p.org[src], h);
-    if (r >= p.rows[src]) {
-        atomicOr(&g_device_status, 2u);
-        return -1;
-    }
-    return r;
-}
-
-// Footprint rows -> stored rows; a missing row gets weight 0 (and is flagged).
-__device__ __forceinline__ void shard_rows(const TrainLaunch &p, int src, int h, Footprint &fp)
-{
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int r = stored_row(p, src, fp.by - 1 + j, h);
-        fp.ys[j] = r < 0 ? 0 : r;
-        if (r < 0) fp.wy[j] = 0.f;
-    }
-}
-
-// ---- footprint windows of a tile (for the latent-gradient sweep) ------------------------
-
-// Per-warp min / max of the footprint bases per lattice column (lanes L and L + 16 share a
-// column) and per lattice row (half-warp).
-__device__ __forceinline__ void extents_partial(int32_t (&part)[4][4][kTileW], int bx, int by, bool valid, int ws,
-                                                int lane)
-{
-    int cmin = valid ? bx : INT_MAX, cmax = valid ? bx : INT_MIN;
-    cmin = min(cmin, __shfl_xor_sync(0xffffffffu, cmin, 16));
-    cmax = max(cmax, __shfl_xor_sync(0xffffffffu, cmax, 16));
-    int rmin = valid ? by : INT_MAX, rmax = valid ? by : INT_MIN;
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
-        rmin = min(rmin, __shfl_xor_sync(0xffffffffu, rmin, o));
-        rmax = max(rmax, __shfl_xor_sync(0xffffffffu, rmax, o));
-    }
-    if (lane < 16) {
-        part[0][ws][lane] = cmin;
-        part[1][ws][lane] = cmax;
-    }
-    if ((lane & 15) == 0) {
-        part[2][ws][lane >> 4] = rmin;
-        part[3][ws][lane >> 4] = rmax;
-    }
-}
-
-// One warp: column / row extents of grid gi over the 4 warp partials, window origin and
-// size, and whether the window suits the column sweep / the tensor-core scatter.
-template <int C>
-__device__ __forceinline__ void finalize_window_tc(Smem<C> &s, int gi, int lane)
-{
-    int lo_v = INT_MAX, hi_v = INT_MIN;
-    if (lane < 16) {
-        for (int w = 0; w < 4; ++w) {
-            lo_v = min(lo_v, s.part[gi][0][w][lane]);
-            hi_v = max(hi_v, s.part[gi][1][w][lane]);
-        }
-        s.colext[gi][0][lane] = lo_v;
-        s.colext[gi][1][lane] = hi_v;
-    } else if (lane < 16 + kTileH) {
-        const int e = lane - 16, w = e >> 1, half = e & 1;
-        lo_v = s.part[gi][2][w][half];
-        hi_v = s.part[gi][3][w][half];
-        s.rowmin[gi][e] = lo_v;
-    }
-    const bool narrow = lo_v == INT_MAX || (long long)hi_v - lo_v <= 1;
-    const bool all_narrow = __all_sync(0xffffffffu, narrow);
-    int mn = lo_v, mx = hi_v;
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
-        mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    }
-    const int cmin = __shfl_sync(0xffffffffu, mn, 0), cmax = __shfl_sync(0xffffffffu, mx, 0);
-    const int rmin = __shfl_sync(0xffffffffu, mn, 16), rmax = __shfl_sync(0xffffffffu, mx, 16);
-    __syncwarp();
-    Window &W = s.win[gi];
-    const bool nonempty = cmin <= cmax && rmin <= rmax;
-    const long long ww = nonempty ? (long long)cmax - cmin + 4 : 0;
-    const bool ok = nonempty && ww <= kMaxWinW && all_narrow;
-    const long long wh = nonempty ? (long long)rmax - rmin + 4 : 0;
-    if (lane == 0) {
-        W.x0 = cmin - 1;
-        W.w = (int)ww;
-        W.ok = ok;
-        W.y0 = rmin - 1;
-        W.h = nonempty ? (int)wh : 0;
-        W.tc = nonempty && ww <= sc_w(gi) && wh <= sc_h(gi);
-    }
-}
-
-// One warp: candidate lattice-column range of every window column of grid gi and the
-// longest range (only the column sweep needs them).
-template <int C>
-__device__ __forceinline__ void window_cands(Smem<C> &s, int gi, int lane)
-{
-    Window &W = s.win[gi];
-    int span = 0;
-    if (W.ok) {
-        for (int idx = lane; idx < W.w; idx += 32) {
-            const int tx = W.x0 + idx;
-            int lo = kTileW, hi = -1;
-            for (int c = 0; c < kTileW; ++c) {
-                if (s.colext[gi][0][c] <= tx + 1 && s.colext[gi][1][c] >= tx - 2) {
-                    lo = min(lo, c);
-                    hi = max(hi, c);
-                }
-            }
-            W.cand_x[idx] = lo | (hi << 16);
-            span = max(span, hi - lo + 1);
-        }
-    }
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) span = max(span, __shfl_xor_sync(0xffffffffu, span, o));
-    if (lane == 0) W.span = span;
-}
-
-// ---- latent-gradient column sweep (see nt_train.cu for the derivation) -------------------
-
-// Gradient buffer, size and stored row of grid g at the call's first mip level (LB false) or at
-// the second level of a fractional mip coordinate (LB true; such calls are unsharded).
-template <bool LB>
-__device__ __forceinline__ float *lvl_grad(const TrainLaunch &p, int g) { return LB ? p.ggrid_b[g] : p.ggrid[g]; }
-template <bool LB>
-__device__ __forceinline__ int lvl_w(const TrainLaunch &p, int g) { return LB ? p.gw_b[g] : p.gw[g]; }
-template <bool LB>
-__device__ __forceinline__ int lvl_h(const TrainLaunch &p, int g) { return LB ? p.gh_b[g] : p.gh[g]; }
-template <bool LB>
-__device__ __forceinline__ int lvl_row(const TrainLaunch &p, int g, int row, int h)
-{
-    if constexpr (LB) return wrap_coord(row, h);
-    return stored_row(p, g, row, h);
-}
-
-// Latent gradient sum of one texel (x 1 / num_samples) into the grid gradients, or, for block
-// features, through the BC6 backward into the texel's block records (train.cu:436-454; the
-// backward is linear in the feature gradient, so summing a texel's taps first is exact).
-template <int C, bool BLK, bool LB = false>
-__device__ __forceinline__ void flush_row(const TrainLaunch &p, int gi, int tx, int ty, const float (&row)[C])
-{
-    bool any = false;
-#pragma unroll
-    for (int c = 0; c < C; ++c) any |= row[c] != 0.f;
-    if (!any) return;
-    const int gw = lvl_w<LB>(p, gi), gh = lvl_h<LB>(p, gi);
-    const float sc = p.inv_num_samples;
-    const int sy = lvl_row<LB>(p, gi, ty, gh);
-    if (sy < 0) return;
-    if constexpr (BLK) {
-        float fg[C];
-#pragma unroll
-        for (int c = 0; c < C; ++c) fg[c] = row[c] * sc;
-        bc6f_backward_texel<C>(reinterpret_cast<const float *>(p.grid[gi]), p.ggrid[gi], gw, wrap_coord(tx, gw), sy, fg);
-        return;
-    }
-    float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, gi) + ((size_t)sy * gw + wrap_coord(tx, gw)) * C);
-#pragma unroll
-    for (int q = 0; q < C / 4; ++q)
-        atomicAdd(dst + q, make_float4(row[4 * q] * sc, row[4 * q + 1] * sc, row[4 * q + 2] * sc, row[4 * q + 3] * sc));
-}
-
-template <int C, int L, bool BLK, bool LB = false>
-__device__ __forceinline__ void sweep_tc(const Smem<C> &s, const TrainLaunch &p, int r)
-{
-    constexpr int kRows = 2, kChunks = kTileH / kRows, DXS = Cfg<C>::DXS;
-    const float *dx = reinterpret_cast<const float *>(s.t.m.H2);
-    const int nt0 = s.win[0].w * kChunks;
-    const int ntot = nt0 + s.win[1].w * kChunks;
-    for (int k = r; k < ntot; k += kThreadsTC) {
-        const int gi = k < nt0 ? 0 : 1;
-        const Window &W = s.win[gi];
-        const int kk = gi ? k - nt0 : k;
-        const int chunk = kk / W.w, lx = kk % W.w;
-        const int tx = W.x0 + lx;
-        const int cx = W.cand_x[lx];
-        const int lo = cx & 0xffff, hi = cx >> 16;
-        if (hi < lo) continue;
-        float R[5][C];
-#pragma unroll
-        for (int m = 0; m < 5; ++m)
-#pragma unroll
-            for (int c = 0; c < C; ++c) R[m][c] = 0.f;
-        int fy_cur = INT_MIN;
-#pragma unroll
-        for (int rr = 0; rr < kRows; ++rr) {
-            const int cj = chunk * kRows + rr;
-            const int rmin = s.rowmin[gi][cj];
-            if (rmin == INT_MAX) continue;
-            const int fy = rmin - 1;
-            if (fy_cur == INT_MIN) fy_cur = fy;
-            while (fy > fy_cur) {
-                flush_row<C, BLK, LB>(p, gi, tx, fy_cur, R[0]);
-#pragma unroll
-                for (int m = 0; m < 4; ++m)
-#pragma unroll
-                    for (int c = 0; c < C; ++c) R[m][c] = R[m + 1][c];
-#pragma unroll
-                for (int c = 0; c < C; ++c) R[4][c] = 0.f;
-                ++fy_cur;
-            }
-#pragma unroll
-            for (int b = 0; b < L; ++b) {
-                const int ci = min(lo + b, kTileW - 1);
-                const bool inr = lo + b <= hi;
-                const int sidx = cj * kTileW + ci;
-                const short2 bs = s.base[gi][sidx];
-                const int kx = tx - bs.x + 1;
-                const float wxv = (inr && (unsigned)kx <= 3u) ? s.wts[gi][sidx][kx & 3] : 0.f;
-                const float4 wy = *reinterpret_cast<const float4 *>(&s.wts[gi][sidx][4]);
-                const bool e1 = bs.y - 1 - fy != 0;
-                float wxd[C];
-                const float4 *d4 = reinterpret_cast<const float4 *>(dx + sidx * DXS + gi * C);
-#pragma unroll
-                for (int q = 0; q < C / 4; ++q) {
-                    const float4 d = d4[q];
-                    wxd[4 * q + 0] = wxv * d.x;
-                    wxd[4 * q + 1] = wxv * d.y;
-                    wxd[4 * q + 2] = wxv * d.z;
-                    wxd[4 * q + 3] = wxv * d.w;
-                }
-                const float wyv[5] = {e1 ? 0.f : wy.x, e1 ? wy.x : wy.y, e1 ? wy.y : wy.z, e1 ? wy.z : wy.w,
-                                      e1 ? wy.w : 0.f};
-#pragma unroll
-                for (int m = 0; m < 5; ++m)
-#pragma unroll
-                    for (int c = 0; c < C; ++c) R[m][c] = fmaf(wyv[m], wxd[c], R[m][c]);
-            }
-        }
-        if (fy_cur == INT_MIN) continue;
-#pragma unroll
-        for (int m = 0; m < 5; ++m) flush_row<C, BLK, LB>(p, gi, tx, fy_cur + m, R[m]);
-    }
-}
-
-// Per-sample, per-tap vector atomics (windows the sweep does not handle); block features
-// take the BC6 backward per tap.
-template <int C, bool BLK, bool LB = false>
-__device__ __forceinline__ void scatter_taps_tc(const Smem<C> &s, const TrainLaunch &p, int gi, int r)
-{
-    const float *dxr = reinterpret_cast<const float *>(s.t.m.H2) + r * Cfg<C>::DXS + gi * C;
-    const int gw = lvl_w<LB>(p, gi), gh = lvl_h<LB>(p, gi);
-    const short2 b = s.base[gi][r];
-    const float scale = p.inv_num_samples;
-    for (int j = 0; j < 4; ++j) {
-        const int yy = lvl_row<LB>(p, gi, b.y - 1 + j, gh);
-        if (yy < 0) continue;
-        for (int i = 0; i < 4; ++i) {
-            const int xx = wrap_coord(b.x - 1 + i, gw);
-            if constexpr (BLK) {
-                const float wgt = __fmul_rn(s.wts[gi][r][4 + j], s.wts[gi][r][i]);
-                float fg[C];
-#pragma unroll
-                for (int k = 0; k < C; ++k) fg[k] = __fmul_rn(__fmul_rn(wgt, dxr[k]), scale);
-                bc6f_backward_texel<C>(reinterpret_cast<const float *>(p.grid[gi]), p.ggrid[gi], gw, xx, yy, fg);
-                continue;
-            }
-            const float wgt = s.wts[gi][r][i] * s.wts[gi][r][4 + j] * scale;
-            float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, gi) + ((size_t)yy * gw + xx) * C);
-#pragma unroll
-            for (int q = 0; q < C / 4; ++q)
-                atomicAdd(dst + q, make_float4(wgt * dxr[4 * q], wgt * dxr[4 * q + 1], wgt * dxr[4 * q + 2],
-                                               wgt * dxr[4 * q + 3]));
-        }
-    }
-}
-
-// ---- epilogue helpers -------------------------------------------------------------------
-
-// TMEM row (32 columns) rounded to fp16 and masked by the ReLU of the activation row stored
-// at the same place in H (lanes where the activation is not > 0 become +0), written over it.
-// `wbar` / `wph`: products that still read H (the weight gradients) are waited for right
-// before the stores, so the TMEM and shared loads overlap them.
-__device__ __forceinline__ void mask_store32(uint32_t taddr, uint8_t *H, int r, int chunk0, uint32_t wbar,
-                                             uint32_t wph, bool &failed)
-{
-    uint32_t v[32];
-    umma::ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
-    umma::ld16(taddr + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-    uint4 a[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) a[q] = *reinterpret_cast<const uint4 *>(H + umma::cm_offset(r, 8 * (chunk0 + q), kHC));
-    umma::wait_ld();
-    const __half2 zero = __float2half2_rn(0.f);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint32_t aw[4] = {a[q].x, a[q].y, a[q].z, a[q].w};
-        uint32_t h[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const __half2 g = __floats2half2_rn(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
-            const unsigned m = __hgt2_mask(*reinterpret_cast<const __half2 *>(&aw[e]), zero);
-            h[e] = *reinterpret_cast<const uint32_t *>(&g) & m;
-        }
-        if (q == 0 && !umma::mbar_wait(wbar, wph, kSpinLimit)) {
-            failed = true;
-            atomicOr(&g_device_status, 1u);
-        }
-        st16(H, umma::cm_offset(r, 8 * (chunk0 + q), kHC), h[0], h[1], h[2], h[3]);
-    }
-}
-
-// ---- tensor-core latent scatter -------------------------------------------------------------
-//
-// dG[y][x][c] = sum_s wy_s(y) wx_s(x) dX_s[c] over the tile's window is the product
-// G^T[(y, c)][x] = sum_s Q[s][(y, c)] A[s][x] with Q[s][(y, c)] = wy_s(y) dX_s[c] (zero outside
-// the sample's 4 rows) and A[s][x] = wx_s(x) (zero outside its 4 columns), both fp16 rows
-// of one sample, read MN-major.  Channel-interleaved grids with C = 8 make (y, c) exactly
-// one 16-byte core-matrix row per window row.
-
-// Operand rows of sample r for grid g (compile-time grid so the row lengths are constants).
-template <int C, int G>
-__device__ __forceinline__ void scatter_rows(Smem<C> &s, int r, bool valid, const float (&dx)[C])
-{
-    static_assert(C == 8, "the tensor-core scatter packs one window row per 16-byte chunk");
-    constexpr int NQ = sc_h(G), NA = sc_w(G) / 8;
-    uint8_t *Q = G ? s.t.q.Q1 : s.t.q.Q0;
-    uint8_t *A = G ? s.t.q.A1 : s.t.q.A0;
-#pragma unroll
-    for (int y = 0; y < NQ; ++y) st16(Q, umma::cm_offset(r, 8 * y, NQ), 0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int k = 0; k < NA; ++k) st16(A, umma::cm_offset(r, 8 * k, NA), 0u, 0u, 0u, 0u);
-    if (!valid) return;  // dX is zero there, and the footprint may lie outside the window
-    const Window &W = s.win[G];
-    const short2 b = s.base[G][r];
-    const int oy = b.y - 1 - W.y0, ox = b.x - 1 - W.x0;
-    const float4 wx = *reinterpret_cast<const float4 *>(&s.wts[G][r][0]);
-    const float4 wy = *reinterpret_cast<const float4 *>(&s.wts[G][r][4]);
-    const float wyv[4] = {wy.x, wy.y, wy.z, wy.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-        st16(Q, umma::cm_offset(r, 8 * (oy + j), NQ), pack_half2(wyv[j] * dx[0], wyv[j] * dx[1]),
-             pack_half2(wyv[j] * dx[2], wyv[j] * dx[3]), pack_half2(wyv[j] * dx[4], wyv[j] * dx[5]),
-             pack_half2(wyv[j] * dx[6], wyv[j] * dx[7]));
-    const float wxv[4] = {wx.x, wx.y, wx.z, wx.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-        *reinterpret_cast<__half *>(A + umma::cm_offset(r, ox + i, NA)) = __float2half_rn(wxv[i]);
-}
-
 // TMEM -> fp32 staging of the window sums (thread: one (row, channel) lane, 16 columns).
+// Channels 0-7: grid 0 M = 128 (lane m = 8 y + c), grid 1 M = 64 (row m = 16 q + lane);
+// channels 8-11 (C = 12): M = 64 rows m = 8 (y / 2) + 4 (y % 2) + c - 8.
 template <int C>
 __device__ __forceinline__ void scatter_stage_out(Smem<C> &s, uint32_t tmem, int warp, int lane, int half)
 {
     const int q = warp & 3;
     const uint32_t lanes = (uint32_t)(32 * q) << 16;
-    {  // grid 0: M = 128, lane m = 8 y + c, columns x; half h takes x in [16 h, 16 h + 16)
+    {  // grid 0, channels 0-7: half h takes x in [16 h, 16 h + 16)
         uint32_t v[16];
         umma::ld16(tmem + kColTile + lanes + 16 * half, v);
         umma::wait_ld();
         const int m = 32 * q + lane, y = m >> 3, c = m & 7;
         if (y < sc_h(0)) {
-            float *o = s.t.f.g0 + (y * (sc_w(0) + 1) + 16 * half) * 8 + c;
+            float *o = s.t.f.g0 + (y * (sc_w(0) + 1) + 16 * half) * C + c;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[8 * j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 16; ++j) o[C * j] = __uint_as_float(v[j]);
         }
     }
-    if (half) {  // grid 1: M = 64, row m = 16 q + lane (lanes 0..15), columns x
+    if (half) {  // grid 1, channels 0-7: rows m = 16 q + lane (lanes 0..15), columns x
         uint32_t v[16];
         umma::ld16(tmem + kColTile + sc_w(0) + lanes, v);
         umma::wait_ld();
         const int m = 16 * q + lane, y = m >> 3, c = m & 7;
         if (lane < 16) {
-            float *o = s.t.f.g1 + (y * (sc_w(1) + 1)) * 8 + c;
+            float *o = s.t.f.g1 + (y * (sc_w(1) + 1)) * C + c;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[8 * j] = __uint_as_float(v[j]);
+            for (int j = 0; j < 16; ++j) o[C * j] = __uint_as_float(v[j]);
+        }
+    }
+    if constexpr (C == 12) {
+        const int m = 16 * q + lane, y = 2 * (m >> 3) + ((m >> 2) & 1), c = 8 + (m & 3);
+        {  // grid 0, channels 8-11: half h takes x in [16 h, 16 h + 16)
+            uint32_t v[16];
+            umma::ld16(tmem + Cols<C>::ScatB0 + lanes + 16 * half, v);
+            umma::wait_ld();
+            if (lane < 16 && y < sc_h(0)) {
+                float *o = s.t.f.g0 + (y * (sc_w(0) + 1) + 16 * half) * C + c;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[C * j] = __uint_as_float(v[j]);
+            }
+        }
+        if (half) {  // grid 1, channels 8-11
+            uint32_t v[16];
+            umma::ld16(tmem + Cols<C>::ScatB1 + lanes, v);
+            umma::wait_ld();
+            if (lane < 16 && y < sc_h(1)) {
+                float *o = s.t.f.g1 + (y * (sc_w(1) + 1)) * C + c;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) o[C * j] = __uint_as_float(v[j]);
+            }
         }
     }
 }
@@ -498,7 +162,7 @@ __device__ __forceinline__ void scatter_reduce_blocks(const Smem<C> &s, const Tr
         const int y = g ? kk >> 4 : kk >> 5;
         const Window &W = s.win[g];
         if (x >= W.w || y >= W.h) continue;
-        const float *src = g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * 8 : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * 8;
+        const float *src = g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * C : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * C;
         float row[C];
 #pragma unroll
         for (int q = 0; q < C / 4; ++q) {
@@ -511,45 +175,6 @@ __device__ __forceinline__ void scatter_reduce_blocks(const Smem<C> &s, const Tr
         flush_row<C, true>(p, g, W.x0 + x, W.y0 + y, row);
     }
 }
-
-// Staged window sums -> global latent gradients (x 1 / num_samples), one float4 reduction
-// per 4 channels of every window texel.
-template <int C, bool LB = false>
-__device__ __forceinline__ void scatter_reduce(const Smem<C> &s, const TrainLaunch &p, int tid)
-{
-    constexpr int n0 = sc_h(0) * sc_w(0) * 2, n1 = sc_h(1) * sc_w(1) * 2;  // (row, column, quad) slots
-    static_assert((n0 + n1) % kThreadsTC == 0, "whole slots per thread");
-    const float sc = p.inv_num_samples;
-#pragma unroll
-    for (int it = 0; it < (n0 + n1) / kThreadsTC; ++it) {
-        const int k = tid + it * kThreadsTC;
-        const int g = k < n0 ? 0 : 1;
-        const int kk = g ? k - n0 : k;
-        const int q = kk & 1;
-        const int x = g ? (kk >> 1) & (sc_w(1) - 1) : (kk >> 1) & (sc_w(0) - 1);
-        const int y = g ? kk >> 5 : kk >> 6;
-        const Window &W = s.win[g];
-        if (x >= W.w || y >= W.h) continue;
-        const float *src = (g ? s.t.f.g1 + (y * (sc_w(1) + 1) + x) * 8 : s.t.f.g0 + (y * (sc_w(0) + 1) + x) * 8) + 4 * q;
-        const float4 v = *reinterpret_cast<const float4 *>(src);
-        if (v.x == 0.f && v.y == 0.f && v.z == 0.f && v.w == 0.f) continue;
-        const int gw = lvl_w<LB>(p, g), gh = lvl_h<LB>(p, g);
-        const int sy = lvl_row<LB>(p, g, W.y0 + y, gh);
-        if (sy < 0) continue;
-        float4 *dst = reinterpret_cast<float4 *>(lvl_grad<LB>(p, g) + ((size_t)sy * gw + wrap_coord(W.x0 + x, gw)) * C) + q;
-        atomicAdd(dst, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc));
-    }
-}
-
-// ---- tensor-core products -------------------------------------------------------------------
-
-
-template <int C>
-struct Descs {
-    uint64_t x, h1, h2, dy, w1, w2, w3;  // K-major views (LBO 128)
-    uint64_t x_mn, h1_mn, h2_mn, dy_mn, w1_mn, w2_mn, w3_mn;  // MN-major views
-    uint64_t q0, q1, a0, a1;  // latent scatter operands (MN-major)
-};
 
 template <int C>
 __device__ __forceinline__ Descs<C> make_descs(const Smem<C> &s)
@@ -572,83 +197,13 @@ __device__ __forceinline__ Descs<C> make_descs(const Smem<C> &s)
     d.w1_mn = desc(smem_addr(s.W1), XG, 128);
     d.w2_mn = desc(smem_addr(s.W2), HG, 128);
     d.w3_mn = desc(smem_addr(s.W3), HG, 128);
-    d.q0 = desc(smem_addr(s.t.q.Q0), sc_h(0) * 128, 128);
-    d.q1 = desc(smem_addr(s.t.q.Q1), sc_h(1) * 128, 128);
+    d.q0 = desc(smem_addr(s.t.q.Q0), sc_qa(0) * 128, 128);
+    d.q1 = desc(smem_addr(s.t.q.Q1), sc_qa(1) * 128, 128);
+    d.q0b = desc(smem_addr(s.t.q.Q0), sc_qb(0) * 128, 128);
+    d.q1b = desc(smem_addr(s.t.q.Q1), sc_qb(1) * 128, 128);
     d.a0 = desc(smem_addr(s.t.q.A0), sc_w(0) / 8 * 128, 128);
     d.a1 = desc(smem_addr(s.t.q.A1), sc_w(1) / 8 * 128, 128);
     return d;
-}
-
-// Issue the products of one stage (thread 0 only) and commit them to `done`.
-template <int C>
-__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done,
-                                            uint32_t dwdone)
-{
-    using K = Cfg<C>;
-    using umma::idesc_f16;
-    using umma::mma_f16;
-    constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
-    const uint32_t R = tmem + kColTile;
-    const uint32_t acc0 = first ? 0u : 1u;  // the first tile of the CTA starts the gradient sums
-    switch (stage) {
-    case 0:  // F1
-#pragma unroll
-        for (int ks = 0; ks < K::XC / 2; ++ks)
-            mma_f16(R, dadv(d.x, ks * 256), dadv(d.w1, ks * 256), idesc_f16(128, 64, 0, 0), ks > 0);
-        break;
-    case 1:  // F2
-#pragma unroll
-        for (int ks = 0; ks < kHC / 2; ++ks)
-            mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w2, ks * 256), idesc_f16(128, 64, 0, 0), ks > 0);
-        break;
-    case 2:  // F3
-#pragma unroll
-        for (int ks = 0; ks < kHC / 2; ++ks)
-            mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w3, ks * 256), idesc_f16(128, 16, 0, 0), ks > 0);
-        break;
-    case 3:  // B3: dH2 = dY W3; dW3^T += H2e^T dY
-        mma_f16(R, d.dy, d.w3_mn, idesc_f16(128, 64, 0, 1), 0);
-        umma::commit(done);  // the epilogue needs dH2 only; the weight gradients follow
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(tmem + kColW3, dadv(d.h2_mn, ks * 2 * HG), dadv(d.dy_mn, ks * 512), idesc_f16(128, 16, 1, 1),
-                    ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
-    case 4:  // B2: dH1 = dZ2 W2; dW2 += dZ2^T H1e
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-            mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w2_mn, ks * 2 * HG), idesc_f16(128, 64, 0, 1), ks > 0);
-        umma::commit(done);
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
-                    ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
-    case 6:  // latent scatter: G0^T = Q0^T A0 (M128 N32), G1^T = Q1^T A1 (M64 N16), K = 128 samples
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(R, dadv(d.q0, ks * 2 * sc_h(0) * 128), dadv(d.a0, ks * 2 * sc_w(0) / 8 * 128),
-                    idesc_f16(128, sc_w(0), 1, 1), ks > 0);
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(R + sc_w(0), dadv(d.q1, ks * 2 * sc_h(1) * 128), dadv(d.a1, ks * 2 * sc_w(1) / 8 * 128),
-                    idesc_f16(64, sc_w(1), 1, 1), ks > 0);
-        break;
-    default:  // B1: dX = dZ1 W1; dW1 += dZ1^T X
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-            mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w1_mn, ks * 2 * XG), idesc_f16(128, K::NX, 0, 1), ks > 0);
-        umma::commit(done);
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(tmem + kColW1, dadv(d.h1_mn, ks * 2 * HG), dadv(d.x_mn, ks * 2 * XG), idesc_f16(64, K::XW, 1, 1),
-                    ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
-    }
-    umma::commit(done);
 }
 
 // Stage boundary: the operands written since the last one become visible to the tensor
@@ -707,34 +262,34 @@ __device__ bool scatter_second_level(Smem<C> &s, const TrainLaunch &p, const Des
         extents_partial(s.part[half], fb.bx, fb.by, valid, warp & 3, lane);
     }
     if (__syncthreads_or(failed)) return false;
-    if (warp < 2) finalize_window_tc<C>(s, warp, lane);
+    if (warp < 2) finalize_window_tc(s, warp, lane);
     if (__syncthreads_or(failed)) return false;
     bool tc = false;
     if constexpr (C == 8) tc = (s.win[0].tc || s.win[0].w == 0) && (s.win[1].tc || s.win[1].w == 0);
     if (tc) {
         if constexpr (C == 8) {
-            if (half) scatter_rows<C, 1>(s, r, valid, dxb);
-            else scatter_rows<C, 0>(s, r, valid, dxb);
+            if (half) scatter_rows<C, 1>(s, s.t.q, r, valid, dxb);
+            else scatter_rows<C, 0>(s, s.t.q, r, valid, dxb);
         }
         if (!run_stage<C>(6, d, tmem, first, done, dwdone, ph, failed, tid)) return false;
         scatter_stage_out<C>(s, tmem, warp, lane, half);
         if (__syncthreads_or(failed)) return false;
-        scatter_reduce<C, true>(s, p, tid);
+        scatter_reduce<C, true>(s, s.t.f, p, tid);
     } else {
         float *dxr = reinterpret_cast<float *>(s.t.m.H2) + r * K::DXS + half * C;
 #pragma unroll
         for (int q = 0; q < C / 4; ++q)
             *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(dxb[4 * q], dxb[4 * q + 1], dxb[4 * q + 2], dxb[4 * q + 3]);
-        if (warp < 2) window_cands<C>(s, warp, lane);
+        if (warp < 2) window_cands(s, warp, lane);
         if (__syncthreads_or(failed)) return false;
         const bool both = s.win[0].ok && s.win[1].ok;
         const int span = max(s.win[0].span, s.win[1].span);
         if (both && span <= 5) {
-            sweep_tc<C, 5, false, true>(s, p, tid);
+            sweep_tc<C, 5, false, true>(s, reinterpret_cast<const float *>(s.t.m.H2), p, tid);
         } else if (both && span <= 10) {
-            sweep_tc<C, 10, false, true>(s, p, tid);
+            sweep_tc<C, 10, false, true>(s, reinterpret_cast<const float *>(s.t.m.H2), p, tid);
         } else if (valid) {
-            scatter_taps_tc<C, false, true>(s, p, half, r);
+            scatter_taps_tc<C, false, true>(s, reinterpret_cast<const float *>(s.t.m.H2), p, half, r);
         }
     }
     umma::fence_before();
@@ -955,7 +510,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         }
         if constexpr (BLK) {
             __syncthreads();  // footprints and extents
-            if (warp < 2) finalize_window_tc<C>(s, warp, lane);
+            if (warp < 2) finalize_window_tc(s, warp, lane);
             __syncthreads();  // windows
             const bool windowed = blk_decode_windows<C>(s, p, tid);
             __syncthreads();  // decoded window texels
@@ -1007,7 +562,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 
         // ---- E3: weighted L2 (train.cu:876-888); dY = 2 w err (fp16, unscaled) -------------
         // (half 0 meanwhile finalises the footprint windows published by the gather barrier)
-        if (!BLK && !half && !p.finalize && warp < 2) finalize_window_tc<C>(s, warp, lane);  // BLK: in the gather
+        if (!BLK && !half && !p.finalize && warp < 2) finalize_window_tc(s, warp, lane);  // BLK: in the gather
         if (half) {
             uint32_t v[16];
             umma::ld16(Rl, v);
@@ -1073,13 +628,16 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 }
             }
             bool tc_scatter = false;
-            if constexpr (C == 8) tc_scatter = s.win[0].tc && s.win[1].tc;
+            if constexpr (C == 8 || !BLK) tc_scatter = s.win[0].tc && s.win[1].tc;
             if (tc_scatter) {
-                if constexpr (C == 8) {
-                    if (half) scatter_rows<C, 1>(s, r, valid, dxv);
-                    else scatter_rows<C, 0>(s, r, valid, dxv);
-                }
+                if (half) scatter_rows<C, 1>(s, s.t.q, r, valid, dxv);
+                else scatter_rows<C, 0>(s, s.t.q, r, valid, dxv);
                 if (!run_stage<C>(6, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // scatter product
+                if constexpr (C == 12) {  // channels 8-11 through the same operand tiles
+                    if (half) scatter_rows<C, 1, 1>(s, s.t.q, r, valid, dxv);
+                    else scatter_rows<C, 0, 1>(s, s.t.q, r, valid, dxv);
+                    if (!run_stage<C>(7, d, tmem, first, done, dwdone, ph, failed, tid)) break;
+                }
                 scatter_stage_out<C>(s, tmem, warp, lane, half);
                 if (__syncthreads_or(failed)) {
                     failed = true;
@@ -1088,7 +646,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                 if constexpr (BLK)
                     scatter_reduce_blocks<C>(s, p, tid);
                 else
-                    scatter_reduce<C>(s, p, tid);
+                    scatter_reduce<C>(s, s.t.f, p, tid);
                 first = false;
                 umma::fence_before();
                 if (__syncthreads_or(failed)) {
@@ -1109,7 +667,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 #pragma unroll
             for (int q = 0; q < C / 4; ++q)
                 *reinterpret_cast<float4 *>(dxr + 4 * q) = make_float4(dxv[4 * q], dxv[4 * q + 1], dxv[4 * q + 2], dxv[4 * q + 3]);
-            if (warp < 2) window_cands<C>(s, warp, lane);
+            if (warp < 2) window_cands(s, warp, lane);
             if (__syncthreads_or(failed)) {
                 failed = true;
                 break;
@@ -1117,11 +675,11 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             const bool both = s.win[0].ok && s.win[1].ok;
             const int span = max(s.win[0].span, s.win[1].span);
             if (both && span <= 5) {
-                sweep_tc<C, 5, BLK>(s, p, tid);
+                sweep_tc<C, 5, BLK>(s, reinterpret_cast<const float *>(s.t.m.H2), p, tid);
             } else if (both && span <= 10) {
-                sweep_tc<C, 10, BLK>(s, p, tid);
+                sweep_tc<C, 10, BLK>(s, reinterpret_cast<const float *>(s.t.m.H2), p, tid);
             } else if (valid) {
-                scatter_taps_tc<C, BLK>(s, p, half, r);
+                scatter_taps_tc<C, BLK>(s, reinterpret_cast<const float *>(s.t.m.H2), p, half, r);
             }
         }
         first = false;
@@ -1161,10 +719,9 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     for (int q = 0; q < 4; ++q) {
                         const int in = c0 + 4 * q;
                         if (in + 3 < K::kBias1)
-                            atomicAdd(reinterpret_cast<float4 *>(p.gW[0] + o * 32 + in),
-                                      make_float4(__uint_as_float(v[4 * q]) * sc, __uint_as_float(v[4 * q + 1]) * sc,
-                                                  __uint_as_float(v[4 * q + 2]) * sc,
-                                                  __uint_as_float(v[4 * q + 3]) * sc));
+                            red_add_v4(p.gW[0] + o * 32 + in, __uint_as_float(v[4 * q]) * sc,
+                                       __uint_as_float(v[4 * q + 1]) * sc, __uint_as_float(v[4 * q + 2]) * sc,
+                                       __uint_as_float(v[4 * q + 3]) * sc);
                         else if (in == K::kBias1)
                             atomicAdd(p.gb[0] + o, __uint_as_float(v[4 * q]) * sc);
                     }
@@ -1172,7 +729,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             }
             const int f = 32 * (warp & 3) + lane;  // hidden feature of dW3^T
             uint32_t v[16];
-            umma::ld16(tmem + kColW3 + lanes, v);
+            umma::ld16(tmem + Cols<C>::W3 + lanes, v);
             umma::wait_ld();
 #pragma unroll
             for (int o3 = 0; o3 < 16; ++o3) {
@@ -1192,10 +749,9 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
                     if (c0 < 64) {
 #pragma unroll
                         for (int q = 0; q < 2; ++q)
-                            atomicAdd(reinterpret_cast<float4 *>(p.gW[1] + o * 64 + c0 + 4 * q),
-                                      make_float4(__uint_as_float(v[4 * q]) * sc, __uint_as_float(v[4 * q + 1]) * sc,
-                                                  __uint_as_float(v[4 * q + 2]) * sc,
-                                                  __uint_as_float(v[4 * q + 3]) * sc));
+                            red_add_v4(p.gW[1] + o * 64 + c0 + 4 * q, __uint_as_float(v[4 * q]) * sc,
+                                       __uint_as_float(v[4 * q + 1]) * sc, __uint_as_float(v[4 * q + 2]) * sc,
+                                       __uint_as_float(v[4 * q + 3]) * sc);
                     } else {
                         atomicAdd(p.gb[1] + o, __uint_as_float(v[0]) * sc);
                     }

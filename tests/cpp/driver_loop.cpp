@@ -55,7 +55,7 @@ std::vector<float> image(int w, int h, int ch, uint32_t seed)
     std::vector<float> v((size_t)w * h * ch);
     std::mt19937 rng(seed);
     std::uniform_real_distribution<float> U(0.f, 6.2831853f);
-    float ph[4][3];
+    float ph[4][4];
     for (auto &c : ph)
         for (float &x : c) x = U(rng);
     for (int y = 0; y < h; ++y)
@@ -95,7 +95,8 @@ int main(int argc, char **argv)
         const float weights[4] = {1.f, 1.f, 0.5f, 0.5f};
         int used = 0;
         for (int i = 0; i < 4; ++i) {
-            std::vector<float> img = image(W, H, chans[i], 7u + i);
+            // RGB textures are uploaded as RGBA, 4 floats per texel (main.cpp:216-224, :547)
+            std::vector<float> img = image(W, H, chans[i] == 3 ? 4 : chans[i], 7u + i);
             NtReferenceTexture t;
             if (nt_reference_texture_create(img.data(), W, H, chans[i], 1, weights[i], &t) != NT_OK)
                 throw std::runtime_error(std::string("nt_reference_texture_create: ") + nt_get_last_error_string());

@@ -189,7 +189,7 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c)
 // oracle).  Channel pairs go through the packed fp32 FMA, which rounds each lane like fmaf.
 // The loads of RB footprint rows are issued before their arithmetic, so that the gather pays
 // the memory latency once per RB rows instead of once per tap (RB = 4 for up to 8 channels:
-// 64 registers of texels; 2 above).
+// 64 registers of texels; two rows above).
 template <int C>
 __device__ __forceinline__ void gather_cr(const __half *__restrict__ grid, int32_t w,
                                           const Footprint &fp, float out[C])

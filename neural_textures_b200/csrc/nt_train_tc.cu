@@ -374,6 +374,62 @@ __device__ __forceinline__ void blk_gather_window(const Smem<C> &s, const float 
     }
 }
 
+// ---- gather of one latent grid (fp16 grids) ---------------------------------------------------
+
+// Sample r's Catmull-Rom gather of grid G (second level blended in at a fractional mip
+// coordinate), its footprint for the latent scatter, and its latents in the X operand:
+// grid 0 takes X elements 0 .. C - 1, grid 1 elements C .. 2C - 1.
+template <int C, int G, bool MIP>
+__device__ __forceinline__ void gather_grid(Smem<C> &s, const TrainLaunch &p, int r, bool valid, float u, float v,
+                                            int warp, int lane)
+{
+    using K = Cfg<C>;
+    Footprint fp;
+    footprint(u, v, p.gw[G], p.gh[G], fp);
+    if (valid) shard_rows(p, G, p.gh[G], fp);
+    uint32_t packed[C / 2];
+#pragma unroll
+    for (int k = 0; k < C / 2; ++k) packed[k] = 0u;
+    if (valid) {
+        float f[C];
+        gather_cr<C>(p.grid[G], p.gw[G], fp, f);
+        if constexpr (MIP) {
+            const float t = p.mip_t[G];
+            if (t > 0.f) {  // (1 - t) level m0 + t level m1 (train.cu:303-304)
+                Footprint fb;
+                footprint(u, v, p.gw_b[G], p.gh_b[G], fb);
+                float fl[C];
+                gather_cr<C>(p.grid_b[G], p.gw_b[G], fb, fl);
+                const float omt = __fsub_rn(1.f, t);
+#pragma unroll
+                for (int k = 0; k < C; ++k) f[k] = __fadd_rn(__fmul_rn(omt, f[k]), __fmul_rn(t, fl[k]));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < C / 2; ++k) packed[k] = pack_half2(f[2 * k], f[2 * k + 1]);
+    }
+    if (!p.finalize) {
+        s.base[G][r] = make_short2((short)fp.bx, (short)fp.by);
+        float4 *wr = reinterpret_cast<float4 *>(s.wts[G][r]);
+        wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
+        wr[1] = make_float4(fp.wy[0], fp.wy[1], fp.wy[2], fp.wy[3]);
+        extents_partial(s.part[G], fp.bx, fp.by, valid, warp & 3, lane);
+    }
+    // X elements G * C .. G * C + C - 1 in 4-element (8-byte) pieces
+#pragma unroll
+    for (int e = 0; e < C; e += 4) {
+        const int k = G * C + e;
+        if ((k & 7) == 0 && e + 8 <= C) {
+            st16(s.t.m.X, umma::cm_offset(r, k, K::XC), packed[e / 2], packed[e / 2 + 1], packed[e / 2 + 2],
+                 packed[e / 2 + 3]);
+            e += 4;
+        } else {
+            *reinterpret_cast<uint2 *>(s.t.m.X + umma::cm_offset(r, k, K::XC)) =
+                make_uint2(packed[e / 2], packed[e / 2 + 1]);
+        }
+    }
+}
+
 // ---- the kernel ---------------------------------------------------------------------------------
 
 // C: latent channels per grid; TC: target channels when they have a vector gather (4, 8,
@@ -422,90 +478,116 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 #pragma unroll
         for (int k = 0; k < 16; ++k) tgt[k] = 0.f;
 
-        // ---- gather: half 0 = both latent grids (+ footprints), half 1 = target + posenc --
+        // ---- gather.  8-channel grids: half 0 = grid 0 + positional features, half 1 = grid 1
+        // + target.  12-channel grids (whose half-1 registers would not hold a grid gather beside
+        // the target): half 0 = both grids, half 1 = target + positional features.  Block
+        // features: half 0 = both footprints (the records are gathered after the window decode
+        // below), half 1 = target + positional features.
         {
+            constexpr bool kSplitGrids = C == 8 && !BLK;
             float u = 0.f, v = 0.f;
             if (valid) sample_uv(p.sampler, ix, iy, u, v);
-            if (half == 0) {
-                uint32_t packed[K::LC * 4];
+            if constexpr (kSplitGrids) {
+                if (half == 0) gather_grid<C, 0, MIP>(s, p, r, valid, u, v, warp, lane);
+                else gather_grid<C, 1, MIP>(s, p, r, valid, u, v, warp, lane);
+            } else if constexpr (!BLK) {
+                if (half == 0) {
+                    uint32_t packed[K::LC * 4];
 #pragma unroll
-                for (int k = 0; k < K::LC * 4; ++k) packed[k] = 0u;
+                    for (int k = 0; k < K::LC * 4; ++k) packed[k] = 0u;
 #pragma unroll
-                for (int gi = 0; gi < 2; ++gi) {
-                    Footprint fp;
-                    footprint(u, v, p.gw[gi], p.gh[gi], fp);
-                    if (valid) shard_rows(p, gi, p.gh[gi], fp);
-                    if (valid && !BLK) {  // block features gather after the window decode below
-                        float f[C];
-                        gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
-                        if constexpr (MIP) {
-                            const float t = p.mip_t[gi];
-                            if (t > 0.f) {  // (1 - t) level m0 + t level m1 (train.cu:303-304)
-                                Footprint fb;
-                                footprint(u, v, p.gw_b[gi], p.gh_b[gi], fb);
-                                float fl[C];
-                                gather_cr<C>(p.grid_b[gi], p.gw_b[gi], fb, fl);
-                                const float omt = __fsub_rn(1.f, t);
+                    for (int gi = 0; gi < 2; ++gi) {
+                        Footprint fp;
+                        footprint(u, v, p.gw[gi], p.gh[gi], fp);
+                        if (valid) shard_rows(p, gi, p.gh[gi], fp);
+                        if (valid) {
+                            float f[C];
+                            gather_cr<C>(p.grid[gi], p.gw[gi], fp, f);
+                            if constexpr (MIP) {
+                                const float t = p.mip_t[gi];
+                                if (t > 0.f) {  // (1 - t) level m0 + t level m1 (train.cu:303-304)
+                                    Footprint fb;
+                                    footprint(u, v, p.gw_b[gi], p.gh_b[gi], fb);
+                                    float fl[C];
+                                    gather_cr<C>(p.grid_b[gi], p.gw_b[gi], fb, fl);
+                                    const float omt = __fsub_rn(1.f, t);
 #pragma unroll
-                                for (int k = 0; k < C; ++k) f[k] = __fadd_rn(__fmul_rn(omt, f[k]), __fmul_rn(t, fl[k]));
+                                    for (int k = 0; k < C; ++k)
+                                        f[k] = __fadd_rn(__fmul_rn(omt, f[k]), __fmul_rn(t, fl[k]));
+                                }
                             }
-                        }
 #pragma unroll
-                        for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
+                            for (int k = 0; k < C / 2; ++k) packed[gi * (C / 2) + k] = pack_half2(f[2 * k], f[2 * k + 1]);
+                        }
+                        if (!p.finalize) {
+                            s.base[gi][r] = make_short2((short)fp.bx, (short)fp.by);
+                            float4 *wr = reinterpret_cast<float4 *>(s.wts[gi][r]);
+                            wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
+                            wr[1] = make_float4(fp.wy[0], fp.wy[1], fp.wy[2], fp.wy[3]);
+                            extents_partial(s.part[gi], fp.bx, fp.by, valid, warp, lane);
+                        }
                     }
-                    if (BLK || !p.finalize) {
-                        s.base[gi][r] = make_short2((short)fp.bx, (short)fp.by);
-                        float4 *wr = reinterpret_cast<float4 *>(s.wts[gi][r]);
-                        wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
-                        wr[1] = make_float4(fp.wy[0], fp.wy[1], fp.wy[2], fp.wy[3]);
-                        extents_partial(s.part[gi], fp.bx, fp.by, valid, warp, lane);
-                    }
-                }
-                if constexpr (!BLK) {
 #pragma unroll
                     for (int j = 0; j < K::LC; ++j)
                         st16(s.t.m.X, umma::cm_offset(r, 8 * j, K::XC), packed[4 * j], packed[4 * j + 1],
                              packed[4 * j + 2], packed[4 * j + 3]);
                 }
-            } else {
+            }
+            if (BLK && half == 0) {
+#pragma unroll
+                for (int gi = 0; gi < 2; ++gi) {
+                    Footprint fp;
+                    footprint(u, v, p.gw[gi], p.gh[gi], fp);
+                    if (valid) shard_rows(p, gi, p.gh[gi], fp);
+                    s.base[gi][r] = make_short2((short)fp.bx, (short)fp.by);
+                    float4 *wr = reinterpret_cast<float4 *>(s.wts[gi][r]);
+                    wr[0] = make_float4(fp.wx[0], fp.wx[1], fp.wx[2], fp.wx[3]);
+                    wr[1] = make_float4(fp.wy[0], fp.wy[1], fp.wy[2], fp.wy[3]);
+                    extents_partial(s.part[gi], fp.bx, fp.by, valid, warp, lane);
+                }
+            }
+            const bool pe_half = kSplitGrids ? half == 0 : half == 1;  // writes the positional features
+            if (pe_half) {
                 uint32_t packed[4] = {0u, 0u, 0u, 0u};
                 if (valid) {
                     float pe[8];
                     posenc(u, v, pe);
 #pragma unroll
                     for (int k = 0; k < 4; ++k) packed[k] = pack_half2(pe[2 * k], pe[2 * k + 1]);
-                    Footprint fp;
-                    footprint(u, v, p.tw, p.th, fp);
-                    shard_rows(p, 2, p.th, fp);
-                    if constexpr (TC > 0)
-                        gather_cr<TC>(p.target, p.tw, fp, tgt);
-                    else if (p.num_ref > 0)  // reference textures (train.cu:105-157)
-                        ref_expected(p.ref, p.num_ref, u, v, p.ref_lod, tgt);
-                    else
-                        gather_cr_any(p.target, p.tw, cout, fp, tgt);
-                    if constexpr (MIP) {
-                        const float t = p.target_t;
-                        if (t > 0.f) {  // train.cu:102: sample0 (1 - t) + sample1 t
-                            float tb[16];
-                            footprint(u, v, p.tw_b, p.th_b, fp);
-                            if constexpr (TC > 0) {
-#pragma unroll
-                                for (int k = TC; k < 16; ++k) tb[k] = 0.f;
-                                gather_cr<TC>(p.target_b, p.tw_b, fp, tb);
-                            } else {
-                                gather_cr_any(p.target_b, p.tw_b, cout, fp, tb);
-                            }
-                            const float omt = __fsub_rn(1.f, t);
-#pragma unroll
-                            for (int k = 0; k < 16; ++k) tgt[k] = __fadd_rn(__fmul_rn(omt, tgt[k]), __fmul_rn(t, tb[k]));
-                        }
-                    }
                 }
                 static_assert(K::XC == K::LC + 2 || K::XC == K::LC + 3, "X row: latents, posenc, 1, [0]");
                 st16(s.t.m.X, umma::cm_offset(r, 8 * K::LC, K::XC), packed[0], packed[1], packed[2], packed[3]);
                 st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 1), K::XC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
                 if constexpr (K::XC > K::LC + 2)
                     st16(s.t.m.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
+            }
+            if (half == 1 && valid) {  // the target (the loss epilogue runs on half 1)
+                Footprint fp;
+                footprint(u, v, p.tw, p.th, fp);
+                shard_rows(p, 2, p.th, fp);
+                if constexpr (TC > 0)
+                    gather_cr<TC>(p.target, p.tw, fp, tgt);
+                else if (p.num_ref > 0)  // reference textures (train.cu:105-157)
+                    ref_expected(p.ref, p.num_ref, u, v, p.ref_lod, tgt);
+                else
+                    gather_cr_any(p.target, p.tw, cout, fp, tgt);
+                if constexpr (MIP) {
+                    const float t = p.target_t;
+                    if (t > 0.f) {  // train.cu:102: sample0 (1 - t) + sample1 t
+                        float tb[16];
+                        footprint(u, v, p.tw_b, p.th_b, fp);
+                        if constexpr (TC > 0) {
+#pragma unroll
+                            for (int k = TC; k < 16; ++k) tb[k] = 0.f;
+                            gather_cr<TC>(p.target_b, p.tw_b, fp, tb);
+                        } else {
+                            gather_cr_any(p.target_b, p.tw_b, cout, fp, tb);
+                        }
+                        const float omt = __fsub_rn(1.f, t);
+#pragma unroll
+                        for (int k = 0; k < 16; ++k) tgt[k] = __fadd_rn(__fmul_rn(omt, tgt[k]), __fmul_rn(t, tb[k]));
+                    }
+                }
             }
         }
         if constexpr (BLK) {

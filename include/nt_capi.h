@@ -423,6 +423,48 @@ NT_API nt_status nt_dist_band(int32_t rank, int32_t world, int32_t lattice_heigh
  * reloaded (from a checkpoint) before training goes on. */
 NT_API nt_status nt_dist_train_step(const NtShard *shards, int32_t count);
 
+/* ---- row-sharded training with one process (or host thread) per GPU over NCCL (no reference
+ * counterpart: the reference trains on one device, main.cpp:1071-1077) -----------------------
+ *
+ * The same band layout as nt_dist_train_step (an NtShard per rank: halo rows above and below the
+ * owned band of each latent grid, bands in a ring), but every rank steps only its own shard and
+ * the exchanges run over NCCL (NVLink / NVSwitch between the GPUs of a node):
+ *   1. the training pass of the band;
+ *   2. the gradients of the halo rows go to the neighbours that own those rows (the halo above to
+ *      rank - 1, the halo below to rank + 1; NCCL send / receive into the workspace), the
+ *      network gradients are summed over the ranks (NCCL all-reduce, in place);
+ *   3. the received halo gradients are added to the band's first / last halo_rows rows and the
+ *      halo gradients zeroed; Adam on the network (identical on every rank) and on the owned band;
+ *   4. the updated first / last halo_rows rows of the band go to the neighbours' halo rows
+ *      (NCCL send / receive straight into them).
+ * Everything is queued on the shard's stream; nt_nccl_train_step returns once it is queued.  The
+ * library loads NCCL (libnccl.so.2) at the first call; NT_ERR_NCCL when it cannot.  The caller
+ * passes a workspace of nt_nccl_workspace_bytes(shard) device bytes on the shard's device (the
+ * library allocates no device memory; NCCL allocates its own buffers for the communicator). */
+#define NT_NCCL_UNIQUE_ID_BYTES 128
+typedef struct NtNcclComm NtNcclComm; /* opaque */
+
+/* The communicator id: one rank creates it and hands the 128 bytes to every rank. */
+NT_API nt_status nt_nccl_unique_id(void *id);
+/* Joins the `world`-rank communicator as `rank` on CUDA device `device` (a collective call: every
+ * rank makes it, each from its own process or thread).  *comm is NULL on failure. */
+NT_API nt_status nt_nccl_comm_create(const void *id, int32_t world, int32_t rank, int32_t device,
+                                     NtNcclComm **comm);
+/* Releases the communicator (after its work completed, or after nt_nccl_comm_wait gave up). */
+NT_API nt_status nt_nccl_comm_destroy(NtNcclComm *comm);
+/* Device bytes of the workspace of nt_nccl_train_step for this shard (16-byte multiple). */
+NT_API size_t nt_nccl_workspace_bytes(const NtShard *shard);
+/* One training step of this rank's shard (see above); shard->device must be the communicator's
+ * device.  All ranks must call it with the same step and the same band plan.  An argument error
+ * returns before anything is queued. */
+NT_API nt_status nt_nccl_train_step(NtNcclComm *comm, const NtShard *shard, void *workspace,
+                                    size_t workspace_bytes);
+/* Waits at most timeout_ms for the work queued by this communicator's last nt_nccl_train_step,
+ * polling NCCL's asynchronous error state: NT_OK when it completed, NT_ERR_NCCL on an NCCL error
+ * and NT_ERR_TIMEOUT when the time ran out; in both error cases the communicator is aborted (its
+ * ranks' pending operations end with an error) and must be destroyed. */
+NT_API nt_status nt_nccl_comm_wait(NtNcclComm *comm, int32_t timeout_ms);
+
 /* ---- tensor-core self-test (no reference counterpart) ---------------------------------- */
 
 /* Runs the tcgen05 operand layouts of the fused kernels on small known matrices (device

@@ -103,6 +103,7 @@ class NtKernelParams(C.Structure):
 
 
 NT_DIST_MAX_SHARDS = 16
+NT_NCCL_UNIQUE_ID_BYTES = 128
 
 
 class NtShard(C.Structure):
@@ -160,6 +161,12 @@ SIGNATURES = {
                                       C.POINTER(C.c_int32)]),
     "nt_checkpoint_read": (C.c_int, [C.c_char_p, C.c_char_p, C.c_void_p, C.c_int64]),
     "nt_build_mips": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
+    "nt_nccl_unique_id": (C.c_int, [C.c_void_p]),
+    "nt_nccl_comm_create": (C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
+    "nt_nccl_comm_destroy": (C.c_int, [C.c_void_p]),
+    "nt_nccl_workspace_bytes": (C.c_size_t, [C.POINTER(NtShard)]),
+    "nt_nccl_train_step": (C.c_int, [C.c_void_p, C.POINTER(NtShard), C.c_void_p, C.c_size_t]),
+    "nt_nccl_comm_wait": (C.c_int, [C.c_void_p, C.c_int32]),
 }
 
 _lib = None

@@ -478,13 +478,14 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
 #pragma unroll
         for (int k = 0; k < 16; ++k) tgt[k] = 0.f;
 
-        // ---- gather.  8-channel grids: half 0 = grid 0 + positional features, half 1 = grid 1
-        // + target.  12-channel grids (whose half-1 registers would not hold a grid gather beside
-        // the target): half 0 = both grids, half 1 = target + positional features.  Block
-        // features: half 0 = both footprints (the records are gathered after the window decode
-        // below), half 1 = target + positional features.
+        // ---- gather.  8-channel grids with an fp16 target buffer: half 0 = grid 0 + positional
+        // features, half 1 = grid 1 + target.  12-channel grids (whose half-1 registers would
+        // not hold a grid gather beside the target) and the generic target (reference textures:
+        // 9 texture fetches per texture and level): half 0 = both grids, half 1 = target +
+        // positional features.  Block features: half 0 = both footprints (the records are
+        // gathered after the window decode below), half 1 = target + positional features.
         {
-            constexpr bool kSplitGrids = C == 8 && !BLK;
+            constexpr bool kSplitGrids = C == 8 && TC > 0 && !BLK;
             float u = 0.f, v = 0.f;
             if (valid) sample_uv(p.sampler, ix, iy, u, v);
             if constexpr (kSplitGrids) {

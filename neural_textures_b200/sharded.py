@@ -534,3 +534,53 @@ def dist_train_step(shards: list[ShardedTexture], streams=None):
     check(load().nt_dist_train_step(arr, n))
     for s in shards:
         s.step += 1
+
+
+class NcclComm:
+    """One rank's communicator of the C ABI's NCCL path (include/nt_capi.h nt_nccl_*): a process
+    (or host thread) per GPU, the halo exchanges and the network-gradient sum over NCCL, the
+    step queued on the shard's stream by nt_nccl_train_step.  The exchange workspace is a torch
+    buffer on the shard's device."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_ubyte * N.NT_NCCL_UNIQUE_ID_BYTES)()
+        check(load().nt_nccl_unique_id(buf))
+        return bytes(buf)
+
+    def __init__(self, uid: bytes, world: int, rank: int, device: int):
+        self.world, self.rank, self.device = world, rank, device
+        buf = (C.c_ubyte * N.NT_NCCL_UNIQUE_ID_BYTES).from_buffer_copy(uid)
+        h = C.c_void_p()
+        check(load().nt_nccl_comm_create(buf, world, rank, device, C.byref(h)))
+        self.handle = h
+        self.workspace = None
+
+    def shard_of(self, shard: ShardedTexture, stream=None) -> N.NtShard:
+        torch = shard.torch
+        s = N.NtShard()
+        s.params = shard.train_params()
+        for i in range(2):
+            s.halo_rows[i] = shard.bands[i].halo
+        s.device = self.device
+        s.stream = stream if stream is not None else torch.cuda.current_stream(shard.device).cuda_stream
+        return s
+
+    def train_step(self, shard: ShardedTexture, stream=None):
+        """One step of this rank's band (every rank calls it); advances shard.step."""
+        torch = shard.torch
+        s = self.shard_of(shard, stream)
+        need = int(load().nt_nccl_workspace_bytes(C.byref(s)))
+        if self.workspace is None or self.workspace.numel() < need:
+            self.workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=shard.device)
+        check(load().nt_nccl_train_step(self.handle, C.byref(s), self.workspace.data_ptr(), self.workspace.numel()))
+        shard.step += 1
+
+    def wait(self, timeout_ms: int = 60000):
+        """Bounded wait for the last step (NT_ERR_TIMEOUT / NT_ERR_NCCL abort the communicator)."""
+        check(load().nt_nccl_comm_wait(self.handle, int(timeout_ms)))
+
+    def close(self):
+        if self.handle is not None:
+            check(load().nt_nccl_comm_destroy(self.handle))
+            self.handle = None

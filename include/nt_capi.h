@@ -215,6 +215,16 @@ typedef struct NtKernelParams {
      * channels output_channels .. stride - 1 as 0, so a caller laid out like the reference
      * (train.cu:950-955: NT_OUTPUT_SIZE = 16 fp32 values per texel) reads its layout. */
     int32_t inference_output_stride;
+
+    /* Optional workspace of nt_invoke_training (no reference counterpart): at least
+     * nt_workspace_bytes() device bytes, 16-byte aligned, zeroed once by the caller.  With it,
+     * the training kernel hands out its tiles through a counter there (each CTA starts on its
+     * own tile, then takes the next unclaimed one as it finishes a tile, instead of a fixed
+     * share), and the last CTA to finish sets the
+     * counter back to zero, so the workspace is zero again after every call.  NULL: fixed
+     * shares.  Calls that run at the same time on the GPU must not share a workspace. */
+    void *workspace;
+    int64_t workspace_bytes;
 } NtKernelParams;
 
 /* ---- library ------------------------------------------------------------------------ */
@@ -223,6 +233,8 @@ NT_API const char *nt_get_last_error_string(void);
 NT_API size_t nt_kernel_params_size(void);
 /* Offset of a named field of NtKernelParams (for binding checks), or (size_t)-1. */
 NT_API size_t nt_kernel_params_offset(const char *field);
+/* Device bytes of NtKernelParams.workspace (nt_invoke_training's tile counter). */
+NT_API size_t nt_workspace_bytes(void);
 /* Kernels launched by this library on the calling thread since load (for launch accounting). */
 NT_API uint64_t nt_launch_count(void);
 

@@ -99,6 +99,8 @@ class NtKernelParams(C.Structure):
         ("reference_textures", NtReferenceTexture * NT_MAX_REFERENCE_TEXTURES),
         ("num_reference_textures", C.c_int32),
         ("inference_output_stride", C.c_int32),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_int64),
     ]
 
 
@@ -125,6 +127,7 @@ SIGNATURES = {
     "nt_kernel_params_size": (C.c_size_t, []),
     "nt_kernel_params_offset": (C.c_size_t, [C.c_char_p]),
     "nt_launch_count": (C.c_uint64, []),
+    "nt_workspace_bytes": (C.c_size_t, []),
     "nt_invoke_training": (C.c_int, [_P, C.c_int, C.c_void_p]),
     "nt_invoke_optimize_network": (C.c_int, [_P, C.c_void_p]),
     "nt_invoke_optimize_features": (C.c_int, [_P, C.c_int, C.c_void_p]),

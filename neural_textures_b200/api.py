@@ -372,6 +372,8 @@ class NeuralTexture:
         self.target_chain = z(mip_chain_texels(image_w, image_h, self.target_num_mips) * self.cout, f16)
         self.target = self.target_chain[:image_w * image_h * self.cout].view(image_h, image_w, self.cout)
         self.loss_accum = z(1, f32)
+        # tile counter of the training kernel (NtKernelParams.workspace; zero between calls)
+        self.workspace = z(int(load().nt_workspace_bytes()) // 4, torch.int32)
         if lattice is None:
             lattice = (image_w, image_h)
         self.lattice = tuple(lattice)
@@ -648,6 +650,8 @@ class NeuralTexture:
         p.seed = self.seed
         if loss_accum:
             p.loss_accum = self.loss_accum.data_ptr()
+        p.workspace = self.workspace.data_ptr()
+        p.workspace_bytes = self.workspace.numel() * 4
         return p
 
     # -- operations ---------------------------------------------------------------------------

@@ -375,11 +375,15 @@ size_t nt_kernel_params_offset(const char *field)
     NT_FIELD(reference_textures)
     NT_FIELD(num_reference_textures)
     NT_FIELD(inference_output_stride)
+    NT_FIELD(workspace)
+    NT_FIELD(workspace_bytes)
 #undef NT_FIELD
     return (size_t)-1;
 }
 
 uint64_t nt_launch_count(void) { return g_launches.load(); }
+
+size_t nt_workspace_bytes(void) { return kWorkspaceBytes; }
 
 nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type, nt_stream_t stream)
 {
@@ -475,6 +479,12 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
     L.sampler.seed = p->seed;
     L.inv_num_samples = 1.0f / (float)p->num_samples;
     L.loss_accum = p->loss_accum;
+    if (p->workspace) {
+        NT_REQUIRE(p->workspace_bytes >= (int64_t)kWorkspaceBytes && aligned16(p->workspace),
+                   "workspace must hold nt_workspace_bytes() = %zu bytes, 16-byte aligned (got %lld)",
+                   kWorkspaceBytes, (long long)p->workspace_bytes);
+        L.tile_counter = static_cast<uint32_t *>(p->workspace);
+    }
     L.finalize = type == NT_TRAIN_FINALIZE;
     // row sharding (all zero: the whole material)
     NT_REQUIRE(p->lattice_row0 >= 0 && p->lattice_rows >= 0 &&

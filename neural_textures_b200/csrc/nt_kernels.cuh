@@ -54,7 +54,13 @@ struct TrainLaunch {
     RefTexView ref[kMaxRefTextures];
     int32_t num_ref;
     float ref_lod;
+    // optional tile counter pair (next tile, CTAs finished) in the caller's workspace: NULL for
+    // a fixed share of the tiles per CTA
+    uint32_t *tile_counter;
 };
+
+// Bytes of NtKernelParams.workspace (two 32-bit counters, padded).
+constexpr size_t kWorkspaceBytes = 256;
 
 struct DecodeLaunch {
     const __half *grid[2];

@@ -89,6 +89,7 @@ struct Smem {
     Window win[2];
     alignas(8) uint64_t done, dwdone;  // stage products; weight-gradient products of B3 / B2 / B1
     uint32_t tmem_base;
+    int32_t next_tile;  // with a tile counter: the CTA's next tile (written by the last thread)
     float red[kThreadsTC / 32];
 };
 
@@ -469,7 +470,11 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     bool failed = false, first = true;
     float sse = 0.f;
 
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    // Tiles: every CTA starts on tile blockIdx.x.  With a tile counter it then takes the next
+    // unclaimed tile past the first gridDim.x (claimed during the tile before, published after
+    // B1, read by all after a later barrier); without one, tiles blockIdx.x + gridDim.x, ...
+    const bool dyn = p.tile_counter != nullptr;
+    for (int tile = blockIdx.x; tile < ntiles; tile = dyn ? s.next_tile : tile + gridDim.x) {
         const int cx0 = (tile % p.tiles_x) * kTileW, cy0 = (tile / p.tiles_x) * kTileH;
         const int ix = cx0 + (r & (kTileW - 1));
         const int iy = p.lat_row0 + cy0 + (r >> 4);  // full lattice row (sharded calls train a band)
@@ -626,6 +631,10 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
             }
         }
         if (!run_stage<C>(0, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // F1
+        // the next tile is claimed by the last thread (not thread 0, which issues the products),
+        // and its number is only needed after B1, so the atomic's latency is hidden
+        uint32_t claim = 0;
+        if (dyn && tid == kThreadsTC - 1) claim = gridDim.x + atomicAdd(p.tile_counter, 1u);
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
         relu_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
@@ -680,6 +689,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         mask_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half, dwdone, dph, failed);  // after dW2 (reads H1)
         dph ^= 1u;
         if (!run_stage<C>(5, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // B1
+        if (dyn && tid == kThreadsTC - 1) s.next_tile = (int)claim;  // read after the next barrier
 
         // ---- E6: dX -> shared (fp32 rows over the dead H2 tile) -> latent gradients ------
         // dW1 (reads X and dZ1) must finish before anything below or the next tile writes them
@@ -853,6 +863,13 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         float tot = 0.f;
         for (int w = 0; w < kThreadsTC / 32; ++w) tot += s.red[w];
         atomicAdd(p.loss_accum, tot);
+    }
+    if (dyn && tid == 0) {  // the last CTA to finish (every CTA has made its last claim) zeroes the counters
+        __threadfence();
+        if (atomicAdd(p.tile_counter + 1, 1u) == gridDim.x - 1) {
+            atomicExch(p.tile_counter, 0u);
+            atomicExch(p.tile_counter + 1, 0u);
+        }
     }
     if (warp == 0) {
         umma::fence_after();

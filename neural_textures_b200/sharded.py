@@ -125,6 +125,7 @@ class ShardedTexture:
         self.mb = [z(b.shape, f32) for b in self.b]
         self.vb = [z(b.shape, f32) for b in self.b]
         self.loss_accum = z(1, f32)
+        self.workspace = z(int(load().nt_workspace_bytes()) // 4, torch.int32)  # the training pass's tile counter
         self.latent_adam = (beta1, beta2, latent_lr, eps)
         self.network_adam = (beta1, beta2, network_lr, eps)
         self.channel_weights = [1.0] * self.cout
@@ -259,6 +260,8 @@ class ShardedTexture:
         p.lattice_row0 = self.lat_band[0]
         p.lattice_rows = self.lat_band[1] - self.lat_band[0]
         p.loss_accum = self.loss_accum.data_ptr()
+        p.workspace = self.workspace.data_ptr()
+        p.workspace_bytes = self.workspace.numel() * 4
         return p
 
     def _build_adam_params(self) -> N.NtKernelParams:

@@ -336,3 +336,34 @@ def test_material_on_another_device(cuda):
     assert abs(la - lb) <= 1e-5 * la
     da, db = a.decode(dtype=torch.float32).cpu().numpy(), b.decode(dtype=torch.float32).cpu().numpy()
     assert max_rel(db, da) <= 1e-3
+
+
+def test_tile_counter_workspace(cuda):
+    """The training pass with a workspace (each CTA claims the next tile from a counter) gives
+    the gradients of the fixed tile shares up to the order of float atomics, leaves the
+    workspace zeroed, and rejects a workspace that is too small."""
+    import ctypes
+    import torch
+    from neural_textures_b200 import _native
+    L = _native.load()
+    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=23)
+    res = []
+    for ws in (True, False, True):
+        for t in tex.gW + tex.gb + tex.ggrads:
+            t.zero_()
+        tex.loss_accum.zero_()
+        p = tex.params(step=4)
+        if not ws:
+            p.workspace, p.workspace_bytes = None, 0
+        _native.check(L.nt_invoke_training(ctypes.byref(p), 0, None))
+        torch.cuda.synchronize()
+        res.append((tex.loss_accum.item(), [_host(g) for g in tex.gW + tex.gb + tex.ggrads]))
+        assert int(tex.workspace.abs().sum()) == 0
+    for a, b in ((res[0], res[1]), (res[2], res[1])):
+        assert abs(a[0] - b[0]) <= 1e-5 * b[0]
+        for x, y in zip(a[1], b[1]):
+            assert rel_l2(x, y) <= 1e-5
+    p = tex.params(step=4)
+    p.workspace_bytes = 8
+    assert L.nt_invoke_training(ctypes.byref(p), 0, None) == 1
+    assert b"workspace" in L.nt_get_last_error_string()

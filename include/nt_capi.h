@@ -247,6 +247,21 @@ NT_API uint64_t nt_launch_count(void);
 NT_API nt_status nt_invoke_training(const NtKernelParams *params, NtTrainingKernelType type,
                              nt_stream_t stream);
 
+/* No counterpart in the reference.  nt_invoke_training for callers that cannot allocate device
+ * memory when they train: an engine that reserves its device memory at start-up and may not
+ * call cudaMalloc / cudaFree later (they can stall the device and break its memory budget), or
+ * a binding that passes parameter blocks only and has no allocator to make a workspace with.
+ * The tile counters live in a 256-byte array of device memory owned by the library (the most
+ * scratch this call may use; a pass that would need more is rejected with NT_ERR_INVALID_ARG),
+ * and params->workspace must be NULL.  It calls no cudaMalloc, cudaFree or other allocating
+ * routine.  The first call on a device, with that device current, looks up the array's address
+ * (cudaGetSymbolAddress) and keeps it: make that first call before any stream capture starts.
+ * All calls on a device share the array and it keeps the last call's contents, so each call
+ * zeroes the counters on its stream before the pass; calls whose work overlaps on the GPU (other
+ * streams, other host threads) race on the counters and must be ordered on one stream. */
+NT_API nt_status nt_invoke_training_static_scratch(const NtKernelParams *params, NtTrainingKernelType type,
+                                                   nt_stream_t stream);
+
 /* train.h:158.  Adam over the three weight matrices and bias vectors (train.cu:681-726). */
 NT_API nt_status nt_invoke_optimize_network(const NtKernelParams *params, nt_stream_t stream);
 

@@ -129,6 +129,7 @@ SIGNATURES = {
     "nt_launch_count": (C.c_uint64, []),
     "nt_workspace_bytes": (C.c_size_t, []),
     "nt_invoke_training": (C.c_int, [_P, C.c_int, C.c_void_p]),
+    "nt_invoke_training_static_scratch": (C.c_int, [_P, C.c_int, C.c_void_p]),
     "nt_invoke_optimize_network": (C.c_int, [_P, C.c_void_p]),
     "nt_invoke_optimize_features": (C.c_int, [_P, C.c_int, C.c_void_p]),
     "nt_invoke_optimize_all": (C.c_int, [_P, C.c_void_p]),

@@ -341,12 +341,13 @@ def test_material_on_another_device(cuda):
 def test_tile_counter_workspace(cuda):
     """The training pass with a workspace (each CTA claims the next tile from a counter) gives
     the gradients of the fixed tile shares up to the order of float atomics, leaves the
-    workspace zeroed, and rejects a workspace that is too small."""
+    workspace zeroed, and rejects a workspace that is too small.  The lattice has 4,096 tiles,
+    at least 8 per CTA, where the kernel takes the counters."""
     import ctypes
     import torch
     from neural_textures_b200 import _native
     L = _native.load()
-    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=23)
+    tex = make_texture((2048, 2048), ((512, 512), (256, 256)), 8, 8, lattice=(1024, 512), seed=23)
     res = []
     for ws in (True, False, True):
         for t in tex.gW + tex.gb + tex.ggrads:

@@ -2,7 +2,8 @@
 static device array, for callers that cannot allocate) against nt_invoke_training with a
 caller workspace: two calls in a row, each from zeroed gradients, give the same loss and
 gradients up to the order of float atomics (relative L2 <= 1e-5, the bound the workspace
-test uses).  Named to run last, after every other test has used the library on the device;
+test uses), on a lattice of 4,096 tiles (at least 8 per CTA, where the kernel takes the
+counters).  Named to run last, after every other test has used the library on the device;
 it passes alone in a fresh process as well."""
 import ctypes
 
@@ -32,7 +33,7 @@ def _pass(L, tex, entry, workspace):
 def test_static_scratch_matches_workspace(cuda):
     from neural_textures_b200 import _native
     L = _native.load()
-    tex = make_texture((1024, 1024), ((512, 512), (256, 256)), 8, 8, lattice=(512, 512), seed=29)
+    tex = make_texture((2048, 2048), ((512, 512), (256, 256)), 8, 8, lattice=(1024, 512), seed=29)
     want = _pass(L, tex, "nt_invoke_training", workspace=True)
     for _ in range(2):
         got = _pass(L, tex, "nt_invoke_training_static_scratch", workspace=False)

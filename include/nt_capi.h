@@ -220,8 +220,8 @@ typedef struct NtKernelParams {
      * nt_workspace_bytes() device bytes, 16-byte aligned, zeroed once by the caller.  With it,
      * the training kernel hands out its tiles through a counter there (each CTA starts on its
      * own tile, then takes the next unclaimed one as it finishes a tile, instead of a fixed
-     * share; lattices of fewer than 8 tiles of 128 samples per CTA keep the fixed shares, which
-     * are as balanced there), and the last CTA to finish sets the
+     * share; lattices of fewer than 8 tiles of 128 samples per CTA, BC6 block features and
+     * fractional mip levels keep the fixed shares), and the last CTA to finish sets the
      * counter back to zero, so the workspace is zero again after every call.  NULL: fixed
      * shares.  Calls that run at the same time on the GPU must not share a workspace. */
     void *workspace;

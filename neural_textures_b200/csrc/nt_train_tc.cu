@@ -439,7 +439,9 @@ __device__ __forceinline__ void gather_grid(Smem<C> &s, const TrainLaunch &p, in
 // MIP: a fractional mip coordinate, so a grid or the target also reads a second level
 // (weight mip_t / target_t): features and target blend the two, the first level's gradient
 // takes the usual scatter at weight 1 - t and the second level per-tap atomics at weight t.
-template <int C, int TC, bool BLK, bool MIP>
+// DYN: tiles after the first come from the tile counter p.tile_counter (a separate
+// instantiation: the claim code measured 6 % slower on the fixed-share path of config 1).
+template <int C, int TC, bool BLK, bool MIP, bool DYN>
 __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaunch p)
 {
     using K = Cfg<C>;
@@ -473,8 +475,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
     // Tiles: every CTA starts on tile blockIdx.x.  With a tile counter it then takes the next
     // unclaimed tile past the first gridDim.x (claimed during the tile before, published after
     // B1, read by all after a later barrier); without one, tiles blockIdx.x + gridDim.x, ...
-    const bool dyn = p.tile_counter != nullptr;
-    for (int tile = blockIdx.x; tile < ntiles; tile = dyn ? s.next_tile : tile + gridDim.x) {
+    for (int tile = blockIdx.x; tile < ntiles; tile = DYN ? s.next_tile : tile + gridDim.x) {
         const int cx0 = (tile % p.tiles_x) * kTileW, cy0 = (tile / p.tiles_x) * kTileH;
         const int ix = cx0 + (r & (kTileW - 1));
         const int iy = p.lat_row0 + cy0 + (r >> 4);  // full lattice row (sharded calls train a band)
@@ -634,7 +635,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         // the next tile is claimed by the last thread (not thread 0, which issues the products),
         // and its number is only needed after B1, so the atomic's latency is hidden
         uint32_t claim = 0;
-        if (dyn && tid == kThreadsTC - 1) claim = gridDim.x + atomicAdd(p.tile_counter, 1u);
+        if (DYN && tid == kThreadsTC - 1) claim = gridDim.x + atomicAdd(p.tile_counter, 1u);
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] -----------------------------------------------
         relu_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half);
@@ -689,7 +690,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         mask_store32(Rl + 32 * half, s.t.m.H1, r, 4 * half, dwdone, dph, failed);  // after dW2 (reads H1)
         dph ^= 1u;
         if (!run_stage<C>(5, d, tmem, first, done, dwdone, ph, failed, tid)) break;  // B1
-        if (dyn && tid == kThreadsTC - 1) s.next_tile = (int)claim;  // read after the next barrier
+        if (DYN && tid == kThreadsTC - 1) s.next_tile = (int)claim;  // read after the next barrier
 
         // ---- E6: dX -> shared (fp32 rows over the dead H2 tile) -> latent gradients ------
         // dW1 (reads X and dZ1) must finish before anything below or the next tile writes them
@@ -864,7 +865,7 @@ __global__ void __launch_bounds__(kThreadsTC, 2) train_tc_kernel(const TrainLaun
         for (int w = 0; w < kThreadsTC / 32; ++w) tot += s.red[w];
         atomicAdd(p.loss_accum, tot);
     }
-    if (dyn && tid == 0) {  // the last CTA to finish (every CTA has made its last claim) zeroes the counters
+    if (DYN && tid == 0) {  // the last CTA to finish (every CTA has made its last claim) zeroes the counters
         __threadfence();
         if (atomicAdd(p.tile_counter + 1, 1u) == gridDim.x - 1) {
             atomicExch(p.tile_counter, 0u);
@@ -882,17 +883,27 @@ static cudaError_t launch_t(TrainLaunch p, cudaStream_t stream)
 {
     const size_t smem = sizeof(Smem<C>);
     static_assert(sizeof(Smem<C>) <= 113 * 1024, "two CTAs per SM");
-    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK, MIP>), smem);
-    if (e != cudaSuccess) return e;
     p.tiles_x = (p.sampler.lattice_w + kTileW - 1) / kTileW;
     p.tiles_y = (p.lat_rows + kTileH - 1) / kTileH;
     const int ntiles = p.tiles_x * p.tiles_y;
     const int cap = 2 * sm_count();
     const int grid = ntiles < cap ? ntiles : cap;
-    // below 8 tiles per CTA the fixed shares are balanced to within a tile and measured faster
-    // than claiming (2 us of 108 at 7 tiles per CTA); from there on the counter wins (5 % at 27)
-    if (ntiles < 8 * grid) p.tile_counter = nullptr;
-    train_tc_kernel<C, TC, BLK, MIP><<<grid, kThreadsTC, smem, stream>>>(p);
+    // Tile counters (single-level fp16 grids): below 8 tiles per CTA the fixed shares are
+    // balanced to within a tile and measured faster; from there on the counter wins (5 % at 27
+    // tiles per CTA)
+    if constexpr (!BLK && !MIP) {
+        if (p.tile_counter && ntiles >= 8 * grid) {
+            cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK, MIP, true>), smem);
+            if (e != cudaSuccess) return e;
+            train_tc_kernel<C, TC, BLK, MIP, true><<<grid, kThreadsTC, smem, stream>>>(p);
+            count_launch();
+            return cudaGetLastError();
+        }
+    }
+    cudaError_t e = set_smem_limit(reinterpret_cast<const void *>(train_tc_kernel<C, TC, BLK, MIP, false>), smem);
+    if (e != cudaSuccess) return e;
+    p.tile_counter = nullptr;
+    train_tc_kernel<C, TC, BLK, MIP, false><<<grid, kThreadsTC, smem, stream>>>(p);
     count_launch();
     return cudaGetLastError();
 }

@@ -411,7 +411,6 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
 
     TrainLaunch L;
     memset(&L, 0, sizeof L);
-    bool fractional = false;
     for (int f = 0; f < 2; ++f) {
         const LevelView v = feature_levels(p, f);
         L.grid[f] = reinterpret_cast<const __half *>(v.grid);
@@ -427,7 +426,6 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
             L.gw_b[f] = v.w_b;
             L.gh_b[f] = v.h_b;
             L.mip_t[f] = v.t;
-            fractional = true;
         }
     }
     L.net = net_view(p);
@@ -462,7 +460,6 @@ nt_status nt_invoke_training(const NtKernelParams *p, NtTrainingKernelType type,
             L.tw_b = mip_dim(tw, ts.m1);
             L.th_b = mip_dim(th, ts.m1);
             L.target_t = ts.t;
-            fractional = true;
         }
     }  // target
     if (!L.num_ref)
@@ -583,7 +580,6 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
                "inference_mse_accum requires a target or reference textures");
     DecodeLaunch L;
     memset(&L, 0, sizeof L);
-    bool fractional = false;
     for (int f = 0; f < 2; ++f) {
         const LevelView v = feature_levels(p, f);
         L.grid[f] = reinterpret_cast<const __half *>(v.grid);
@@ -594,7 +590,6 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
             L.gw_b[f] = v.w_b;
             L.gh_b[f] = v.h_b;
             L.mip_t[f] = v.t;
-            fractional = true;
         }
     }
     L.net = net_view(p);

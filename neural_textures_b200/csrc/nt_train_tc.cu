@@ -222,7 +222,10 @@ __device__ __forceinline__ bool run_stage(int stage, const Descs<C> &d, uint32_t
         return false;
     }
     umma::fence_after();
-    if (tid == 0) issue_stage<C>(stage, d, tmem, first, done, dwdone);
+    // the stage's product by thread 0; the weight-gradient products of B3 / B2 / B1 by the last
+    // thread (another warp and scheduler), so that neither issue delays one warp's epilogue twice
+    if (tid == 0) issue_stage<C>(stage, d, tmem, done);
+    if (tid == kThreadsTC - 1 && stage >= 3 && stage <= 5) issue_dw<C>(stage, d, tmem, first, dwdone);
     if (!umma::mbar_wait(done, ph, kSpinLimit)) {
         failed = true;
         atomicOr(&g_device_status, 1u);

@@ -476,17 +476,16 @@ struct Descs {
     uint64_t q0b, q1b;        // Q0 / Q1 holding channels 8-11 (C = 12)
 };
 
-// Issue the products of one stage (thread 0 only) and commit them to `done`.
+// Issue the products of one stage (thread 0 only) and commit them to `done` (the weight
+// gradients of B3 / B2 / B1 come from issue_dw).
 template <int C>
-__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t done,
-                                            uint32_t dwdone)
+__device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32_t tmem, uint32_t done)
 {
     using K = Cfg<C>;
     using umma::idesc_f16;
     using umma::mma_f16;
     constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
     const uint32_t R = tmem + kColTile;
-    const uint32_t acc0 = first ? 0u : 1u;  // the first tile of the CTA starts the gradient sums
     switch (stage) {
     case 0:  // F1
 #pragma unroll
@@ -505,24 +504,12 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
         break;
     case 3:  // B3: dH2 = dY W3; dW3^T += H2e^T dY
         mma_f16(R, d.dy, d.w3_mn, idesc_f16(128, 64, 0, 1), 0);
-        umma::commit(done);  // the epilogue needs dH2 only; the weight gradients follow
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(tmem + Cols<C>::W3, dadv(d.h2_mn, ks * 2 * HG), dadv(d.dy_mn, ks * 512), idesc_f16(128, 16, 1, 1),
-                    ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
+        break;
     case 4:  // B2: dH1 = dZ2 W2; dW2 += dZ2^T H1e
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
             mma_f16(R, dadv(d.h2, ks * 256), dadv(d.w2_mn, ks * 2 * HG), idesc_f16(128, 64, 0, 1), ks > 0);
-        umma::commit(done);
-#pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks)
-            mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
-                    ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
+        break;
     case 6:  // latent scatter: G0^T = Q0^T A0 (M128 N32), G1^T = Q1^T A1 (M64 N16), K = 128 samples
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
@@ -549,15 +536,39 @@ __device__ __forceinline__ void issue_stage(int stage, const Descs<C> &d, uint32
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
             mma_f16(R, dadv(d.h1, ks * 256), dadv(d.w1_mn, ks * 2 * XG), idesc_f16(128, K::NX, 0, 1), ks > 0);
-        umma::commit(done);
+        break;
+    }
+    umma::commit(done);
+}
+
+// Issue the weight-gradient products of B3 / B2 / B1 (stage 3 / 4 / 5) and commit them to
+// `dwdone`.  They write only the dW accumulator columns; the commit covers the products of the
+// calling thread alone, so they must not be issued by the thread that issues the stage.
+template <int C>
+__device__ __forceinline__ void issue_dw(int stage, const Descs<C> &d, uint32_t tmem, bool first, uint32_t dwdone)
+{
+    using K = Cfg<C>;
+    using umma::idesc_f16;
+    using umma::mma_f16;
+    constexpr uint32_t XG = K::XC * 128, HG = kHC * 128;
+    const uint32_t acc0 = first ? 0u : 1u;  // the first tile of the CTA starts the gradient sums
+    if (stage == 3) {
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(tmem + Cols<C>::W3, dadv(d.h2_mn, ks * 2 * HG), dadv(d.dy_mn, ks * 512), idesc_f16(128, 16, 1, 1),
+                    ks > 0 ? 1u : acc0);
+    } else if (stage == 4) {
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks)
+            mma_f16(tmem + kColW2, dadv(d.h2_mn, ks * 2 * HG), dadv(d.h1_mn, ks * 2 * HG), idesc_f16(64, 72, 1, 1),
+                    ks > 0 ? 1u : acc0);
+    } else {
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks)
             mma_f16(tmem + kColW1, dadv(d.h1_mn, ks * 2 * HG), dadv(d.x_mn, ks * 2 * XG), idesc_f16(64, K::XW, 1, 1),
                     ks > 0 ? 1u : acc0);
-        umma::commit(dwdone);
-        return;
     }
-    umma::commit(done);
+    umma::commit(dwdone);
 }
 
 }  // namespace tc

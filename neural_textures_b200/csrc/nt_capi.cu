@@ -596,7 +596,8 @@ nt_status nt_invoke_inference(const NtKernelParams *p, nt_stream_t stream)
     L.out = p->inference_output;
     L.out_f32 = p->inference_output_dtype == NT_DTYPE_F32;
     L.out_stride = out_stride;
-    L.target = reinterpret_cast<const __half *>(p->target);
+    // the target is read only for the squared error
+    L.target = p->inference_mse_accum ? reinterpret_cast<const __half *>(p->target) : nullptr;
     if ((st = reference_views(p, L.ref, L.num_ref)) != NT_OK) return st;
     L.ref_lod = p->lod;
     if (L.num_ref > 0) {

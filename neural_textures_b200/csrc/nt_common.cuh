@@ -75,6 +75,15 @@ __device__ __forceinline__ float clampf(float x, float lo, float hi)
     return x < lo ? lo : (x > hi ? hi : x);
 }
 
+// a / n correctly rounded, for a size n >= 1 (the IEEE division of the reference's float
+// expressions): a power of two divides exactly as the product with 2^-k, which costs one
+// multiply instead of a division sequence; other sizes take the IEEE division.
+__device__ __forceinline__ float div_by_size(float a, int32_t n)
+{
+    if ((n & (n - 1)) == 0) return __fmul_rn(a, __int_as_float((127 - (31 - __clz(n))) << 23));
+    return __fdiv_rn(a, (float)n);
+}
+
 __device__ __forceinline__ void sample_uv(const SamplerView &s, int32_t ix, int32_t iy, float &u,
                                           float &v)
 {
@@ -88,16 +97,16 @@ __device__ __forceinline__ void sample_uv(const SamplerView &s, int32_t ix, int3
     float py = __fadd_rn(__fmul_rn(ty, s.stride_y), (float)s.offset_y);
     px = clampf(px, 0.5f, __fsub_rn((float)s.image_w, 0.5f));
     py = clampf(py, 0.5f, __fsub_rn((float)s.image_h, 0.5f));
-    u = __fdiv_rn(px, (float)s.image_w);
-    v = __fdiv_rn(py, (float)s.image_h);
+    u = div_by_size(px, s.image_w);
+    v = div_by_size(py, s.image_h);
 }
 
 // Decode texel centres (train.cu:926-933).
 __device__ __forceinline__ void texel_uv(int32_t x, int32_t y, int32_t w, int32_t h, float &u,
                                          float &v)
 {
-    u = __fdiv_rn(__fadd_rn((float)x, 0.5f), (float)w);
-    v = __fdiv_rn(__fadd_rn((float)y, 0.5f), (float)h);
+    u = div_by_size(__fadd_rn((float)x, 0.5f), w);
+    v = div_by_size(__fadd_rn((float)y, 0.5f), h);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -68,7 +68,7 @@ __host__ __device__ constexpr int sep_rows() { return (kTileN * kHW * 2) / (2 * 
 // Base row of image row y in a grid of height gh (footprint()'s arithmetic).
 __device__ __forceinline__ int base_row(int y, int image_h, int gh, float &f)
 {
-    const float v = __fdiv_rn(__fadd_rn((float)y, 0.5f), (float)image_h);
+    const float v = div_by_size(__fadd_rn((float)y, 0.5f), image_h);
     return cr_base(v, gh, f);
 }
 
@@ -84,7 +84,7 @@ __device__ __forceinline__ void sep_pass1(float *hs, const DecodeLaunch &p, int 
         for (int q = 0; q < C / 2; ++q) row[q] = make_float2(0.f, 0.f);
         if (x < p.image_w) {
             float fx;
-            const float u = __fdiv_rn(__fadd_rn((float)x, 0.5f), (float)p.image_w);
+            const float u = div_by_size(__fadd_rn((float)x, 0.5f), p.image_w);
             const int bx = cr_base(u, p.gw[g], fx);
             float wx[4];
             catmull_rom_weights(fx, wx);
@@ -96,6 +96,122 @@ __device__ __forceinline__ void sep_pass1(float *hs, const DecodeLaunch &p, int 
 #pragma unroll
                 for (int q = 0; q < C / 4; ++q) {
                     const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(tp) + q);
+                    row[2 * q] = ffma2(w2, unpack_half2(raw.x), row[2 * q]);
+                    row[2 * q + 1] = ffma2(w2, unpack_half2(raw.y), row[2 * q + 1]);
+                }
+            }
+        }
+        float4 *o = reinterpret_cast<float4 *>(hs + (size_t)(ri * kTileW + xi) * C);
+#pragma unroll
+        for (int q = 0; q < C / 4; ++q) o[q] = make_float4(row[2 * q].x, row[2 * q].y, row[2 * q + 1].x, row[2 * q + 1].y);
+    }
+}
+
+// ---- window staging: the next tile's pass-1 texels copied into X while this tile computes --
+//
+// After F1 has read X, the texels that the next tile's pass 1 reads (per grid, rows
+// row0 .. row0 + nr - 1 and columns col0 .. col0 + ncol - 1 of the unwrapped grid, wrapped at
+// copy time) are copied into X with cp.async; the next tile waits for them, forms its row sums
+// from shared memory, and only then overwrites X with its features.  The row sums take the
+// same operations in the same order as sep_pass1, so they are bit-identical.
+
+struct DecWin {
+    int row0, nr, col0, ncol;
+};
+
+// Unwrapped base texel of image column x in a grid of width gw (sep_pass1's arithmetic).
+__device__ __forceinline__ int base_col(int x, int image_w, int gw)
+{
+    float f;
+    return cr_base(div_by_size(__fadd_rn((float)x, 0.5f), image_w), gw, f);
+}
+
+// The windows of `tile`: 2 when both fit the separable path and X together (staged), 1 when
+// they fit the separable path only, 0 when a grid needs more rows than the row-sum buffer.
+template <int C>
+__device__ __forceinline__ int dec_windows(const DecodeLaunch &p, int tile, DecWin (&w)[2])
+{
+    const int x0 = (tile % p.tiles_x) * kTileW, y0 = (tile / p.tiles_x) * kTileH;
+    const int xlast = min(x0 + kTileW, p.image_w) - 1, ylast = min(y0 + kTileH, p.image_h) - 1;
+    int texels = 0;
+    bool ok = true;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        float fdum;
+        const int b0 = base_row(y0, p.image_h, p.gh[g], fdum), b1 = base_row(ylast, p.image_h, p.gh[g], fdum);
+        const int c0 = base_col(x0, p.image_w, p.gw[g]), c1 = base_col(xlast, p.image_w, p.gw[g]);
+        w[g].row0 = b0 - 1;
+        w[g].nr = b1 - b0 + 4;
+        w[g].col0 = c0 - 1;
+        w[g].ncol = c1 - c0 + 4;
+        ok = ok && w[g].nr <= sep_rows<C>();
+        texels += w[g].nr * w[g].ncol;
+    }
+    return !ok ? 0 : (texels * C * 2 <= kTileN * Cfg<C>::XW * 2 ? 2 : 1);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Byte offset of grid g's window in X.
+template <int C>
+__device__ __forceinline__ int win_offset(const DecWin (&w)[2], int g)
+{
+    return g ? w[0].nr * w[0].ncol * C * 2 : 0;
+}
+
+template <int C>
+__device__ __forceinline__ void stage_windows(uint8_t *X, const DecodeLaunch &p, const DecWin (&w)[2], int tid, int nth)
+{
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        const uint32_t base = smem_addr(X) + win_offset<C>(w, g);
+        const int n = w[g].nr * w[g].ncol;
+        for (int k = tid; k < n; k += nth) {
+            const int ri = k / w[g].ncol, ci = k - ri * w[g].ncol;
+            const __half *src = p.grid[g] + ((size_t)wrap_coord(w[g].row0 + ri, p.gh[g]) * p.gw[g] +
+                                             wrap_coord(w[g].col0 + ci, p.gw[g])) * C;
+            if constexpr (C == 8) {
+                cp_async16(base + k * 16, src);
+            } else {
+#pragma unroll
+                for (int j = 0; j < C / 4; ++j) cp_async8(base + k * C * 2 + 8 * j, src + 4 * j);
+            }
+        }
+    }
+}
+
+// Pass 1 of grid g from its staged window (sep_pass1 with shared-memory taps).
+template <int C>
+__device__ __forceinline__ void sep_pass1_win(float *hs, const uint8_t *win, const DecWin &w, const DecodeLaunch &p,
+                                              int g, int x0, int tid, int nth)
+{
+    for (int k = tid; k < w.nr * kTileW; k += nth) {
+        const int ri = k / kTileW, xi = k - ri * kTileW, x = x0 + xi;
+        float2 row[C / 2];
+#pragma unroll
+        for (int q = 0; q < C / 2; ++q) row[q] = make_float2(0.f, 0.f);
+        if (x < p.image_w) {
+            float fx;
+            const float u = div_by_size(__fadd_rn((float)x, 0.5f), p.image_w);
+            const int bx = cr_base(u, p.gw[g], fx);
+            float wx[4];
+            catmull_rom_weights(fx, wx);
+            const uint8_t *rp = win + (size_t)ri * w.ncol * C * 2;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint8_t *tp = rp + (size_t)(bx - 1 + i - w.col0) * C * 2;
+                const float2 w2 = make_float2(wx[i], wx[i]);
+#pragma unroll
+                for (int q = 0; q < C / 4; ++q) {
+                    const uint2 raw = *reinterpret_cast<const uint2 *>(tp + 8 * q);
                     row[2 * q] = ffma2(w2, unpack_half2(raw.x), row[2 * q]);
                     row[2 * q + 1] = ffma2(w2, unpack_half2(raw.y), row[2 * q + 1]);
                 }
@@ -209,6 +325,12 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
     bool failed = false;
     float sse = 0.f;
 
+    DecWin w[2];  // this tile's windows (computed when the tile before staged them)
+    int wmode = 0;
+    if ((int)blockIdx.x < ntiles) {
+        wmode = dec_windows<C>(p, blockIdx.x, w);
+        if (wmode == 2) stage_windows<C>(s.X, p, w, tid, kDecThreads);
+    }
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         const int x = (tile % p.tiles_x) * kTileW + (r & (kTileW - 1));
         const int y = (tile / p.tiles_x) * kTileH + (r >> 4);
@@ -216,22 +338,19 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
 
         // ---- gather: separable passes through shared memory (direct taps if rows overflow) ---
         {
-            const int x0 = (tile % p.tiles_x) * kTileW, y0 = (tile / p.tiles_x) * kTileH;
-            const int ylast = min(y0 + kTileH, p.image_h) - 1;
-            int row0[2], nr[2];
-            bool sep = true;
-#pragma unroll
-            for (int g = 0; g < 2; ++g) {
-                float fdum;
-                const int b0 = base_row(y0, p.image_h, p.gh[g], fdum), b1 = base_row(ylast, p.image_h, p.gh[g], fdum);
-                row0[g] = b0 - 1;
-                nr[g] = b1 - b0 + 4;
-                sep = sep && nr[g] <= sep_rows<C>();
-            }
+            const int x0 = (tile % p.tiles_x) * kTileW;
+            const bool sep = wmode > 0;
+            const int row0[2] = {w[0].row0, w[1].row0};
             float *hs0 = reinterpret_cast<float *>(s.H), *hs1 = hs0 + sep_rows<C>() * kTileW * C;
-            if (sep) {
-                sep_pass1<C>(hs0, p, 0, row0[0], nr[0], x0, tid, kDecThreads);
-                sep_pass1<C>(hs1, p, 1, row0[1], nr[1], x0, tid, kDecThreads);
+            if (wmode == 2) {  // the windows were staged into X during the tile before
+                cp_async_wait_all();
+                __syncthreads();
+                sep_pass1_win<C>(hs0, s.X, w[0], p, 0, x0, tid, kDecThreads);
+                sep_pass1_win<C>(hs1, s.X + win_offset<C>(w, 1), w[1], p, 1, x0, tid, kDecThreads);
+                __syncthreads();  // X is overwritten below
+            } else if (sep) {
+                sep_pass1<C>(hs0, p, 0, w[0].row0, w[0].nr, x0, tid, kDecThreads);
+                sep_pass1<C>(hs1, p, 1, w[1].row0, w[1].nr, x0, tid, kDecThreads);
                 __syncthreads();
             }
             float u = 0.f, v = 0.f;
@@ -286,6 +405,10 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
             }
         }
         if (!dec_stage<C>(0, s, tmem, done, ph, failed, tid)) break;
+        if (tile + (int)gridDim.x < ntiles) {  // F1 has read X: stage the next tile's windows
+            wmode = dec_windows<C>(p, tile + gridDim.x, w);
+            if (wmode == 2) stage_windows<C>(s.X, p, w, tid, kDecThreads);
+        }
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] ------------------------------------------------
 #pragma unroll
@@ -337,10 +460,24 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
                 }
                 if (p.target) {
                     const __half *t = p.target + texel * cout;
+                    float tv[8];
+                    if (cout == 8 && (reinterpret_cast<uintptr_t>(p.target) & 15u) == 0) {  // one 16-byte load
+                        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(t));
+                        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const float2 f2 = __half22float2(*reinterpret_cast<const __half2 *>(&w4[q]));
+                            tv[2 * q] = f2.x;
+                            tv[2 * q + 1] = f2.y;
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) tv[e] = c0 + e < c1 ? __half2float(t[c0 + e]) : 0.f;
+                    }
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
                         if (c0 + e < c1) {
-                            const float d = yv[e] - __half2float(t[c0 + e]);
+                            const float d = yv[e] - tv[e];
                             sse = fmaf(d, d, sse);
                         }
                 } else if (p.num_ref > 0 && p.mse_accum) {  // reference textures (train.cu:946-960)
@@ -363,6 +500,7 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
         umma::fence_before();  // the next tile's F1 overwrites the accumulator after its barrier
     }
 
+    cp_async_wait_all();  // copies staged for a tile that a failed stage left untouched
     if (p.mse_accum) {
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sse += __shfl_xor_sync(0xffffffffu, sse, o);

@@ -249,10 +249,11 @@ __device__ __forceinline__ void sep_pass2(const float *hs, int ri0, int xi, cons
 }
 
 // Stage boundary (operands fenced to the async proxy, CTA barrier that also agrees on
-// failure), thread 0 issues the stage's products, every thread waits for them.
-template <int C>
+// failure), thread 0 issues the stage's products, every thread runs `meanwhile` and then
+// waits for them.
+template <int C, typename F>
 __device__ __forceinline__ bool dec_stage(int stage, const DecSmem<C> &s, uint32_t tmem, uint32_t done, uint32_t &ph,
-                                          bool &failed, int tid)
+                                          bool &failed, int tid, F &&meanwhile)
 {
     using K = Cfg<C>;
     using umma::desc;
@@ -286,6 +287,7 @@ __device__ __forceinline__ bool dec_stage(int stage, const DecSmem<C> &s, uint32
         }
         umma::commit(done);
     }
+    meanwhile();
     if (!umma::mbar_wait(done, ph, kSpinLimit)) {
         failed = true;
         atomicOr(&g_decode_status, 1u);
@@ -404,23 +406,27 @@ __global__ void __launch_bounds__(kDecThreads, kDecCtas) decode_tc_kernel(const 
                     st16(s.X, umma::cm_offset(r, 8 * (K::LC + 2), K::XC), 0u, 0u, 0u, 0u);
             }
         }
-        if (!dec_stage<C>(0, s, tmem, done, ph, failed, tid)) break;
-        if (tile + (int)gridDim.x < ntiles) {  // F1 has read X: stage the next tile's windows
-            wmode = dec_windows<C>(p, tile + gridDim.x, w);
-            if (wmode == 2) stage_windows<C>(s.X, p, w, tid, kDecThreads);
-        }
+        const auto nothing = [] {};
+        if (!dec_stage<C>(0, s, tmem, done, ph, failed, tid, nothing)) break;
 
         // ---- E1: H1e = [relu(Z1) | 1 | 0] ------------------------------------------------
 #pragma unroll
         for (int b = 0; b < 3 - kSplit; ++b) relu_store32(Rl + 32 * (half + b), s.H, r, 4 * (half + b));
         if (half == kSplit - 1) st16(s.H, umma::cm_offset(r, 64, kHC), pack_half2(1.f, 0.f), 0u, 0u, 0u);
         if (half == 0) st16(s.H, umma::cm_offset(r, 72, kHC), 0u, 0u, 0u, 0u);
-        if (!dec_stage<C>(1, s, tmem, done, ph, failed, tid)) break;
+        // while F2 runs (F1 has read X): stage the next tile's windows
+        const auto stage_next = [&] {
+            if (tile + (int)gridDim.x < ntiles) {
+                wmode = dec_windows<C>(p, tile + gridDim.x, w);
+                if (wmode == 2) stage_windows<C>(s.X, p, w, tid, kDecThreads);
+            }
+        };
+        if (!dec_stage<C>(1, s, tmem, done, ph, failed, tid, stage_next)) break;
 
         // ---- E2: H2e over H1e (the constant columns stay) ----------------------------------
 #pragma unroll
         for (int b = 0; b < 3 - kSplit; ++b) relu_store32(Rl + 32 * (half + b), s.H, r, 4 * (half + b));
-        if (!dec_stage<C>(2, s, tmem, done, ph, failed, tid)) break;
+        if (!dec_stage<C>(2, s, tmem, done, ph, failed, tid, nothing)) break;
 
         // ---- outputs: half 0 channels 0..7, half 1 channels 8..15 -------------------------
         {

@@ -10,9 +10,10 @@
 // latents are stored as UF16 of (value + bias) because BC6H interpolates half-float bit
 // patterns, which is meaningful only within one sign.
 //
-// One thread per 4x4 block: a warp covers 32 consecutive blocks of a block row, so every
-// texel row of a plane is read (encode) or written (decode) as 256 contiguous bytes, and
-// the 16-byte blocks move as one vector access each.
+// Decode: one thread per 4x4 block; a warp covers 32 consecutive blocks of a block row, so
+// every texel row of a plane is written as 256 contiguous bytes, and the 16-byte blocks move
+// as one vector access each.  Encode: 16 lanes per block, one texel each (the search's
+// per-texel work in parallel, its sums and extents by shuffles).
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -197,51 +198,6 @@ __device__ __forceinline__ int quantize_unsigned(int x, int bits)
     return q;
 }
 
-__device__ void fit_endpoints(const int x[16][3], uint32_t mask, int want, int A[3], int B[3])
-{
-    int lo[3] = {65535, 65535, 65535}, hi[3] = {0, 0, 0};
-    int64_t sum[3] = {0, 0, 0};
-    int n = 0;
-#pragma unroll
-    for (int px = 0; px < 16; ++px) {
-        if ((int)((mask >> px) & 1) != want) continue;
-        ++n;
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            lo[c] = min(lo[c], x[px][c]);
-            hi[c] = max(hi[c], x[px][c]);
-            sum[c] += x[px][c];
-        }
-    }
-    if (n == 0) {
-#pragma unroll
-        for (int c = 0; c < 3; ++c) A[c] = B[c] = 0;
-        return;
-    }
-    int k = 0;
-    if (hi[1] - lo[1] > hi[k] - lo[k]) k = 1;
-    if (hi[2] - lo[2] > hi[k] - lo[k]) k = 2;
-#pragma unroll
-    for (int c = 0; c < 3; ++c) {
-        int64_t cov = 0;
-        if (c != k) {
-            int64_t sxy = 0;
-#pragma unroll
-            for (int px = 0; px < 16; ++px)
-                if ((int)((mask >> px) & 1) == want) sxy += (int64_t)x[px][c] * x[px][k];
-            const int64_t sk = k == 0 ? sum[0] : (k == 1 ? sum[1] : sum[2]);
-            cov = (int64_t)n * sxy - sum[c] * sk;
-        }
-        if (cov < 0) {
-            A[c] = hi[c];
-            B[c] = lo[c];
-        } else {
-            A[c] = lo[c];
-            B[c] = hi[c];
-        }
-    }
-}
-
 // Palette index nearest to the projection of x onto a -> b (same arithmetic as the CPU
 // oracle: int64 sums, round-to-nearest conversions, one IEEE division).
 __device__ __forceinline__ int project_index(const int x[3], const int a[3], const int b[3], int ib)
@@ -278,122 +234,6 @@ struct Cand {
     uint64_t idx;
     int mi, part;
 };
-
-// Evaluate one candidate; returns the squared error or -1 when the mode cannot hold the
-// endpoints.  Only the winner of the search is packed (pack_block).
-__device__ int64_t try_mode(int mi, int part, const int x[16][3], const int A[2][3], const int B[2][3],
-                            Cand &out)
-{
-    const NtBc6hMode M = c_modes[mi];
-    const int regions = M.regions, epb = M.endpoint_bits, ib = regions == 2 ? 3 : 4;
-    const int ni = 1 << ib;
-    const uint32_t mask = regions == 2 ? c_parts[part] : 0u;
-    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
-    int q[2][2][3], u[2][2][3];
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int c = 0; c < 3; ++c) {
-            q[r][0][c] = r < regions ? quantize_unsigned(A[r][c], epb) : 0;
-            q[r][1][c] = r < regions ? quantize_unsigned(B[r][c], epb) : 0;
-        }
-    int idx[16];
-    int64_t err = 0;
-#pragma unroll 1
-    for (int pass = 0; pass < 2; ++pass) {
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int c = 0; c < 3; ++c) u[r][i][c] = unquantize(q[r][i][c], epb, false);
-        err = 0;
-#pragma unroll
-        for (int px = 0; px < 16; ++px) {
-            const int r = (mask >> px) & 1;
-            int a3[3], b3[3];
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                a3[c] = r ? u[1][0][c] : u[0][0][c];
-                b3[c] = r ? u[1][1][c] : u[0][1][c];
-            }
-            const int k0 = project_index(x[px], a3, b3, ib);
-            int64_t best = INT64_MAX;
-            int bi = 0;
-#pragma unroll
-            for (int dk = -1; dk <= 1; ++dk) {
-                const int kk = k0 + dk;
-                if (kk < 0 || kk >= ni) continue;
-                const int w = bc6h_weight(kk, ib == 3);
-                int64_t dsum = 0;
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    const int v = (a3[c] * (64 - w) + b3[c] * w + 32) >> 6;
-                    const int64_t dd = (int64_t)(x[px][c] - v);
-                    dsum += dd * dd;
-                }
-                if (dsum < best) {
-                    best = dsum;
-                    bi = kk;
-                }
-            }
-            idx[px] = bi;
-            err += best;
-        }
-        if (pass == 1) break;
-        bool swapped = false;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            if (r >= regions) break;
-            const int ap = r == 0 ? 0 : anchor1;
-            int aidx = 0;
-#pragma unroll
-            for (int px = 0; px < 16; ++px)
-                if (px == ap) aidx = idx[px];
-            if (aidx >= ni / 2) {
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    const int t = q[r][0][c];
-                    q[r][0][c] = q[r][1][c];
-                    q[r][1][c] = t;
-                }
-                swapped = true;
-            }
-        }
-        if (!swapped) break;
-    }
-    int e[4][3];
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int i = 0; i < 2; ++i)
-#pragma unroll
-            for (int c = 0; c < 3; ++c) e[2 * r + i][c] = q[r][i][c];
-    if (M.transformed) {
-#pragma unroll
-        for (int i = 1; i < 4; ++i) {
-            if (i >= 2 * regions) break;
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                const int dlt = e[i][c] - e[0][c];
-                const int db = M.delta_bits[c];
-                if (dlt < -(1 << (db - 1)) || dlt > (1 << (db - 1)) - 1) return -1;
-                e[i][c] = dlt;
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int c = 0; c < 3; ++c) out.e[i][c] = e[i][c];
-    uint64_t pk = 0;
-#pragma unroll
-    for (int px = 0; px < 16; ++px) pk |= (uint64_t)idx[px] << (4 * px);
-    out.idx = pk;
-    out.mi = mi;
-    out.part = part;
-    return err;
-}
 
 // Bitstream of a candidate: header fields through the mode's bit layout, then the indices
 // (anchor indices one bit shorter).
@@ -436,68 +276,314 @@ __device__ void pack_block(const Cand &cd, Block128 &out)
     }
 }
 
-__device__ void encode_block(const uint16_t tex[48], Block128 &out)
+// ---- cooperative encoder: 16 lanes per block, one texel per lane -------------------------
+//
+// The same search as encode_block (modes 11-14 on the whole block, the partition with the
+// smallest summed squared channel extents, modes 1-10 on it; strict improvement keeps the
+// first best) with the per-texel work spread over a half warp: each lane projects and scores
+// its own texel, integer sums and extents are reduced with shuffles (exact in any order), and
+// the per-candidate endpoint work is split across lanes and broadcast.  Bit-identical to
+// encode_block.  Shuffles name only the 16 lanes of the block, so the two blocks of a warp may
+// take different branches.
+
+struct Grp {
+    unsigned mask;  // the block's 16 lanes
+    int px;         // this lane's texel (row-major in the 4x4 block)
+    int base;       // lane of texel 0
+};
+
+__device__ __forceinline__ int grp_min(const Grp &g, int v)
 {
-    int x[16][3];
 #pragma unroll
-    for (int px = 0; px < 16; ++px)
+    for (int o = 8; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(g.mask, v, o));
+    return v;
+}
+__device__ __forceinline__ int grp_max(const Grp &g, int v)
+{
 #pragma unroll
-        for (int c = 0; c < 3; ++c) x[px][c] = to_domain(tex[px * 3 + c]);
-    int64_t best = INT64_MAX;
-    Cand cand, winner;
-    int A[2][3], B[2][3];
-    fit_endpoints(x, 0u, 0, A[0], B[0]);
+    for (int o = 8; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(g.mask, v, o));
+    return v;
+}
+__device__ __forceinline__ int grp_sum(const Grp &g, int v)
+{
 #pragma unroll
-    for (int c = 0; c < 3; ++c) A[1][c] = B[1][c] = 0;
-#pragma unroll 1
-    for (int mi = 10; mi < 14; ++mi) {
-        const int64_t e = try_mode(mi, 0, x, A, B, cand);
-        if (e >= 0 && e < best) {
-            best = e;
-            winner = cand;
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(g.mask, v, o);
+    return v;
+}
+__device__ __forceinline__ long long grp_sum64(const Grp &g, long long v)
+{
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(g.mask, v, o);
+    return v;
+}
+__device__ __forceinline__ int grp_at(const Grp &g, int v, int px) { return __shfl_sync(g.mask, v, g.base + px); }
+
+// fit_endpoints over the texels whose partition bit equals `want`.
+__device__ __forceinline__ void fit_endpoints_grp(const Grp &g, const int (&x)[3], uint32_t mask, int want, int A[3], int B[3])
+{
+    const bool mem = (int)((mask >> g.px) & 1) == want;
+    const int ones = __popc(mask & 0xFFFFu);
+    const int n = want ? ones : 16 - ones;
+    int lo[3], hi[3], sum[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        lo[c] = grp_min(g, mem ? x[c] : 65535);
+        hi[c] = grp_max(g, mem ? x[c] : 0);
+        sum[c] = grp_sum(g, mem ? x[c] : 0);
+    }
+    if (n == 0) {
+#pragma unroll
+        for (int c = 0; c < 3; ++c) A[c] = B[c] = 0;
+        return;
+    }
+    int k = 0;
+    if (hi[1] - lo[1] > hi[k] - lo[k]) k = 1;
+    if (hi[2] - lo[2] > hi[k] - lo[k]) k = 2;
+    const int xk = k == 0 ? x[0] : (k == 1 ? x[1] : x[2]);
+    const int sk = k == 0 ? sum[0] : (k == 1 ? sum[1] : sum[2]);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        // every lane takes part in both sums (c == k contributes nothing: cov stays 0)
+        const long long sxy = grp_sum64(g, mem && c != k ? (long long)x[c] * xk : 0ll);
+        const long long cov = c != k ? (long long)n * sxy - (long long)sum[c] * sk : 0ll;
+        if (cov < 0) {
+            A[c] = hi[c];
+            B[c] = lo[c];
+        } else {
+            A[c] = lo[c];
+            B[c] = hi[c];
         }
     }
-    int bp = 0;
-    int64_t bcost = INT64_MAX;
+}
+
+// try_mode for one candidate; returns the block's squared error (the same on every lane) or
+// -1 when the mode cannot hold the endpoints.  e: the stored endpoints; idx: this lane's index.
+__device__ __forceinline__ int64_t try_mode_grp(const Grp &g, int mi, int part, const int (&x)[3], const int A[2][3],
+                                const int B[2][3], int (&e)[4][3], int &idx)
+{
+    const NtBc6hMode M = c_modes[mi];
+    const int regions = M.regions, epb = M.endpoint_bits, ib = regions == 2 ? 3 : 4;
+    const int ni = 1 << ib;
+    const uint32_t mask = regions == 2 ? c_parts[part] : 0u;
+    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
+    // endpoint value v = 6 r + 3 i + c: lane v quantizes it
+    int myq = 0;
+    if (g.px < 12) {
+        const int r = g.px / 6, i = (g.px / 3) & 1, c = g.px % 3;
+        const int src = i ? (r ? B[1][c] : B[0][c]) : (r ? A[1][c] : A[0][c]);
+        myq = r < regions ? quantize_unsigned(src, epb) : 0;
+    }
+    int q[2][2][3];
+#pragma unroll
+    for (int v = 0; v < 12; ++v) q[v / 6][(v / 3) & 1][v % 3] = grp_at(g, myq, v);
+    const int r = (mask >> g.px) & 1;
+    int64_t err = 0;
+    int bi = 0;
 #pragma unroll 1
-    for (int p = 0; p < 32; ++p) {
-        const uint32_t pm = c_parts[p];
-        int64_t cost = 0;
+    for (int pass = 0; pass < 2; ++pass) {
+        int a3[3], b3[3];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            int lo[3] = {65535, 65535, 65535}, hi[3] = {0, 0, 0};
+        for (int c = 0; c < 3; ++c) {
+            a3[c] = unquantize(r ? q[1][0][c] : q[0][0][c], epb, false);
+            b3[c] = unquantize(r ? q[1][1][c] : q[0][1][c], epb, false);
+        }
+        const int k0 = project_index(x, a3, b3, ib);
+        int64_t best = INT64_MAX;
+        bi = 0;
 #pragma unroll
-            for (int px = 0; px < 16; ++px) {
-                if ((int)((pm >> px) & 1) != r) continue;
-#pragma unroll
-                for (int c = 0; c < 3; ++c) {
-                    lo[c] = min(lo[c], x[px][c]);
-                    hi[c] = max(hi[c], x[px][c]);
-                }
-            }
+        for (int dk = -1; dk <= 1; ++dk) {
+            const int kk = k0 + dk;
+            if (kk < 0 || kk >= ni) continue;
+            const int w = bc6h_weight(kk, ib == 3);
+            int64_t dsum = 0;
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
-                const int64_t ext = (int64_t)hi[c] - lo[c];
-                cost += ext * ext;
+                const int v = (a3[c] * (64 - w) + b3[c] * w + 32) >> 6;
+                const int64_t dd = (int64_t)(x[c] - v);
+                dsum += dd * dd;
+            }
+            if (dsum < best) {
+                best = dsum;
+                bi = kk;
             }
         }
-        if (cost < bcost) {
-            bcost = cost;
-            bp = p;
+        err = grp_sum64(g, best);
+        if (pass == 1) break;
+        bool swapped = false;
+        const int a0 = grp_at(g, bi, 0), a1 = grp_at(g, bi, anchor1);
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            if (rr >= regions) break;
+            if ((rr == 0 ? a0 : a1) >= ni / 2) {
+#pragma unroll
+                for (int c = 0; c < 3; ++c) {
+                    const int t = q[rr][0][c];
+                    q[rr][0][c] = q[rr][1][c];
+                    q[rr][1][c] = t;
+                }
+                swapped = true;
+            }
+        }
+        if (!swapped) break;
+    }
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) e[2 * rr + i][c] = q[rr][i][c];
+    if (M.transformed) {
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+            if (i >= 2 * regions) break;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int dlt = e[i][c] - e[0][c];
+                const int db = M.delta_bits[c];
+                if (dlt < -(1 << (db - 1)) || dlt > (1 << (db - 1)) - 1) return -1;
+                e[i][c] = dlt;
+            }
         }
     }
-    fit_endpoints(x, c_parts[bp], 0, A[0], B[0]);
-    fit_endpoints(x, c_parts[bp], 1, A[1], B[1]);
+    idx = bi;
+    return err;
+}
+
+// pack_block with the header bits spread over the lanes and each lane's index bits placed by
+// the lane; the words are OR-reduced, so every lane returns the whole block.
+__device__ __forceinline__ void pack_block_grp(const Grp &g, int mi, int part, const int (&e)[4][3], int idx, Block128 &out)
+{
+    const NtBc6hMode M = c_modes[mi];
+    const int regions = M.regions, ib = regions == 2 ? 3 : 4;
+    const int anchor1 = regions == 2 ? c_anchors[part] : 0;
+    out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
 #pragma unroll 1
-    for (int mi = 0; mi < 10; ++mi) {
-        const int64_t e = try_mode(mi, bp, x, A, B, cand);
-        if (e >= 0 && e < best) {
-            best = e;
-            winner = cand;
+    for (int k = g.px; k < M.header_bits; k += 16) {
+        const int ent = c_layout[mi][k];
+        const int f = ent >> 4, bit = ent & 15;
+        int v = 0;
+        if (f < 12) {
+#pragma unroll
+            for (int qf = 0; qf < 12; ++qf)
+                if (qf == f) v = ((unsigned)e[qf / 3][qf % 3] >> bit) & 1;
+        } else if (f == NT_BC6H_FIELD_D) {
+            v = (part >> bit) & 1;
+        } else {
+            v = (M.mode_value >> bit) & 1;
+        }
+        out.set(k, v);
+    }
+    // index bits: texel px starts after the header and the indices of texels 0 .. px - 1, the
+    // anchors' indices one bit shorter
+    const int px = g.px;
+    const bool anchor = px == 0 || (regions == 2 && px == anchor1);
+    const int nb = ib - (anchor ? 1 : 0);
+    const int pos = M.header_bits + px * ib - (px > 0 ? 1 : 0) - (regions == 2 && anchor1 < px ? 1 : 0);
+    for (int bb = 0; bb < nb; ++bb) out.set(pos + bb, (idx >> bb) & 1);
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) out.w[w] |= __shfl_xor_sync(g.mask, out.w[w], o);
+}
+
+// The first-best partition (strictly smallest summed squared extents of its two regions) over
+// the block's texels: lane j scores partitions j and j + 16.
+__device__ __forceinline__ int best_partition_grp(const Grp &g, const int (&x)[3])
+{
+    int64_t pc[2] = {0, 0};
+    const uint32_t pm0 = c_parts[g.px], pm1 = c_parts[g.px + 16];
+    int lo[2][2][3], hi[2][2][3];  // [candidate][region][channel]
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                lo[j][rr][c] = 65535;
+                hi[j][rr][c] = 0;
+            }
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+        int xt[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) xt[c] = grp_at(g, x[c], t);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const bool r1 = ((j ? pm1 : pm0) >> t) & 1;
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                if (r1) {
+                    lo[j][1][c] = min(lo[j][1][c], xt[c]);
+                    hi[j][1][c] = max(hi[j][1][c], xt[c]);
+                } else {
+                    lo[j][0][c] = min(lo[j][0][c], xt[c]);
+                    hi[j][0][c] = max(hi[j][0][c], xt[c]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                const int64_t ext = (int64_t)hi[j][rr][c] - lo[j][rr][c];
+                pc[j] += ext * ext;
+            }
+    long long bcost = pc[0];
+    int bp = g.px;
+    if (pc[1] < bcost) {
+        bcost = pc[1];
+        bp = g.px + 16;
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+        const long long oc = __shfl_xor_sync(g.mask, bcost, o);
+        const int op = __shfl_xor_sync(g.mask, bp, o);
+        if (oc < bcost || (oc == bcost && op < bp)) {
+            bcost = oc;
+            bp = op;
+        }
+    }
+    return bp;
+}
+
+// encode_block for the texel x (domain values) of this lane: modes 11-14 (indices 10-13) on
+// the whole block, then the best partition and modes 1-10 on it, in one loop (one copy of the
+// candidate code).
+__device__ void encode_block_grp(const Grp &g, const int (&x)[3], Block128 &out)
+{
+    int64_t best = INT64_MAX;
+    int we[4][3] = {}, wmi = 0, wpart = 0, widx = 0;
+    int e[4][3], idx = 0;
+    int A[2][3], B[2][3];
+    fit_endpoints_grp(g, x, 0u, 0, A[0], B[0]);
+#pragma unroll
+    for (int c = 0; c < 3; ++c) A[1][c] = B[1][c] = 0;
+    int bp = 0;
+#pragma unroll 1
+    for (int step = 0; step < 14; ++step) {
+        if (step == 4) {
+            bp = best_partition_grp(g, x);
+            fit_endpoints_grp(g, x, c_parts[bp], 0, A[0], B[0]);
+            fit_endpoints_grp(g, x, c_parts[bp], 1, A[1], B[1]);
+        }
+        const int mi = step < 4 ? 10 + step : step - 4, part = step < 4 ? 0 : bp;
+        const int64_t er = try_mode_grp(g, mi, part, x, A, B, e, idx);
+        if (er >= 0 && er < best) {
+            best = er;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int c = 0; c < 3; ++c) we[i][c] = e[i][c];
+            wmi = mi;
+            wpart = part;
+            widx = idx;
         }
     }
     if (best == INT64_MAX) out.w[0] = out.w[1] = out.w[2] = out.w[3] = 0u;
-    else pack_block(winner, out);
+    else pack_block_grp(g, wmi, wpart, we, widx, out);
 }
 
 struct CodecLaunch {
@@ -510,56 +596,33 @@ struct CodecLaunch {
     int32_t rows4;  // planar, 8-byte aligned rows of whole blocks: 4 texels move as one uint2
 };
 
-// grid: (ceil(block columns / 128), block rows, channel triples); one thread per block
-__global__ void __launch_bounds__(128) bc6h_encode_kernel(const CodecLaunch p)
+constexpr int kEncThreads = 128;  // 8 blocks of 16 lanes per CTA
+
+// grid: (ceil(block columns / 8), block rows, channel triples); 16 lanes per block, one texel
+// per lane (texels past the surface edge repeat the last row / column)
+__global__ void __launch_bounds__(kEncThreads) bc6h_encode_kernel(const CodecLaunch p)
 {
-    const int bx = blockIdx.x * blockDim.x + threadIdx.x, by = blockIdx.y, t = blockIdx.z;
-    if (bx < p.bw) do {
-        const int64_t b = ((int64_t)t * p.bh + by) * p.bw + bx;
-        uint16_t tex[48];
-        const uint16_t biash = __half_as_ushort(__float2half_rn(p.bias));
-        if (p.rows4) {
+    const int lane = threadIdx.x & 31;
+    Grp g;
+    g.px = lane & 15;
+    g.base = lane & 16;
+    g.mask = 0xFFFFu << g.base;
+    const int bx = blockIdx.x * (kEncThreads / 16) + (threadIdx.x >> 4), by = blockIdx.y, t = blockIdx.z;
+    if (bx >= p.bw) return;  // all 16 lanes of the block
+    const int y = min(by * 4 + g.px / 4, p.h - 1), xx = min(bx * 4 + g.px % 4, p.w - 1);
+    const uint16_t biash = __half_as_ushort(__float2half_rn(p.bias));
+    int x[3];
 #pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                const int ch = t * 3 + c;
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    uint2 raw = make_uint2(0u, 0u);
-                    if (ch < p.channels)
-                        raw = __ldg(reinterpret_cast<const uint2 *>(p.data + ch * p.cstride +
-                                                                    (int64_t)(by * 4 + r) * p.rstride + bx * 4));
-                    const uint16_t v[4] = {(uint16_t)(raw.x & 0xffff), (uint16_t)(raw.x >> 16), (uint16_t)(raw.y & 0xffff),
-                                           (uint16_t)(raw.y >> 16)};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        tex[(r * 4 + i) * 3 + c] =
-                            ch < p.channels ? __half_as_ushort(__float2half_rn(__half2float(__ushort_as_half(v[i])) + p.bias))
-                                            : biash;
-                }
-            }
-            Block128 out;
-            encode_block(tex, out);
-            p.blocks[b] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
-            continue;
-        }
-#pragma unroll
-        for (int px = 0; px < 16; ++px) {
-            const int y = min(by * 4 + px / 4, p.h - 1), xx = min(bx * 4 + px % 4, p.w - 1);
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                const int ch = t * 3 + c;
-                if (ch < p.channels) {
-                    const __half v = p.data[ch * p.cstride + y * p.rstride + xx * p.tstride];
-                    tex[px * 3 + c] = __half_as_ushort(__float2half_rn(__half2float(v) + p.bias));
-                } else {
-                    tex[px * 3 + c] = biash;
-                }
-            }
-        }
-        Block128 out;
-        encode_block(tex, out);
-        p.blocks[b] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
-    } while (0);
+    for (int c = 0; c < 3; ++c) {
+        const int ch = t * 3 + c;
+        uint16_t h = biash;
+        if (ch < p.channels)
+            h = __half_as_ushort(__float2half_rn(__half2float(p.data[ch * p.cstride + y * p.rstride + xx * p.tstride]) + p.bias));
+        x[c] = to_domain(h);
+    }
+    Block128 out;
+    encode_block_grp(g, x, out);
+    if (g.px == 0) p.blocks[((int64_t)t * p.bh + by) * p.bw + bx] = make_uint4(out.w[0], out.w[1], out.w[2], out.w[3]);
 }
 
 // grid: (ceil(block columns / 128), block rows, channel triples); one thread per block
@@ -656,7 +719,8 @@ cudaError_t launch_bc6h(const NtBc6hSurface *s, const void *blocks, float bias, 
     if (L.bh > 65535 || L.ntrip > 65535) return cudaErrorInvalidValue;
     const dim3 grid((L.bw + 127) / 128, L.bh, L.ntrip);
     if (encode)
-        bc6h_encode_kernel<<<grid, 128, 0, st>>>(L);
+        bc6h_encode_kernel<<<dim3((L.bw + kEncThreads / 16 - 1) / (kEncThreads / 16), L.bh, L.ntrip), kEncThreads, 0,
+                             st>>>(L);
     else
         bc6h_decode_kernel<<<grid, 128, 0, st>>>(L);
     count_launch();

@@ -432,6 +432,7 @@ def run_config2(torch, dev, stream, L, nt, _native, steps, warmup, rank, peak_hb
                         "algorithmic": f"30 B x {sum(w * h for (w, h) in CFG2['grids']) * CFG2['C']} latent params "
                                        f"+ {B} x {CFG2['cout']} x 2 B of target = {nbytes} B per step"},
            "train_kernel_tflops": flop / (t_train * 1e-3) / 1e12,
+           "train_kernel_traffic": ncu_traffic().get("train_kernel_config2", {}).get("bytes_per_launch"),
            "l2": "state above L2 (no flush)"}
     del tex, ps
     torch.cuda.empty_cache()

@@ -49,7 +49,8 @@ L2_FLUSH_BYTES = 256 << 20
 MLP_FLOP_FWD = 2 * (32 * 64 + 64 * 64 + 64 * 8)          # 13,312 per texel / sample
 MLP_FLOP_TRAIN = 3 * MLP_FLOP_FWD                         # fwd + dX + dW = 39,936 per sample
 HEADLINE_METRIC = "train samples/s (fwd+bwd+Adam), config 1"
-E2E_MATERIALS = 4  # config-1 materials the e2e loop rotates over: 4 x 51 MB of state > 126 MB L2
+E2E_MATERIALS = 4  # config-1 materials the timed loops rotate over: 4 x 51 MB of state > 126 MB L2
+DECODE_MATERIALS = 8  # config-0 decodes rotate over 8 materials and outputs: 8 x 22 MB > 126 MB L2
 
 
 def mlp_flop_train(cout):
@@ -773,14 +774,23 @@ def main():
     args.warmup = max(args.warmup, 3)
 
     # ---- config 1 training ---------------------------------------------------------------
-    tex = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
-                           output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
-    tex.init(seed=rank)
+    # The timed steps rotate over E2E_MATERIALS materials (one step each in turn): their state
+    # together exceeds the L2, so every step finds its material's state evicted, without a
+    # flush kernel between the steps.  (A flush also evicts the kernels' code from L2: the
+    # next training pass then refetches it from DRAM, ~6 us that a training loop never pays;
+    # the flushed timing is reported beside, as `l2_flushed`.)
+    mats = []
+    for i in range(E2E_MATERIALS):
+        t = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
+                             output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
+        t.init(seed=rank + 17 * i)
+        mats.append(t)
+    tex = mats[0]
     scratch = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     B = CFG1["lattice"][0] * CFG1["lattice"][1]
 
-    def step_once(step, ev=None):
-        p = tex.params(step=step)
+    def step_once(step, ev=None, m=0):
+        p = mats[m].params(step=step)
         if ev:
             ev[0].record(stream)
         _native.check(L.nt_invoke_training(ctypes.byref(p), 0, sptr))
@@ -793,30 +803,44 @@ def main():
     # untimed pre-warm: ~0.5 s of steps so the SM clock leaves idle, then W warm-up steps
     t_end = time.perf_counter() + args.prewarm
     while time.perf_counter() < t_end:
-        for _ in range(20):
-            step_once(0)
+        for k in range(20):
+            step_once(0, m=k % E2E_MATERIALS)
         torch.cuda.synchronize(dev)
     for w in range(args.warmup):
-        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
-        step_once(w + 1)
+        step_once(w + 1, m=w % E2E_MATERIALS)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clocks = ClockSampler(dev)
     clocks.start()
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    # the headline: K steps back to back, bracketed by one pair of events
     launches0 = nt.launch_count()
     torch.cuda.synchronize(dev)
+    e_begin, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_begin.record(stream)
     for k in range(args.steps):
-        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
-        step_once(args.warmup + k + 1, events[k])
+        step_once(args.warmup + k + 1, m=k % E2E_MATERIALS)
+    e_end.record(stream)
     torch.cuda.synchronize(dev)
-    launches = nt.launch_count() - launches0 - args.steps  # exclude the L2 flushes
-    if world > 1:
-        dist.barrier()
+    launches = nt.launch_count() - launches0
+    t_step = e_begin.elapsed_time(e_end) / args.steps  # ms
+    # the same K steps with an event pair around each kernel: the training / Adam split
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        step_once(args.warmup + args.steps + k + 1, events[k], m=k % E2E_MATERIALS)
+    torch.cuda.synchronize(dev)
     t_train = sum(e[0].elapsed_time(e[1]) for e in events) / args.steps   # ms
     t_adam = sum(e[1].elapsed_time(e[2]) for e in events) / args.steps
-    t_step = t_train + t_adam
+    # one material with the 256 MB flush before every step (the other cache condition)
+    fl_events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
+        step_once(args.warmup + 2 * args.steps + k + 1, fl_events[k])
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    fl_train = sum(e[0].elapsed_time(e[1]) for e in fl_events) / args.steps
+    fl_adam = sum(e[1].elapsed_time(e[2]) for e in fl_events) / args.steps
     if world > 1:
         t = torch.tensor([t_step], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -826,26 +850,30 @@ def main():
     value = world * B / (t_step_max * 1e-3)
 
     # ---- e2e through the C ABI: params from host memory, every step's loss read on the host ----
-    # Each step zeroes its loss slot, calls nt_train_step with the parameter block from host
-    # memory (its step advanced per call, main.cpp:1077) and copies the loss into a pinned
-    # host slot.  Pipelined: the host reads step k-1's loss after queuing step k, as a
-    # training loop that logs its loss does.  Synchronous: the host waits for every step.
-    # The loop rotates over E2E_MATERIALS config-1 materials (one step each in turn), whose
-    # state together exceeds the L2, so each step starts with its material's state evicted,
-    # the cache condition the flushed device timing above has, without a flush kernel.
+    # Each step calls nt_train_step with the parameter block from host memory (its step
+    # advanced per call, main.cpp:1077) on the compute stream; a copy stream then copies the
+    # step's loss into a pinned host slot and zeroes the device slot again with a 4-byte copy
+    # from pinned host memory (the step two later waits for that), so the compute stream runs
+    # only the two kernels per step.  Pipelined: the host reads step k-1's loss after queuing
+    # step k, as a training loop that logs its loss does.  Synchronous: the host waits for
+    # every step.
+    # The loop rotates over the same E2E_MATERIALS config-1 materials (one step each in turn),
+    # whose state together exceeds the L2, so each step starts with its material's state
+    # evicted: the cache condition of the device timing above.
     pbytes = ctypes.sizeof(_native.NtKernelParams)
     slots = 2
     loss_dev = torch.zeros(slots, dtype=torch.float32, device=dev)
     loss_host = torch.zeros(slots, dtype=torch.float32, pin_memory=True)
     dev_slot = [loss_dev[i] for i in range(slots)]
     host_slot = [loss_host[i] for i in range(slots)]
-    done = [torch.cuda.Event() for _ in range(slots)]
-    e2e_texs = [tex]
-    for i in range(1, E2E_MATERIALS):
-        t = nt.NeuralTexture(*CFG1["image"], grid_sizes=CFG1["grids"], latent_channels=CFG1["C"],
-                             output_channels=CFG1["cout"], device=dev, lattice=CFG1["lattice"])
-        t.init(seed=rank + 17 * i)
-        e2e_texs.append(t)
+    done = [torch.cuda.Event() for _ in range(slots)]     # slot's loss in host memory
+    stepped = [torch.cuda.Event() for _ in range(slots)]  # slot's step queued on the compute stream
+    cleared = [torch.cuda.Event() for _ in range(slots)]  # slot read and zeroed for its next step
+    copy_stream = torch.cuda.Stream(dev)
+    zero_host = torch.zeros(1, dtype=torch.float32, pin_memory=True)
+    for i in range(slots):
+        cleared[i].record(copy_stream)
+    e2e_texs = mats
     e2e_params = [t.params() for t in e2e_texs]
     e2e_steps = args.steps
 
@@ -858,12 +886,17 @@ def main():
         for k in range(e2e_steps):
             i = k % slots
             p = e2e_params[k % E2E_MATERIALS]
-            dev_slot[i].zero_()
+            stream.wait_event(cleared[i])
             p.loss_accum = dev_slot[i].data_ptr()
             p.step = 10_000 + k // E2E_MATERIALS
             _native.check(L.nt_train_step(ctypes.byref(p), sptr))
-            host_slot[i].copy_(dev_slot[i], non_blocking=True)
-            done[i].record(stream)
+            stepped[i].record(stream)
+            copy_stream.wait_event(stepped[i])
+            with torch.cuda.stream(copy_stream):
+                host_slot[i].copy_(dev_slot[i], non_blocking=True)
+                done[i].record(copy_stream)
+                dev_slot[i].copy_(zero_host[0], non_blocking=True)
+                cleared[i].record(copy_stream)
             j = (k - 1) % slots if pipelined else i
             if pipelined and k == 0:
                 continue
@@ -888,21 +921,36 @@ def main():
     torch.cuda.empty_cache()
 
     # ---- config 0 decode -----------------------------------------------------------------
-    dtex = nt.NeuralTexture(*CFG0["image"], grid_sizes=CFG0["grids"], latent_channels=CFG0["C"],
-                            output_channels=CFG0["cout"], device=dev)
-    dtex.init(seed=100 + rank)
-    out = torch.empty((CFG0["image"][0] * CFG0["image"][1], CFG0["cout"]), dtype=torch.float16, device=dev)
-    dp = dtex.params(inference_output=out)
-    for _ in range(5):
-        _native.check(L.nt_invoke_inference(ctypes.byref(dp), sptr))
+    # decodes rotate over DECODE_MATERIALS materials, each with its own output: each launch reads
+    # 5.2 MB of latents and writes 16.8 MB, 8 x 22 MB > L2, so no launch finds its data cached
+    dmats, douts, dps = [], [], []
+    for i in range(DECODE_MATERIALS):
+        t = nt.NeuralTexture(*CFG0["image"], grid_sizes=CFG0["grids"], latent_channels=CFG0["C"],
+                             output_channels=CFG0["cout"], device=dev)
+        t.init(seed=100 + rank + 31 * i)
+        o = torch.empty((CFG0["image"][0] * CFG0["image"][1], CFG0["cout"]), dtype=torch.float16, device=dev)
+        dmats.append(t)
+        douts.append(o)
+        dps.append(t.params(inference_output=o))
+    for k in range(2 * DECODE_MATERIALS):
+        _native.check(L.nt_invoke_inference(ctypes.byref(dps[k % DECODE_MATERIALS]), sptr))
+    torch.cuda.synchronize(dev)
+    e_begin.record(stream)
+    for k in range(args.decode_iters):
+        _native.check(L.nt_invoke_inference(ctypes.byref(dps[k % DECODE_MATERIALS]), sptr))
+    e_end.record(stream)
+    torch.cuda.synchronize(dev)
+    t_dec = e_begin.elapsed_time(e_end) / max(args.decode_iters, 1)
+    # one material with the 256 MB flush before every launch
     dev_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.decode_iters)]
     for k in range(args.decode_iters):
         _native.check(L.nt_flush_l2(scratch.data_ptr(), L2_FLUSH_BYTES, sptr))
         dev_ev[k][0].record(stream)
-        _native.check(L.nt_invoke_inference(ctypes.byref(dp), sptr))
+        _native.check(L.nt_invoke_inference(ctypes.byref(dps[0]), sptr))
         dev_ev[k][1].record(stream)
     torch.cuda.synchronize(dev)
-    t_dec = sum(a.elapsed_time(b) for a, b in dev_ev) / args.decode_iters
+    t_dec_flushed = sum(a.elapsed_time(b) for a, b in dev_ev) / max(args.decode_iters, 1)
+    del dmats[1:], douts[1:], dps[1:]
 
     # ---- config 3 codec: 16 latent planes of 4096^2 fp16 per GPU -------------------------
     codec = None
@@ -949,13 +997,18 @@ def main():
         "dtype": "f16 operands, f32 accumulate", "data": "synthetic",
         "config": {"workload": CFG1["workload"], "global_batch": B * world, "samples_per_gpu": B,
                    "latents": "512^2x8 + 256^2x8 fp16", "mlp": "32-64-64-8", "parallelism": f"materials x{world}",
-                   "l2": "flushed (256 MB write) before every timed step"},
+                   "l2": f"inputs larger than L2: steps rotate over {E2E_MATERIALS} materials (4 x 51 MB of "
+                         "training state > 126 MB L2), so each finds its material's state evicted; no flush kernel"},
         "roofline": {"kernel": "nt::tc::train_tc_kernel (tcgen05)", "bound": "tensor", "achieved": achieved_tf, "peak": pk["tensor"],
                      "unit": "TFLOP/s", "frac": achieved_tf / pk["tensor"],
                      "traffic": tr.get("train_kernel", {}).get("bytes_per_launch"),
                      "peak_source": pk["source"] + " burst bf16",
                      "algorithmic": f"{MLP_FLOP_TRAIN} FLOP/sample x {B} samples"},
         "kernels_ms": {"train_kernel": t_train, "adam_kernel": t_adam},
+        "l2_flushed": {"ms_per_step": fl_train + fl_adam, "value": world * B / ((fl_train + fl_adam) * 1e-3),
+                       "kernels_ms": {"train_kernel": fl_train, "adam_kernel": fl_adam},
+                       "note": "one material, 256 MB L2 flush before every step (CUDA events around each kernel); "
+                               "after the flush the training pass also refetches its code from DRAM"},
         "step_roofline": {"bound": "hbm", "achieved": step_bytes(CFG1["grids"], CFG1["C"], B, CFG1["cout"]) /
                           (t_step * 1e-3) / 1e9, "peak": pk["hbm"], "unit": "GB/s",
                           "frac": step_bytes(CFG1["grids"], CFG1["C"], B, CFG1["cout"]) / (t_step * 1e-3) / 1e9 /
@@ -968,13 +1021,16 @@ def main():
         "decode": {"workload": CFG0["workload"], "value": texels / (t_dec * 1e-3), "unit": "texels/s",
                    "ms": t_dec, "tensor_frac": MLP_FLOP_FWD * texels / (t_dec * 1e-3) / 1e12 / pk["tensor"],
                    "hbm_frac": dec_bytes / (t_dec * 1e-3) / 1e9 / pk["hbm"],
-                   "traffic": tr.get("decode_kernel", {}).get("bytes_per_launch")},
-        "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": pbytes,
+                   "traffic": tr.get("decode_kernel", {}).get("bytes_per_launch"),
+                   "l2": f"launches back to back over {DECODE_MATERIALS} materials and outputs (8 x 22 MB > L2)",
+                   "l2_flushed_ms": t_dec_flushed},
+        "e2e": {"value": e2e_value, "unit": "samples/s", "h2d_bytes_per_step": pbytes + 4,
                 "d2h_bytes_per_step": 4, "sync_every_step_value": e2e_sync_value,
                 "note": "nt_train_step through the C ABI per step: the parameter block read from host memory "
-                        "(kept by the caller, its step advanced per call as the reference driver does), the "
-                        "step's loss copied to a pinned host slot and read on the host one step behind (the "
-                        "next step already queued); sync_every_step_value waits for each step before the "
+                        "(kept by the caller, its step advanced per call as the reference driver does); on a "
+                        "copy stream the step's loss is copied to a pinned host slot, read on the host one step "
+                        "behind (the next step already queued), and the device slot zeroed by a 4-byte copy from "
+                        "pinned memory; sync_every_step_value waits for each step before the "
                         f"next. Steps rotate over {E2E_MATERIALS} config-1 materials whose state (4 x 51 MB) "
                         "exceeds the L2, so no step finds its material cached (no flush kernel in the loop)"},
         "gpu_launches": launches,

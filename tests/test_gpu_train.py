@@ -112,7 +112,8 @@ def test_gradients_accumulate_across_passes(cuda):
     assert rel_l2(gg2[0], 2 * gg1[0]) < 1e-5
 
 
-def test_adam_bit_exact(cuda, oracle):
+@pytest.mark.parametrize("step", [17, 500, 3000])  # 500: 1 - beta1^t is 1; 3000: both corrections are 1
+def test_adam_bit_exact(cuda, oracle, step):
     import torch
     import neural_textures_b200 as nt
     tex = make_texture((64, 64), ((32, 32), (16, 16)), 8, 8, lattice=(32, 32), seed=2)
@@ -128,7 +129,6 @@ def test_adam_bit_exact(cuda, oracle):
     before = {k: [_host(x) for x in v] for k, v in dict(W=tex.W, b=tex.b, grids=tex.grids, gW=tex.gW, gb=tex.gb,
                                                           gg=tex.ggrads, mW=tex.mW, vW=tex.vW, mb=tex.mb,
                                                           vb=tex.vb, m1=tex.gm1, m2=tex.gm2).items()}
-    step = 17
     nt.InvokeOptimizeAll(tex.params(step=step))
     torch.cuda.synchronize()
     b1, b2, lr, eps = tex.network_adam

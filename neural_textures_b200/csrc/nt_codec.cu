@@ -115,18 +115,16 @@ __device__ __forceinline__ int bc6h_weight(int idx, bool three_bit)
     return three_bit ? (128 * idx + 7) / 14 : (128 * idx + 15) / 30;
 }
 
-__device__ __forceinline__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48])
+// The block's endpoints, unquantised (e[2 r + i][c]: region r, endpoint i), its mode and its
+// partition; false for a reserved mode.
+__device__ __forceinline__ bool decode_endpoints(const Block128 &b, bool is_signed, int (&e)[4][3], NtBc6hMode &M,
+                                                 int &d)
 {
     const int mi = mode_index(b);
-    if (mi < 0) {
-#pragma unroll
-        for (int i = 0; i < 48; ++i) out[i] = 0;
-        return;
-    }
-    const NtBc6hMode M = c_modes[mi];
+    if (mi < 0) return false;
+    M = c_modes[mi];
     const uint64_t lo = (uint64_t)b.w[0] | ((uint64_t)b.w[1] << 32), hi = (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32);
-    int e[4][3];
-    int d = 0;
+    d = 0;
     bc6h_unpack_header(mi, lo, hi, e, d);
     const int ne = 2 * M.regions, epb = M.endpoint_bits;
 #pragma unroll
@@ -145,6 +143,20 @@ __device__ __forceinline__ void decode_block(const Block128 &b, bool is_signed, 
         for (int i = 0; i < 4; ++i)
             if (i < ne) e[i][c] = unquantize(e[i][c], epb, is_signed);
     }
+    return true;
+}
+
+__device__ __forceinline__ void decode_block(const Block128 &b, bool is_signed, uint16_t out[48])
+{
+    int e[4][3];
+    NtBc6hMode M;
+    int d = 0;
+    if (!decode_endpoints(b, is_signed, e, M, d)) {
+#pragma unroll
+        for (int i = 0; i < 48; ++i) out[i] = 0;
+        return;
+    }
+    const uint64_t hi = (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32);
     const bool two = M.regions == 2;
     const int ib = two ? 3 : 4;
     const int anchor1 = two ? c_anchors[d] : -1;
@@ -171,6 +183,64 @@ __device__ __forceinline__ void decode_block(const Block128 &b, bool is_signed, 
             const int a = r ? e[2][c] : e[0][c], dd = r ? dl[1][c] : dl[0][c];
             out[px * 3 + c] = finish_unquantize(a + ((dd * w + 32) >> 6), is_signed);
         }
+    }
+}
+
+// UF16 block -> its 16 texels' three channels minus `bias`, as fp16, through a palette: the
+// interpolated colour of each index value is formed once (16 entries: index i of a one-region
+// block, or 8 r + i for region r of a two-region block), stored at pal[k * stride] (shared
+// memory private to the thread: (c0, c1) in .x, (c2, 0) in .y) and looked up per texel.  The
+// same operations as decode_block followed by the bias step of bc6h_decode_kernel, evaluated
+// per palette entry instead of per texel, so the texels are bit-identical.
+template <int kStride>
+__device__ __forceinline__ void decode_block_palette(const Block128 &b, float bias, uint2 *pal, uint2 (&tx)[16])
+{
+    const auto entry = [&](int v0, int v1, int v2) {
+        const float2 f01 = __half22float2(__halves2half2(__ushort_as_half((uint16_t)v0), __ushort_as_half((uint16_t)v1)));
+        const __half2 o01 = __floats2half2_rn(f01.x - bias, f01.y - bias);
+        const __half o2 = __float2half_rn(__half2float(__ushort_as_half((uint16_t)v2)) - bias);
+        return make_uint2(*reinterpret_cast<const uint32_t *>(&o01), (uint32_t)__half_as_ushort(o2));
+    };
+    int e[4][3];
+    NtBc6hMode M;
+    int d = 0;
+    if (!decode_endpoints(b, false, e, M, d)) {  // reserved mode: every texel decodes to 0
+        const uint2 z = entry(0, 0, 0);
+#pragma unroll
+        for (int px = 0; px < 16; ++px) tx[px] = z;
+        return;
+    }
+    const bool two = M.regions == 2;
+    int dl[2][3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+        dl[0][c] = e[1][c] - e[0][c];
+        dl[1][c] = e[3][c] - e[2][c];
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        const int w = two ? bc6h_weight(k & 7, true) : bc6h_weight(k, false);
+        const bool r1 = two && k >= 8;
+        int v[3];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+            const int a = r1 ? e[2][c] : e[0][c], dd = r1 ? dl[1][c] : dl[0][c];
+            v[c] = finish_unquantize(a + ((dd * w + 32) >> 6), false);
+        }
+        pal[k * kStride] = entry(v[0], v[1], v[2]);
+    }
+    const uint64_t hi = (uint64_t)b.w[2] | ((uint64_t)b.w[3] << 32);
+    const int ib = two ? 3 : 4;
+    const int anchor1 = two ? c_anchors[d] : -1;
+    const uint32_t pmask = two ? c_parts[d] : 0u;
+    uint64_t s = hi >> (M.header_bits - 64);
+#pragma unroll
+    for (int px = 0; px < 16; ++px) {
+        const int nb = ib - ((px == 0 || px == anchor1) ? 1 : 0);
+        const int idx = (int)(s & ((1u << nb) - 1u));
+        s >>= nb;
+        const int k = two ? (int)(((pmask >> px) & 1u) << 3) | idx : idx;
+        tx[px] = pal[k * kStride];
     }
 }
 
@@ -637,30 +707,28 @@ __global__ void __launch_bounds__(128) bc6h_decode_kernel(const CodecLaunch p)
         blk.w[1] = raw.y;
         blk.w[2] = raw.z;
         blk.w[3] = raw.w;
-        uint16_t tex[48];
-        decode_block(blk, false, tex);
-        if (p.rows4) {
+        if (p.rows4) {  // whole blocks of a planar surface: palette decode, 4 texels per store
+            __shared__ uint2 pal[16 * 128];
+            uint2 tx[16];
+            decode_block_palette<128>(blk, p.bias, pal + threadIdx.x, tx);
 #pragma unroll
             for (int c = 0; c < 3; ++c) {
                 const int ch = t * 3 + c;
                 if (ch >= p.channels) break;
+                const uint32_t sel = c == 1 ? 0x7632u : 0x5410u;  // high or low halves
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    uint32_t v2[2];
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        // half -> float - bias -> half, two texels per packed conversion
-                        const float2 f = __half22float2(__halves2half2(__ushort_as_half(tex[(r * 4 + 2 * i) * 3 + c]),
-                                                                       __ushort_as_half(tex[(r * 4 + 2 * i + 1) * 3 + c])));
-                        const __half2 o = __floats2half2_rn(f.x - p.bias, f.y - p.bias);
-                        v2[i] = *reinterpret_cast<const uint32_t *>(&o);
-                    }
+                    const uint2 *q = tx + 4 * r;
+                    const uint32_t w0 = c == 2 ? __byte_perm(q[0].y, q[1].y, sel) : __byte_perm(q[0].x, q[1].x, sel);
+                    const uint32_t w1 = c == 2 ? __byte_perm(q[2].y, q[3].y, sel) : __byte_perm(q[2].x, q[3].x, sel);
                     *reinterpret_cast<uint2 *>(p.data + ch * p.cstride + (int64_t)(by * 4 + r) * p.rstride + bx * 4) =
-                        make_uint2(v2[0], v2[1]);
+                        make_uint2(w0, w1);
                 }
             }
             continue;
         }
+        uint16_t tex[48];
+        decode_block(blk, false, tex);
 #pragma unroll
         for (int px = 0; px < 16; ++px) {
             const int y = by * 4 + px / 4, xx = bx * 4 + px % 4;

@@ -43,6 +43,24 @@ def test_encode_decode_bit_exact(cuda, oracle, shape, layout):
     np.testing.assert_array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
 
 
+@pytest.mark.parametrize("bias", [4.0, 0.5, 3.3, 1e-3])
+def test_decode_bias_bit_exact(cuda, oracle, bias):
+    """Decode with several biases (fp16-exact or not), whole blocks (the palette decode) and a
+    ragged surface (the per-texel decode), bit for bit against the oracle."""
+    import torch
+    from neural_textures_b200 import api
+    rng = np.random.default_rng(11)
+    for shape in ((6, 64, 32), (3, 21, 10)):
+        x = oracle.smooth_latents(rng, shape)
+        ref_blocks = oracle.bc6h_encode_surface(x, bias=bias)
+        blocks = torch.from_numpy(ref_blocks).to(cuda)
+        out = torch.zeros(shape, dtype=torch.float16, device=cuda)
+        api.bc6h_decode(blocks, out, bias=bias)
+        torch.cuda.synchronize()
+        ref = oracle.bc6h_decode_surface(ref_blocks, shape, bias=bias)
+        np.testing.assert_array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+
+
 @pytest.mark.parametrize("signed", [0, 1])
 def test_raw_decode_all_modes_bit_exact(cuda, oracle, signed):
     import torch

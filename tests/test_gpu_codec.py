@@ -81,6 +81,28 @@ def test_raw_decode_all_modes_bit_exact(cuda, oracle, signed):
     np.testing.assert_array_equal(got, oracle.bc6h_decode_blocks(blocks, bool(signed)))
 
 
+def test_surface_decode_all_modes_bit_exact(cuda, oracle):
+    """Random bitstreams of every mode (reserved mode values included) decoded into a planar
+    surface of whole blocks, the per-block palette path, bit for bit against the oracle's
+    surface decode (bias 4, UF16)."""
+    import torch
+    from neural_textures_b200 import api
+    from neural_textures_b200 import bc6h_format as F
+    rng = np.random.default_rng(23)
+    bw, bh = 64, 113  # 7,232 blocks of one channel triple
+    blocks = rng.integers(0, 256, (bw * bh, 16), dtype=np.uint8)
+    for mi in range(14):
+        val, mbits = F.MODES[mi][0], F.MODES[mi][1]
+        sl = slice(mi * 512, (mi + 1) * 512)
+        blocks[sl, 0] = (blocks[sl, 0] & np.uint8(0xFF ^ ((1 << mbits) - 1))) | np.uint8(val)
+    shape = (3, 4 * bh, 4 * bw)
+    out = torch.zeros(shape, dtype=torch.float16, device=cuda)
+    api.bc6h_decode(torch.from_numpy(blocks.reshape(-1)).to(cuda), out)
+    torch.cuda.synchronize()
+    ref = oracle.bc6h_decode_surface(blocks.reshape(-1), shape)
+    np.testing.assert_array_equal(out.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+
+
 @pytest.mark.parametrize("signed", [0, 1])
 def test_decoder_matches_texture_hardware(cuda, oracle, signed):
     """Upload random blocks of every mode into a BC6H CUDA array and fetch them through the
